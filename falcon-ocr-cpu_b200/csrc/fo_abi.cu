@@ -1,0 +1,621 @@
+// fo_abi.cu -- host side of the C ABI (include/fo_attention.h): contexts,
+// sealed caches, shape validation with the reference's rules, host/device
+// staging and kernel dispatch.  Host code only; kernels live in the other
+// .cu files of this directory.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/fo_attention.h"
+#include "fo_common.cuh"
+#include "fo_kernels.h"
+
+#define FO_RECORD_ELEMS 160   // prefix record elements (src/quant/kv.rs:55)
+#define FO_TAIL_ELEMS 128     // tail record elements (src/quant/kv.rs:60)
+#define FO_MAX_ROWS_ABI 8     // verification rows (src/quant/kv.rs:68)
+
+extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
+                                              const float *sinks, float *out, int64_t total, int64_t n_heads,
+                                              int64_t n_kv_heads, int64_t image_start, int64_t image_end,
+                                              int softmax_static, int exp_fast, cudaStream_t stream);
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(FO_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define FO_CUDA(call, what)                         \
+    do {                                            \
+        cudaError_t e_ = (call);                    \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+// A device buffer that grows on demand (prefill staging and scratch only;
+// decode paths use buffers reserved at seal time).
+struct DevBuf {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    cudaError_t ensure(size_t need) {
+        if (need <= bytes) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&ptr, need);
+        if (e == cudaSuccess) bytes = need;
+        return e;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+// Keeps the caller's current device and restores it on exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+struct fo_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    unsigned *flags = nullptr;                 // seal status bits
+    DevBuf stage[6];                           // prefill host staging: q, prefix_k, generated_k, v, sinks, out
+    DevBuf bf16_k, bf16_v;                     // Bf16Kv::Convert scratch
+    DevBuf pages;                              // decode batch descriptors
+    std::vector<fo_decode_page> host_pages;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.0f;
+};
+
+struct fo_kv_cache {
+    fo_ctx *ctx = nullptr;
+    int32_t format = 0;
+    int32_t chunks = 0;
+    int32_t fast_exp = 0;
+    int64_t prefix_len = 0, capacity = 0, tail_capacity = 0, tail_len = 0;
+    int64_t heads = 0, groups = 0;
+    int64_t prefix_stride = 0, tail_stride = 0, max_splits = 0;
+    void *codes = nullptr, *tail_codes = nullptr;
+    uint16_t *scales = nullptr, *tail_scales = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;     // decode partials, rows <= 8
+    float *q_stage = nullptr, *out_stage = nullptr;  // [8][H][64] host-mode staging
+    float *sinks_stage = nullptr;                    // [H]
+    float *rows_stage = nullptr;                     // [2][8][H][64] append staging
+    size_t bytes = 0;                                // record bytes
+};
+
+namespace {
+
+size_t elem_size(int format) {
+    switch (format) {
+    case FO_KV_F32: return 4;
+    case FO_KV_Q16: return 2;
+    case FO_KV_Q8: return 1;
+    case FO_KV_BF16: return 2;
+    }
+    return 0;
+}
+
+bool coded(int format) { return format == FO_KV_Q16 || format == FO_KV_Q8; }
+
+// CompactKv::validate (src/kernels/attention/mod.rs:159-195).
+int validate_compact(const float *q, const fo_compact_kv *kv, int64_t query_len, const fo_geometry &g,
+                     const float *sinks, const float *output) {
+    if (!kv) return fail(FO_ERR_INVALID, "attention: null CompactKv");
+    if (!(kv->head_dim > 0 && kv->n_heads > 0 && kv->n_kv_heads > 0))
+        return fail(FO_ERR_INVALID, "attention head dimensions must be positive");
+    if (kv->n_heads % kv->n_kv_heads != 0) return fail(FO_ERR_INVALID, "attention GQA grouping");
+    if (kv->prefix_len < 0 || kv->prefix_len > kv->total_len) return fail(FO_ERR_INVALID, "attention prefix length");
+    if (query_len < 0) return fail(FO_ERR_INVALID, "attention Q shape");
+    if (!(g.image_start >= 0 && g.image_start <= g.image_end && g.image_end <= kv->prefix_len))
+        return fail(FO_ERR_INVALID, "attention image must be inside the prefix");
+    if (!(g.query_offset >= 0 && g.query_offset + query_len <= kv->total_len))
+        return fail(FO_ERR_INVALID, "attention query interval");
+    if (query_len > 0 && (!q || !output)) return fail(FO_ERR_INVALID, "attention Q/output pointer is null");
+    if (!sinks) return fail(FO_ERR_INVALID, "attention sink pointer is null");
+    if (kv->prefix_len > 0 && !kv->prefix_k) return fail(FO_ERR_INVALID, "attention prefix K pointer is null");
+    if (kv->total_len > kv->prefix_len && !kv->generated_k)
+        return fail(FO_ERR_INVALID, "attention generated K pointer is null");
+    if (kv->total_len > 0 && !kv->v) return fail(FO_ERR_INVALID, "attention V pointer is null");
+    return FO_OK;
+}
+
+struct Staged {
+    const float *q, *pk, *gk, *v, *sinks;
+    float *out;
+};
+
+// Host-mode inputs to device staging (FO_MEM_HOST), or the device pointers.
+int stage_compact(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len, const float *sinks,
+                  float *output, int mem, Staged *s) {
+    const int64_t qn = query_len * kv->n_heads * kv->head_dim;
+    const int64_t pkn = kv->prefix_len * kv->n_heads * kv->head_dim;
+    const int64_t gkn = (kv->total_len - kv->prefix_len) * kv->n_kv_heads * kv->head_dim;
+    const int64_t vn = kv->total_len * kv->n_kv_heads * kv->head_dim;
+    if (mem == FO_MEM_DEVICE) {
+        *s = {q, kv->prefix_k, kv->generated_k, kv->v, sinks, output};
+        return FO_OK;
+    }
+    if (mem != FO_MEM_HOST) return fail(FO_ERR_INVALID, "mem must be FO_MEM_HOST or FO_MEM_DEVICE");
+    const int64_t sizes[6] = {qn, pkn, gkn, vn, kv->n_heads, qn};
+    const void *srcs[5] = {q, kv->prefix_k, kv->generated_k, kv->v, sinks};
+    for (int i = 0; i < 6; i++) {
+        FO_CUDA(ctx->stage[i].ensure((size_t)std::max<int64_t>(sizes[i], 1) * 4), "cudaMalloc(staging)");
+        if (i < 5 && sizes[i] > 0)
+            FO_CUDA(cudaMemcpyAsync(ctx->stage[i].ptr, srcs[i], (size_t)sizes[i] * 4, cudaMemcpyHostToDevice,
+                                    ctx->stream),
+                    "cudaMemcpyAsync(H2D)");
+    }
+    *s = {(const float *)ctx->stage[0].ptr, (const float *)ctx->stage[1].ptr, (const float *)ctx->stage[2].ptr,
+          (const float *)ctx->stage[3].ptr, (const float *)ctx->stage[4].ptr, (float *)ctx->stage[5].ptr};
+    return FO_OK;
+}
+
+int finish_host(fo_ctx *ctx, float *host_out, const float *dev_out, int64_t n, int mem) {
+    if (mem == FO_MEM_HOST) {
+        if (n > 0)
+            FO_CUDA(cudaMemcpyAsync(host_out, dev_out, (size_t)n * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                    "cudaMemcpyAsync(D2H)");
+        FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    }
+    return FO_OK;
+}
+
+int timed_begin(fo_ctx *ctx, bool on) {
+    if (on) FO_CUDA(cudaEventRecord(ctx->ev0, ctx->stream), "cudaEventRecord");
+    return FO_OK;
+}
+int timed_end(fo_ctx *ctx, bool on) {
+    if (!on) return FO_OK;
+    FO_CUDA(cudaEventRecord(ctx->ev1, ctx->stream), "cudaEventRecord");
+    FO_CUDA(cudaEventSynchronize(ctx->ev1), "cudaEventSynchronize");
+    FO_CUDA(cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1), "cudaEventElapsedTime");
+    return FO_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fo_version(void) { return 100; }
+
+const char *fo_last_error(void) { return g_last_error.c_str(); }
+
+int fo_ctx_create(int device, void *stream, fo_ctx **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_ctx_create: null output pointer");
+    *out = nullptr;
+    int count = 0;
+    FO_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device < 0 || device >= count) return fail(FO_ERR_INVALID, "fo_ctx_create: no CUDA device %d", device);
+    DeviceGuard guard(device);
+    fo_ctx *ctx = new fo_ctx();
+    ctx->device = device;
+    // NULL is CUDA's default stream, as in the runtime API.
+    ctx->stream = (cudaStream_t)stream;
+    cudaError_t e = cudaMalloc(&ctx->flags, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev1);
+    if (e == cudaSuccess) e = ctx->pages.ensure(sizeof(fo_decode_page) * 1024);
+    if (e != cudaSuccess) {
+        fo_ctx_destroy(ctx);
+        return cuda_fail(e, "fo_ctx_create");
+    }
+    ctx->host_pages.reserve(1024);
+    *out = ctx;
+    return FO_OK;
+}
+
+int fo_ctx_destroy(fo_ctx *ctx) {
+    if (!ctx) return FO_OK;
+    DeviceGuard guard(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (auto &b : ctx->stage) b.release();
+    ctx->bf16_k.release();
+    ctx->bf16_v.release();
+    ctx->pages.release();
+    if (ctx->flags) cudaFree(ctx->flags);
+    if (ctx->ev0) cudaEventDestroy(ctx->ev0);
+    if (ctx->ev1) cudaEventDestroy(ctx->ev1);
+    if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return FO_OK;
+}
+
+int fo_ctx_synchronize(fo_ctx *ctx) {
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    DeviceGuard guard(ctx->device);
+    FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return FO_OK;
+}
+
+int fo_ctx_last_ms(fo_ctx *ctx, float *ms) {
+    if (!ctx || !ms) return fail(FO_ERR_INVALID, "null argument");
+    *ms = ctx->last_ms;
+    return FO_OK;
+}
+
+int fo_attention(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len, fo_geometry geometry,
+                 const float *sinks, float *output, fo_prefill_options options, int mem) {
+    int st = validate_compact(q, kv, query_len, geometry, sinks, output);
+    if (st != FO_OK) return st;
+    if (kv->head_dim > 256) return fail(FO_ERR_DECLINED, "attention: head_dim %lld above 256", (long long)kv->head_dim);
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    if (query_len == 0) return FO_OK;
+    DeviceGuard guard(ctx->device);
+    Staged s;
+    if ((st = stage_compact(ctx, q, kv, query_len, sinks, output, mem, &s)) != FO_OK) return st;
+    const bool tiles = query_len >= 4 && kv->head_dim == 64 && aligned16(s.q) && aligned16(s.pk) &&
+                       aligned16(s.gk) && aligned16(s.v) && aligned16(s.out);
+    if ((st = timed_begin(ctx, options.profile)) != FO_OK) return st;
+    cudaError_t e;
+    if (tiles) {
+        // The FP32 tiles (prefill64.rs); static softmax only on pure prefixes.
+        const int stat = options.fp32_softmax == FO_SOFTMAX_STATIC && kv->total_len == kv->prefix_len;
+        e = fo_launch_prefill_f32(s.q, s.pk, s.gk, s.v, s.sinks, s.out, query_len, kv->prefix_len, kv->total_len,
+                                  kv->n_heads, kv->n_kv_heads, geometry.query_offset, geometry.image_start,
+                                  geometry.image_end, stat, options.exp == FO_EXP_FAST, ctx->stream);
+    } else {
+        // The online head (online.rs; decode64.rs for one query); decode
+        // paths keep the platform exp (mod.rs:198-203).
+        const int fast = query_len >= 4 && options.exp == FO_EXP_FAST;
+        e = fo_launch_online(s.q, s.pk, s.gk, s.v, s.sinks, s.out, query_len, kv->prefix_len, kv->total_len,
+                             kv->n_heads, kv->n_kv_heads, kv->head_dim, geometry.query_offset, geometry.image_start,
+                             geometry.image_end, fast, ctx->stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "attention kernel launch");
+    if ((st = timed_end(ctx, options.profile)) != FO_OK) return st;
+    return finish_host(ctx, output, s.out, query_len * kv->n_heads * kv->head_dim, mem);
+}
+
+int fo_convert_bf16(fo_ctx *ctx, const float *src, uint16_t *dst, int64_t n) {
+    if (!ctx || (n > 0 && (!src || !dst)) || n < 0) return fail(FO_ERR_INVALID, "fo_convert_bf16: bad argument");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = fo_launch_convert_bf16(src, dst, n, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "convert kernel launch");
+    return FO_OK;
+}
+
+int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len,
+                              fo_geometry geometry, const float *sinks, float *output, const uint16_t *keys_bf16,
+                              const uint16_t *values_bf16, fo_prefill_options options, int mem) {
+    int st = validate_compact(q, kv, query_len, geometry, sinks, output);
+    if (st != FO_OK) return st;
+    // mod.rs:333-339: a pure prefix prefilled whole, 64-wide heads.
+    if (!(query_len >= 4 && kv->head_dim == 64 && geometry.query_offset == 0 && query_len == kv->total_len &&
+          kv->total_len == kv->prefix_len))
+        return fail(FO_ERR_DECLINED, "BF16 prefill declines this shape");
+    if ((keys_bf16 == nullptr) != (values_bf16 == nullptr))
+        return fail(FO_ERR_INVALID, "BF16 keys and values must both be given or both be null");
+    if (keys_bf16 && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "BF16 copies must be device pointers");
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    DeviceGuard guard(ctx->device);
+    const int64_t T = kv->total_len, H = kv->n_heads, G = kv->n_kv_heads;
+    Staged s;
+    // The FP32 keys and values are only read when converting.
+    fo_compact_kv kv_stage = *kv;
+    if (keys_bf16) {
+        kv_stage.prefix_k = nullptr;
+        kv_stage.v = nullptr;
+        kv_stage.prefix_len = 0;
+        kv_stage.total_len = 0;
+    }
+    if ((st = stage_compact(ctx, q, &kv_stage, query_len, sinks, output, mem, &s)) != FO_OK) return st;
+    if ((st = timed_begin(ctx, options.profile)) != FO_OK) return st;
+    const uint16_t *kb = keys_bf16, *vb = values_bf16;
+    cudaError_t e;
+    if (!kb) {
+        FO_CUDA(ctx->bf16_k.ensure((size_t)T * H * 64 * 2), "cudaMalloc(bf16 keys)");
+        FO_CUDA(ctx->bf16_v.ensure((size_t)T * G * 64 * 2), "cudaMalloc(bf16 values)");
+        e = fo_launch_convert_bf16(s.pk, (uint16_t *)ctx->bf16_k.ptr, T * H * 64, ctx->stream);
+        if (e == cudaSuccess) e = fo_launch_convert_bf16(s.v, (uint16_t *)ctx->bf16_v.ptr, T * G * 64, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "convert kernel launch");
+        kb = (const uint16_t *)ctx->bf16_k.ptr;
+        vb = (const uint16_t *)ctx->bf16_v.ptr;
+    }
+    if (!aligned16(kb) || !aligned16(vb) || !aligned16(s.q) || !aligned16(s.out))
+        return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
+    e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, T, H, G, geometry.image_start, geometry.image_end,
+                               options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
+    if ((st = timed_end(ctx, options.profile)) != FO_OK) return st;
+    return finish_host(ctx, output, s.out, query_len * H * 64, mem);
+}
+
+int fo_kv_destroy(fo_kv_cache *c) {
+    if (!c) return FO_OK;
+    DeviceGuard guard(c->ctx->device);
+    cudaStreamSynchronize(c->ctx->stream);
+    void *ptrs[] = {c->codes, c->tail_codes, c->scales, c->tail_scales, c->part_o,
+                    c->part_ml, c->q_stage, c->out_stage, c->sinks_stage, c->rows_stage};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    delete c;
+    return FO_OK;
+}
+
+int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, int64_t capacity, int64_t n_heads,
+               int64_t n_kv_heads, int64_t head_dim, int32_t format, int32_t chunks, int mem, fo_kv_cache **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_kv_seal: null output pointer");
+    *out = nullptr;
+    // kv.rs:248-263
+    if (!(head_dim == 64 && n_heads == 2 * n_kv_heads && n_kv_heads >= 1 && n_kv_heads <= 8))
+        return fail(FO_ERR_INVALID, "split cache requires Falcon 64-wide paired GQA heads");
+    if (!(prefix_len > 0 && capacity >= prefix_len)) return fail(FO_ERR_CAPACITY, "invalid split-prefix capacity");
+    if (format < FO_KV_F32 || format > FO_KV_BF16) return fail(FO_ERR_INVALID, "unknown split-cache format %d", format);
+    if (!k || !v) return fail(FO_ERR_INVALID, "split prefix key/value pointer is null");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    DeviceGuard guard(ctx->device);
+    fo_kv_cache *c = new fo_kv_cache();
+    c->ctx = ctx;
+    c->format = format;
+    c->chunks = chunks;
+    c->prefix_len = prefix_len;
+    c->capacity = capacity;
+    c->tail_capacity = capacity - prefix_len;
+    c->heads = n_heads;
+    c->groups = n_kv_heads;
+    c->prefix_stride = prefix_len;
+    c->tail_stride = c->tail_capacity;
+    c->max_splits = (capacity + FO_SPLIT - 1) / FO_SPLIT;
+    const size_t es = elem_size(format);
+    const int64_t G = n_kv_heads, H = n_heads;
+    const size_t code_bytes = (size_t)G * prefix_len * FO_RECORD_ELEMS * es;
+    const size_t tail_bytes = (size_t)G * std::max<int64_t>(c->tail_capacity, 1) * FO_TAIL_ELEMS * es;
+    const size_t scale_bytes = coded(format) ? (size_t)G * prefix_len * 5 * 2 : 16;
+    const size_t tscale_bytes = coded(format) ? (size_t)G * std::max<int64_t>(c->tail_capacity, 1) * 4 * 2 : 16;
+    cudaError_t e = cudaSuccess;
+    auto alloc = [&](void **p, size_t n) {
+        if (e == cudaSuccess) e = cudaMalloc(p, n);
+    };
+    alloc(&c->codes, code_bytes);
+    alloc(&c->tail_codes, tail_bytes);
+    alloc((void **)&c->scales, scale_bytes);
+    alloc((void **)&c->tail_scales, tscale_bytes);
+    alloc((void **)&c->part_o, (size_t)FO_MAX_ROWS_ABI * H * c->max_splits * 64 * 4);
+    alloc((void **)&c->part_ml, (size_t)FO_MAX_ROWS_ABI * H * c->max_splits * 2 * 4);
+    alloc((void **)&c->q_stage, (size_t)FO_MAX_ROWS_ABI * H * 64 * 4);
+    alloc((void **)&c->out_stage, (size_t)FO_MAX_ROWS_ABI * H * 64 * 4);
+    alloc((void **)&c->sinks_stage, (size_t)H * 4);
+    alloc((void **)&c->rows_stage, (size_t)2 * FO_MAX_ROWS_ABI * H * 64 * 4);
+    if (e != cudaSuccess) {
+        fo_kv_destroy(c);
+        return cuda_fail(e, "fo_kv_seal: cudaMalloc");
+    }
+    c->bytes = code_bytes + tail_bytes + (coded(format) ? scale_bytes + tscale_bytes : 0);
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->tail_codes, 0, tail_bytes, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->tail_scales, 0, tscale_bytes, ctx->stream);
+    const float *dk = k, *dv = v;
+    if (e == cudaSuccess && mem == FO_MEM_HOST) {
+        const size_t kn = (size_t)prefix_len * H * 64 * 4, vn = (size_t)prefix_len * G * 64 * 4;
+        e = ctx->stage[1].ensure(kn);
+        if (e == cudaSuccess) e = ctx->stage[3].ensure(vn);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(ctx->stage[1].ptr, k, kn, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(ctx->stage[3].ptr, v, vn, cudaMemcpyHostToDevice, ctx->stream);
+        dk = (const float *)ctx->stage[1].ptr;
+        dv = (const float *)ctx->stage[3].ptr;
+    }
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->flags, 0, sizeof(unsigned), ctx->stream);
+    if (e == cudaSuccess)
+        e = fo_launch_seal(dk, dv, prefix_len, H, G, format, c->codes, c->scales, c->prefix_stride, ctx->flags,
+                           ctx->stream);
+    unsigned flags = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&flags, ctx->flags, sizeof flags, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        fo_kv_destroy(c);
+        return cuda_fail(e, "fo_kv_seal");
+    }
+    // The reference validates every pair before anything else (kv.rs:265-278).
+    if (flags & FO_FLAG_PAIR) {
+        fo_kv_destroy(c);
+        return fail(FO_ERR_PAIR, "temporal keys differ inside GQA pair; refusing illegal sharing");
+    }
+    if (flags & FO_FLAG_NONFINITE) {
+        fo_kv_destroy(c);
+        return fail(FO_ERR_NONFINITE, "nonfinite or incomplete KV group");
+    }
+    if (flags & FO_FLAG_OVERFLOW) {
+        fo_kv_destroy(c);
+        return fail(FO_ERR_OVERFLOW, "%s KV conversion overflow", format == FO_KV_Q8 ? "Q8" : "Q16");
+    }
+    *out = c;
+    return FO_OK;
+}
+
+int fo_kv_set_fast_exp(fo_kv_cache *c, int32_t fast) {
+    if (!c) return fail(FO_ERR_INVALID, "null cache");
+    c->fast_exp = fast != 0;
+    return FO_OK;
+}
+
+int fo_kv_append(fo_kv_cache *c, const float *k, const float *v, int64_t rows, int mem) {
+    if (!c || (rows > 0 && (!k || !v)) || rows < 0) return fail(FO_ERR_INVALID, "fo_kv_append: bad argument");
+    if (c->tail_len + rows > c->tail_capacity) return fail(FO_ERR_CAPACITY, "split tail capacity");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    DeviceGuard guard(c->ctx->device);
+    const int64_t width = c->heads * 64;
+    for (int64_t done = 0; done < rows;) {
+        const int64_t n = mem == FO_MEM_HOST ? std::min<int64_t>(FO_MAX_ROWS_ABI, rows - done) : rows - done;
+        const float *dk = k + done * width, *dv = v + done * width;
+        if (mem == FO_MEM_HOST) {
+            float *sk = c->rows_stage, *sv = c->rows_stage + FO_MAX_ROWS_ABI * width;
+            FO_CUDA(cudaMemcpyAsync(sk, dk, (size_t)n * width * 4, cudaMemcpyHostToDevice, c->ctx->stream), "H2D");
+            FO_CUDA(cudaMemcpyAsync(sv, dv, (size_t)n * width * 4, cudaMemcpyHostToDevice, c->ctx->stream), "H2D");
+            dk = sk;
+            dv = sv;
+        }
+        cudaError_t e = fo_launch_append(dk, dv, n, c->heads, c->groups, c->format, c->tail_codes, c->tail_scales,
+                                         c->tail_stride, c->tail_len, c->ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "append kernel launch");
+        if (mem == FO_MEM_HOST) FO_CUDA(cudaStreamSynchronize(c->ctx->stream), "cudaStreamSynchronize");
+        c->tail_len += n;
+        done += n;
+    }
+    return FO_OK;
+}
+
+int fo_kv_truncate_tail(fo_kv_cache *c, int64_t tail_len) {
+    if (!c) return fail(FO_ERR_INVALID, "null cache");
+    if (tail_len < 0 || tail_len > c->tail_len) return fail(FO_ERR_INVALID, "cannot grow the tail by truncation");
+    c->tail_len = tail_len;
+    return FO_OK;
+}
+
+int64_t fo_kv_tail_len(const fo_kv_cache *c) { return c ? c->tail_len : -1; }
+int64_t fo_kv_prefix_len(const fo_kv_cache *c) { return c ? c->prefix_len : -1; }
+int64_t fo_kv_bytes(const fo_kv_cache *c) { return c ? (int64_t)c->bytes : -1; }
+
+int fo_kv_records(const fo_kv_cache *c, void **codes, void **scales, void **tail_codes, void **tail_scales,
+                  int64_t *prefix_stride, int64_t *tail_stride) {
+    if (!c) return fail(FO_ERR_INVALID, "null cache");
+    if (codes) *codes = c->codes;
+    if (scales) *scales = c->scales;
+    if (tail_codes) *tail_codes = c->tail_codes;
+    if (tail_scales) *tail_scales = c->tail_scales;
+    if (prefix_stride) *prefix_stride = c->prefix_stride;
+    if (tail_stride) *tail_stride = c->tail_stride;
+    return FO_OK;
+}
+
+static fo_decode_page make_page(const fo_kv_cache *c, const float *q, const float *sinks, float *out, int rows) {
+    fo_decode_page p{};
+    p.codes = c->codes;
+    p.scales = c->scales;
+    p.tail_codes = c->tail_codes;
+    p.tail_scales = c->tail_scales;
+    p.q = q;
+    p.sinks = sinks;
+    p.out = out;
+    p.part_o = c->part_o;
+    p.part_ml = c->part_ml;
+    p.prefix_len = c->prefix_len;
+    p.prefix_stride = c->prefix_stride;
+    p.tail_stride = c->tail_stride;
+    p.last = c->prefix_len + c->tail_len;
+    p.rows = rows;
+    p.splits = (int32_t)((p.last + FO_SPLIT - 1) / FO_SPLIT);
+    return p;
+}
+
+int fo_kv_attention_decode_rows(fo_kv_cache *c, const float *q, int64_t rows, const float *sinks, float *output,
+                                int mem) {
+    if (!c || !q || !sinks || !output) return fail(FO_ERR_INVALID, "decode: null argument");
+    // kv.rs:858
+    if (!(rows >= 1 && rows <= FO_MAX_ROWS_ABI && rows <= std::max<int64_t>(c->tail_len, 1)))
+        return fail(FO_ERR_INVALID, "decode rows must be 1..8 and at most max(tail_len, 1)");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    DeviceGuard guard(c->ctx->device);
+    cudaStream_t st = c->ctx->stream;
+    const int64_t n = rows * c->heads * 64;
+    const float *dq = q, *ds = sinks;
+    float *dout = output;
+    if (mem == FO_MEM_HOST) {
+        FO_CUDA(cudaMemcpyAsync(c->q_stage, q, (size_t)n * 4, cudaMemcpyHostToDevice, st), "H2D");
+        FO_CUDA(cudaMemcpyAsync(c->sinks_stage, sinks, (size_t)c->heads * 4, cudaMemcpyHostToDevice, st), "H2D");
+        dq = c->q_stage;
+        ds = c->sinks_stage;
+        dout = c->out_stage;
+    }
+    fo_decode_page p = make_page(c, dq, ds, dout, (int)rows);
+    cudaError_t e = fo_launch_decode_one(&p, c->format, c->groups, c->fast_exp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+    return finish_host(c->ctx, output, dout, n, mem);
+}
+
+int fo_kv_attention_decode(fo_kv_cache *c, const float *q, int64_t total_len, const float *sinks, float *output,
+                           int mem) {
+    if (!c) return fail(FO_ERR_INVALID, "null cache");
+    if (total_len != c->prefix_len + c->tail_len)  // kv.rs:572
+        return fail(FO_ERR_INVALID, "decode total_len must equal prefix_len + tail_len");
+    if (!(c->tail_len >= 0)) return fail(FO_ERR_INVALID, "bad tail");
+    // attention_decode over the whole cache is the one-row step.
+    if (!c || !q || !sinks || !output) return fail(FO_ERR_INVALID, "decode: null argument");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    DeviceGuard guard(c->ctx->device);
+    cudaStream_t st = c->ctx->stream;
+    const int64_t n = c->heads * 64;
+    const float *dq = q, *ds = sinks;
+    float *dout = output;
+    if (mem == FO_MEM_HOST) {
+        FO_CUDA(cudaMemcpyAsync(c->q_stage, q, (size_t)n * 4, cudaMemcpyHostToDevice, st), "H2D");
+        FO_CUDA(cudaMemcpyAsync(c->sinks_stage, sinks, (size_t)c->heads * 4, cudaMemcpyHostToDevice, st), "H2D");
+        dq = c->q_stage;
+        ds = c->sinks_stage;
+        dout = c->out_stage;
+    }
+    fo_decode_page p = make_page(c, dq, ds, dout, 1);
+    cudaError_t e = fo_launch_decode_one(&p, c->format, c->groups, c->fast_exp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+    return finish_host(c->ctx, output, dout, n, mem);
+}
+
+int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const float *const *q,
+                                 const float *const *sinks, float *const *output) {
+    if (!caches || !q || !sinks || !output || n < 0) return fail(FO_ERR_INVALID, "decode batch: null argument");
+    if (n == 0) return FO_OK;
+    fo_ctx *ctx = caches[0] ? caches[0]->ctx : nullptr;
+    if (!ctx) return fail(FO_ERR_INVALID, "decode batch: null cache");
+    const fo_kv_cache *c0 = caches[0];
+    for (int64_t i = 0; i < n; i++) {
+        const fo_kv_cache *c = caches[i];
+        if (!c || !q[i] || !sinks[i] || !output[i]) return fail(FO_ERR_INVALID, "decode batch: null entry %lld", (long long)i);
+        if (c->ctx != ctx || c->format != c0->format || c->groups != c0->groups || c->fast_exp != c0->fast_exp)
+            return fail(FO_ERR_INVALID, "decode batch: caches must share context, format, heads and exp");
+    }
+    DeviceGuard guard(ctx->device);
+    const int64_t cap = (int64_t)(ctx->pages.bytes / sizeof(fo_decode_page));
+    for (int64_t base = 0; base < n; base += cap) {
+        const int64_t m = std::min<int64_t>(cap, n - base);
+        ctx->host_pages.resize((size_t)m);
+        int64_t max_splits = 1;
+        for (int64_t i = 0; i < m; i++) {
+            ctx->host_pages[i] = make_page(caches[base + i], q[base + i], sinks[base + i], output[base + i], 1);
+            max_splits = std::max<int64_t>(max_splits, ctx->host_pages[i].splits);
+        }
+        FO_CUDA(cudaMemcpyAsync(ctx->pages.ptr, ctx->host_pages.data(), (size_t)m * sizeof(fo_decode_page),
+                                cudaMemcpyHostToDevice, ctx->stream),
+                "H2D(pages)");
+        cudaError_t e = fo_launch_decode_batch((const fo_decode_page *)ctx->pages.ptr, m, c0->format, c0->groups,
+                                               c0->fast_exp, max_splits, 1, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "decode batch launch");
+        // The descriptor copy reads host memory the next chunk overwrites.
+        FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    }
+    return FO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,104 @@
+// fo_common.cuh -- shared device helpers of the B200 attention backend.
+//
+// Arithmetic restated from the reference (paths relative to its project
+// root); CUDA's own math functions are called, never re-implemented.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define FO_HD 64            // head_dim of every fixed-width kernel
+#define FO_RECORD 160       // prefix record elements (src/quant/kv.rs:55)
+#define FO_TAIL_RECORD 128  // tail record elements (src/quant/kv.rs:60)
+#define FO_MAX_ROWS 8       // verification rows (src/quant/kv.rs:68)
+
+// Device status bits the seal kernel raises (checked on the host).
+#define FO_FLAG_PAIR 1u
+#define FO_FLAG_NONFINITE 2u
+#define FO_FLAG_OVERFLOW 4u
+
+namespace fo {
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+__device__ __forceinline__ float bits_f32(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ uint32_t f32_bits(float f) { return __float_as_uint(f); }
+
+// BF16 bits widened exactly (src/quant/kv/codec.rs:48-50).
+__device__ __forceinline__ float bf16_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// Round to nearest even; NaN stays a quiet NaN with its sign and payload top
+// bits (half::bf16::from_f32, which the reference's BF16 paths use).
+__device__ __forceinline__ uint16_t bf16_rne(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+// Smallest BF16 at or above a positive finite scale, 0 or NaN
+// (src/quant/kv/codec.rs:37-44).
+__device__ __forceinline__ uint16_t bf16_up(float scale) {
+    if (isnan(scale)) return 0x7FC0;
+    uint32_t bits = __float_as_uint(scale);
+    uint16_t high = (uint16_t)(bits >> 16);
+    return (bits & 0xFFFFu) ? (uint16_t)(high + 1) : high;
+}
+
+// The reference's portable polynomial exp (src/kernels/exp.rs:232-277,
+// Cephes-style constants published there).  Written with explicit FMAs in
+// the reference's order; used where the reference selects its fast exp.
+__device__ __forceinline__ float exp_poly_unchecked(float x) {
+    const float LOG2E = 1.44269504088896340736f;
+    const float LN2_HI = 0.6933594f, LN2_LO = -2.1219444e-4f;
+    float n = rintf(__fmul_rn(x, LOG2E));
+    float r = __fmaf_rn(n, -LN2_HI, x);
+    r = __fmaf_rn(n, -LN2_LO, r);
+    float p = 1.9875691e-4f;
+    p = __fmaf_rn(p, r, 1.3981999e-3f);
+    p = __fmaf_rn(p, r, 8.333452e-3f);
+    p = __fmaf_rn(p, r, 4.1665796e-2f);
+    p = __fmaf_rn(p, r, 0.16666665f);
+    p = __fmaf_rn(p, r, 0.5f);
+    float y = __fadd_rn(__fmaf_rn(p, __fmul_rn(r, r), r), 1.0f);
+    return __fmul_rn(y, __uint_as_float((uint32_t)((int)n + 127) << 23));
+}
+
+__device__ __forceinline__ float exp_poly(float x) {
+    if (isnan(x)) return x;
+    if (x < -87.0f) return 0.0f;
+    if (x > 88.376f) return INFINITY;
+    return exp_poly_unchecked(x);
+}
+
+// The softmax exp: CUDA's accurate expf, or the reference's exp_poly.
+template <bool FAST>
+__device__ __forceinline__ float softmax_exp(float x) {
+    if constexpr (FAST) return exp_poly(x); else return expf(x);
+}
+
+// Rust f32::max: the non-NaN operand when one is NaN (fmaxf semantics).
+__device__ __forceinline__ float rmax(float a, float b) { return fmaxf(a, b); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Geometry (src/kernels/attention/mod.rs:35-76): the keys [0, end) that the
+// query at absolute position `a` sees.
+__device__ __forceinline__ int64_t visible_end(int64_t a, int64_t image_start, int64_t image_end) {
+    return (a >= image_start && a < image_end) ? image_end : a + 1;
+}
+
+// The sink epilogue (src/kernels/attention/online.rs:145-149).
+__device__ __forceinline__ float sink_scale(float sink, float lse) { return 1.0f / (1.0f + expf(sink - lse)); }
+
+}  // namespace fo

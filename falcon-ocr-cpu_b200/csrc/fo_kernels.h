@@ -1,0 +1,64 @@
+// fo_kernels.h -- launchers of the CUDA kernels (internal to libfo_cuda.so;
+// the public boundary is include/fo_attention.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+cudaError_t fo_launch_online(const float *q, const float *prefix_k, const float *generated_k, const float *v,
+                             const float *sinks, float *out, int64_t query_len, int64_t prefix_len, int64_t total_len,
+                             int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t query_offset,
+                             int64_t image_start, int64_t image_end, int exp_fast, cudaStream_t stream);
+
+cudaError_t fo_launch_prefill_f32(const float *q, const float *prefix_k, const float *generated_k, const float *v,
+                                  const float *sinks, float *out, int64_t query_len, int64_t prefix_len,
+                                  int64_t total_len, int64_t n_heads, int64_t n_kv_heads, int64_t query_offset,
+                                  int64_t image_start, int64_t image_end, int softmax_static, int exp_fast,
+                                  cudaStream_t stream);
+
+cudaError_t fo_launch_convert_bf16(const float *src, uint16_t *dst, int64_t n, cudaStream_t stream);
+
+// Seal: compact FP32 K [P][H][64], V [P][G][64] -> records [G][stride][160]
+// and scales [G][stride][5]; raises FO_FLAG_* bits in *flags.
+cudaError_t fo_launch_seal(const float *k, const float *v, int64_t prefix_len, int64_t heads, int64_t groups,
+                           int format, void *codes, uint16_t *scales, int64_t stride, unsigned *flags,
+                           cudaStream_t stream);
+// Append rows of expanded K, V [rows][H][64] as tail records at index first..
+cudaError_t fo_launch_append(const float *k, const float *v, int64_t rows, int64_t heads, int64_t groups, int format,
+                             void *tail_codes, uint16_t *tail_scales, int64_t tail_stride, int64_t first,
+                             cudaStream_t stream);
+
+// One decode page: a cache's records and the query rows against it.
+struct fo_decode_page {
+    const void *codes;
+    const uint16_t *scales;
+    const void *tail_codes;
+    const uint16_t *tail_scales;
+    const float *q;      // [rows][H][64]
+    const float *sinks;  // [H]
+    float *out;          // [rows][H][64]
+    float *part_o;       // [rows][H][splits][64]
+    float *part_ml;      // [rows][H][splits][2]
+    int64_t prefix_len, prefix_stride, tail_stride, last;  // last = prefix_len + tail_len
+    int32_t rows, splits;                                   // splits = ceil(last / FO_SPLIT)
+};
+
+// Positions per decode split: the GPU's position partition.  Fixed, so a
+// row's partition depends only on its own length (verify rows equal their
+// single-row decodes bit for bit).
+#define FO_SPLIT 256
+
+// One page (descriptor read on the host, passed by value).
+cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t groups, int fast_exp,
+                                 cudaStream_t stream);
+// n_pages pages whose descriptors are a device array.
+cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format, int64_t groups,
+                                   int fast_exp, int64_t max_splits, int max_rows, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif

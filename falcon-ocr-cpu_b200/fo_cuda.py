@@ -1,0 +1,335 @@
+"""ctypes binding of libfo_cuda.so (include/fo_attention.h), mirroring the
+reference's attention operator interface for tests and benchmarks:
+
+* ``attention_with``          kernels::attention_with (src/kernels/attention/mod.rs:256-311)
+* ``attention_prefill_bf16``  kernels::attention_prefill_bf16 (mod.rs:321-349)
+* ``SplitPrefix``             quant::kv::SplitPrefix (src/quant/kv.rs:155-972):
+  ``from_compact``, ``append``, ``truncate_tail``, ``tail_len``, ``bytes``,
+  ``attention_decode``, ``attention_decode_rows``; ``decode_batch`` for pages.
+
+Arrays may be numpy (host memory: the call copies to and from the device) or
+CUDA torch tensors (device memory, read and written in place).  Shape errors
+raise ``FoError`` as the reference's asserts panic; seal errors raise the
+matching subclass as the reference returns an ``anyhow`` error.  There is no
+CPU fallback: importing this module without the built library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libfo_cuda.so")
+
+OK, ERR_INVALID, ERR_PAIR, ERR_NONFINITE, ERR_OVERFLOW, ERR_CAPACITY, ERR_CUDA, ERR_DECLINED = range(8)
+MEM_DEVICE, MEM_HOST = 0, 1
+KV_F32, KV_Q16, KV_Q8, KV_BF16 = 0, 1, 2, 3
+KV_FORMATS = {"f32": KV_F32, "q16": KV_Q16, "q8": KV_Q8, "bf16": KV_BF16}
+EXP_EXACT, EXP_FAST = 0, 1
+SOFTMAX_ONLINE, SOFTMAX_STATIC = 0, 1
+
+
+class FoError(RuntimeError):
+    status = ERR_INVALID
+
+
+class PairError(FoError):
+    status = ERR_PAIR
+
+
+class NonFiniteError(FoError):
+    status = ERR_NONFINITE
+
+
+class OverflowKvError(FoError):
+    status = ERR_OVERFLOW
+
+
+class CapacityError(FoError):
+    status = ERR_CAPACITY
+
+
+class CudaError(FoError):
+    status = ERR_CUDA
+
+
+class Declined(FoError):
+    status = ERR_DECLINED
+
+
+_ERRORS = {c.status: c for c in (FoError, PairError, NonFiniteError, OverflowKvError, CapacityError, CudaError,
+                                  Declined)}
+
+
+class Geometry(ctypes.Structure):
+    """src/kernels/attention/mod.rs:35-76"""
+    _fields_ = [("query_offset", ctypes.c_int64), ("image_start", ctypes.c_int64), ("image_end", ctypes.c_int64)]
+
+
+class CompactKv(ctypes.Structure):
+    """src/kernels/attention/mod.rs:78-97"""
+    _fields_ = [("prefix_k", ctypes.c_void_p), ("generated_k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+                ("prefix_len", ctypes.c_int64), ("total_len", ctypes.c_int64), ("n_heads", ctypes.c_int64),
+                ("n_kv_heads", ctypes.c_int64), ("head_dim", ctypes.c_int64)]
+
+
+class PrefillOptions(ctypes.Structure):
+    """src/kernels/attention/mod.rs:204-221"""
+    _fields_ = [("exp", ctypes.c_int32), ("profile", ctypes.c_int32), ("softmax", ctypes.c_int32),
+                ("fp32_softmax", ctypes.c_int32)]
+
+    @classmethod
+    def exact(cls):
+        return cls(EXP_EXACT, 0, SOFTMAX_ONLINE, SOFTMAX_ONLINE)
+
+
+EXPORTS = [
+    "fo_version", "fo_last_error", "fo_ctx_create", "fo_ctx_destroy", "fo_ctx_synchronize", "fo_ctx_last_ms",
+    "fo_attention", "fo_attention_prefill_bf16", "fo_convert_bf16", "fo_kv_seal", "fo_kv_destroy",
+    "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
+    "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
+    "fo_kv_attention_decode_batch",
+]
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it was not built (no fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run `python falcon-ocr-cpu_b200/build.py` (no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I32, I64, I = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int
+    PP = ctypes.POINTER(ctypes.c_void_p)
+    sigs = {
+        "fo_version": (I, []),
+        "fo_last_error": (ctypes.c_char_p, []),
+        "fo_ctx_create": (I, [I, P, ctypes.POINTER(P)]),
+        "fo_ctx_destroy": (I, [P]),
+        "fo_ctx_synchronize": (I, [P]),
+        "fo_ctx_last_ms": (I, [P, ctypes.POINTER(ctypes.c_float)]),
+        "fo_attention": (I, [P, P, ctypes.POINTER(CompactKv), I64, Geometry, P, P, PrefillOptions, I]),
+        "fo_attention_prefill_bf16": (I, [P, P, ctypes.POINTER(CompactKv), I64, Geometry, P, P, P, P,
+                                          PrefillOptions, I]),
+        "fo_convert_bf16": (I, [P, P, P, I64]),
+        "fo_kv_seal": (I, [P, P, P, I64, I64, I64, I64, I64, I32, I32, I, ctypes.POINTER(P)]),
+        "fo_kv_destroy": (I, [P]),
+        "fo_kv_set_fast_exp": (I, [P, I32]),
+        "fo_kv_append": (I, [P, P, P, I64, I]),
+        "fo_kv_truncate_tail": (I, [P, I64]),
+        "fo_kv_tail_len": (I64, [P]),
+        "fo_kv_prefix_len": (I64, [P]),
+        "fo_kv_bytes": (I64, [P]),
+        "fo_kv_records": (I, [P, PP, PP, PP, PP, ctypes.POINTER(I64), ctypes.POINTER(I64)]),
+        "fo_kv_attention_decode": (I, [P, P, I64, P, P, I]),
+        "fo_kv_attention_decode_rows": (I, [P, P, I64, P, P, I]),
+        "fo_kv_attention_decode_batch": (I, [PP, I64, PP, PP, PP]),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(status: int) -> None:
+    if status != OK:
+        msg = lib().fo_last_error().decode(errors="replace")
+        raise _ERRORS.get(status, FoError)(f"fo status {status}: {msg}")
+
+
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch")
+
+
+def _ptr_mem(arrays):
+    """Pointers of a call's arrays and its memory mode; all host or all device."""
+    kinds = {_is_torch(a) for a in arrays if a is not None}
+    if len(kinds) > 1:
+        raise FoError("mix of host (numpy) and device (torch) arrays in one call")
+    device = kinds == {True}
+    ptrs = []
+    for a in arrays:
+        if a is None:
+            ptrs.append(None)
+        elif device:
+            if not a.is_cuda or not a.is_contiguous():
+                raise FoError("device arrays must be contiguous CUDA tensors")
+            ptrs.append(a.data_ptr())
+        else:
+            if not (a.flags["C_CONTIGUOUS"]):
+                raise FoError("host arrays must be C-contiguous")
+            ptrs.append(a.ctypes.data)
+    return ptrs, (MEM_DEVICE if device else MEM_HOST)
+
+
+def _f32(a):
+    if a is None or _is_torch(a):
+        return a
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Context:
+    """A device and a stream (fo_ctx)."""
+
+    def __init__(self, device: int = 0, stream: Optional[int] = None):
+        h = ctypes.c_void_p()
+        check(lib().fo_ctx_create(device, stream, ctypes.byref(h)))
+        self.handle = h
+        self.device = device
+
+    def close(self):
+        if self.handle:
+            lib().fo_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synchronize(self):
+        check(lib().fo_ctx_synchronize(self.handle))
+
+    def last_ms(self) -> float:
+        v = ctypes.c_float()
+        check(lib().fo_ctx_last_ms(self.handle, ctypes.byref(v)))
+        return v.value
+
+
+_default: Optional[Context] = None
+
+
+def default_context() -> Context:
+    global _default
+    if _default is None:
+        _default = Context(0)
+    return _default
+
+
+def attention_with(q, prefix_k, v, query_len, geometry, sinks, output, n_heads, n_kv_heads, head_dim,
+                   generated_k=None, prefix_len=None, total_len=None, options=None, ctx=None):
+    """kernels::attention_with: `output` is overwritten."""
+    ctx = ctx or default_context()
+    q, prefix_k, v, sinks, generated_k = _f32(q), _f32(prefix_k), _f32(v), _f32(sinks), _f32(generated_k)
+    (pq, ppk, pgk, pv, ps, po), mem = _ptr_mem([q, prefix_k, generated_k, v, sinks, output])
+    if prefix_len is None:
+        prefix_len = prefix_k.numel() // (n_heads * head_dim) if _is_torch(prefix_k) else prefix_k.size // (
+            n_heads * head_dim)
+    if total_len is None:
+        total_len = (v.numel() if _is_torch(v) else v.size) // (n_kv_heads * head_dim)
+    kv = CompactKv(ppk, pgk, pv, prefix_len, total_len, n_heads, n_kv_heads, head_dim)
+    g = Geometry(*geometry)
+    check(lib().fo_attention(ctx.handle, pq, ctypes.byref(kv), query_len, g, ps, po, options or PrefillOptions.exact(),
+                             mem))
+    return output
+
+
+def attention_prefill_bf16(q, k, v, geometry, sinks, output, n_heads, n_kv_heads, keys_bf16=None, values_bf16=None,
+                           options=None, ctx=None):
+    """kernels::attention_prefill_bf16 over a pure prefix; raises Declined for other shapes."""
+    ctx = ctx or default_context()
+    q, k, v, sinks = _f32(q), _f32(k), _f32(v), _f32(sinks)
+    (pq, pk, pv, ps, po), mem = _ptr_mem([q, k, v, sinks, output])
+    total = (q.numel() if _is_torch(q) else q.size) // (n_heads * 64)
+    kv = CompactKv(pk, None, pv, total, total, n_heads, n_kv_heads, 64)
+    kb = keys_bf16.data_ptr() if keys_bf16 is not None else None
+    vb = values_bf16.data_ptr() if values_bf16 is not None else None
+    if options is None:
+        options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
+    check(lib().fo_attention_prefill_bf16(ctx.handle, pq, ctypes.byref(kv), total, Geometry(*geometry), ps, po, kb, vb,
+                                          options, mem))
+    return output
+
+
+class SplitPrefix:
+    """quant::kv::SplitPrefix on the device (src/quant/kv.rs:155-972)."""
+
+    def __init__(self, handle, ctx, heads):
+        self.handle = handle
+        self.ctx = ctx
+        self.heads = heads
+
+    @classmethod
+    def from_compact(cls, k, v, prefix_len, capacity, fmt="f32", heads=16, kv_heads=8, head_dim=64, chunks=0,
+                     ctx=None):
+        ctx = ctx or default_context()
+        fmt = KV_FORMATS[fmt] if isinstance(fmt, str) else fmt
+        k, v = _f32(k), _f32(v)
+        (pk, pv), mem = _ptr_mem([k, v])
+        h = ctypes.c_void_p()
+        check(lib().fo_kv_seal(ctx.handle, pk, pv, prefix_len, capacity, heads, kv_heads, head_dim, fmt, chunks, mem,
+                               ctypes.byref(h)))
+        return cls(h, ctx, heads)
+
+    def close(self):
+        if self.handle:
+            lib().fo_kv_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def with_fast_exp(self, fast: bool = True) -> "SplitPrefix":
+        check(lib().fo_kv_set_fast_exp(self.handle, int(bool(fast))))
+        return self
+
+    def append(self, k, v):
+        k, v = _f32(k), _f32(v)
+        (pk, pv), mem = _ptr_mem([k, v])
+        n = (k.numel() if _is_torch(k) else k.size) // (self.heads * 64)
+        check(lib().fo_kv_append(self.handle, pk, pv, n, mem))
+
+    def truncate_tail(self, tail_len: int):
+        check(lib().fo_kv_truncate_tail(self.handle, tail_len))
+
+    @property
+    def tail_len(self) -> int:
+        return int(lib().fo_kv_tail_len(self.handle))
+
+    @property
+    def prefix_len(self) -> int:
+        return int(lib().fo_kv_prefix_len(self.handle))
+
+    def bytes(self) -> int:
+        return int(lib().fo_kv_bytes(self.handle))
+
+    def records(self):
+        """(codes, scales, tail_codes, tail_scales) device pointers and strides."""
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        ps, ts = ctypes.c_int64(), ctypes.c_int64()
+        check(lib().fo_kv_records(self.handle, *[ctypes.byref(p) for p in ptrs], ctypes.byref(ps), ctypes.byref(ts)))
+        return [p.value for p in ptrs], ps.value, ts.value
+
+    def attention_decode(self, q, total_len, sinks, output):
+        q, sinks = _f32(q), _f32(sinks)
+        (pq, ps, po), mem = _ptr_mem([q, sinks, output])
+        check(lib().fo_kv_attention_decode(self.handle, pq, total_len, ps, po, mem))
+        return output
+
+    def attention_decode_rows(self, q, rows, sinks, output):
+        q, sinks = _f32(q), _f32(sinks)
+        (pq, ps, po), mem = _ptr_mem([q, sinks, output])
+        check(lib().fo_kv_attention_decode_rows(self.handle, pq, rows, ps, po, mem))
+        return output
+
+
+def decode_batch(caches: Sequence[SplitPrefix], qs, sinks, outputs):
+    """One single-row decode per page in one launch (device tensors)."""
+    n = len(caches)
+    arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
+    check(lib().fo_kv_attention_decode_batch(arr([c.handle.value for c in caches]), n, arr([q.data_ptr() for q in qs]),
+                                             arr([s.data_ptr() for s in sinks]),
+                                             arr([o.data_ptr() for o in outputs])))

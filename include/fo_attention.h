@@ -1,0 +1,190 @@
+/*
+ * fo_attention.h -- C ABI of the B200 attention backend for falcon-ocr.
+ *
+ * This is the drop-in boundary of a `--backend cuda` for the reference's
+ * attention operators.  Each entry point replaces one reference interface
+ * (paths relative to the reference project root):
+ *
+ *   fo_attention                 kernels::attention_with
+ *                                  src/kernels/attention/mod.rs:256-311
+ *   fo_attention_prefill_bf16    kernels::attention_prefill_bf16
+ *                                  src/kernels/attention/mod.rs:321-349
+ *   fo_kv_seal                   SplitPrefix::from_compact  src/quant/kv.rs:225-236
+ *   fo_kv_set_fast_exp           SplitPrefix::with_fast_exp src/quant/kv.rs:423-426
+ *   fo_kv_append                 SplitPrefix::append        src/quant/kv.rs:430-449
+ *   fo_kv_truncate_tail          SplitPrefix::truncate_tail src/quant/kv.rs:846-849
+ *   fo_kv_tail_len               SplitPrefix::tail_len      src/quant/kv.rs:841-843
+ *   fo_kv_bytes                  SplitPrefix::bytes         src/quant/kv.rs:523-525
+ *   fo_kv_attention_decode       SplitPrefix::attention_decode      src/quant/kv.rs:568-576
+ *   fo_kv_attention_decode_rows  SplitPrefix::attention_decode_rows src/quant/kv.rs:856-865
+ *   fo_kv_attention_decode_batch one decode row per page, as Model::decode_batch_next
+ *                                  calls LayerCache::attention per page (src/model/mod.rs:827-852)
+ *
+ * Conventions (mirroring the reference's, src/kernels/attention/mod.rs:159-195
+ * and src/quant/kv.rs:248-295):
+ *   - Every call returns an fo_status; FO_OK is 0.  Shape violations that the
+ *     reference asserts on return FO_ERR_INVALID and write nothing; the seal
+ *     errors the reference returns as anyhow::Result map to FO_ERR_PAIR,
+ *     FO_ERR_NONFINITE, FO_ERR_OVERFLOW and FO_ERR_CAPACITY.
+ *     fo_last_error() returns the calling thread's last message.
+ *   - Buffers are caller-owned.  `mem` says whether the float pointers of a
+ *     call are host (FO_MEM_HOST: copied to and from the device inside the
+ *     call) or device (FO_MEM_DEVICE: read and written in place).  Outputs
+ *     are overwritten, token-major [row][head][head_dim] FP32.
+ *   - Work runs on the context's stream.  FO_MEM_HOST calls return after the
+ *     output is on the host; FO_MEM_DEVICE calls return after launching.
+ *   - Decode never allocates device memory: fo_kv_seal reserves every
+ *     buffer a later append or decode on that cache needs.
+ */
+#ifndef FO_ATTENTION_H
+#define FO_ATTENTION_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    FO_OK = 0,
+    FO_ERR_INVALID = 1,     /* null pointer or shape the reference asserts against */
+    FO_ERR_PAIR = 2,        /* temporal keys differ inside a GQA pair (kv.rs:266-278) */
+    FO_ERR_NONFINITE = 3,   /* non-finite value in a sealed prefix (kv.rs:288) */
+    FO_ERR_OVERFLOW = 4,    /* Q8/Q16 code * scale overflowed (kv.rs:328, 355) */
+    FO_ERR_CAPACITY = 5,    /* prefix_len == 0, capacity < prefix_len, or tail full */
+    FO_ERR_CUDA = 6,        /* a CUDA runtime call failed; see fo_last_error() */
+    FO_ERR_DECLINED = 7     /* shape outside a kernel's scope; nothing written */
+} fo_status;
+
+#define FO_MEM_DEVICE 0
+#define FO_MEM_HOST 1
+
+/* Split-cache record formats (src/quant/kv.rs:120-127; BF16 is new). */
+#define FO_KV_F32 0
+#define FO_KV_Q16 1
+#define FO_KV_Q8 2
+#define FO_KV_BF16 3
+
+/* ExpMode / PrefillSoftmax (src/kernels/attention/mod.rs:204-221). */
+#define FO_EXP_EXACT 0
+#define FO_EXP_FAST 1
+#define FO_SOFTMAX_ONLINE 0
+#define FO_SOFTMAX_STATIC 1
+
+/* Geometry (src/kernels/attention/mod.rs:35-76). */
+typedef struct {
+    int64_t query_offset;
+    int64_t image_start;
+    int64_t image_end;
+} fo_geometry;
+
+/* CompactKv (src/kernels/attention/mod.rs:78-97): prefix_k
+ * [prefix_len][n_heads][head_dim], generated_k [total_len - prefix_len]
+ * [n_kv_heads][head_dim], v [total_len][n_kv_heads][head_dim]. */
+typedef struct {
+    const float *prefix_k;
+    const float *generated_k;
+    const float *v;
+    int64_t prefix_len;
+    int64_t total_len;
+    int64_t n_heads;
+    int64_t n_kv_heads;
+    int64_t head_dim;
+} fo_compact_kv;
+
+/* PrefillOptions (src/kernels/attention/mod.rs:204-210). */
+typedef struct {
+    int32_t exp;          /* FO_EXP_EXACT | FO_EXP_FAST: the online softmax's exp */
+    int32_t profile;      /* nonzero: record per-launch device times (fo_ctx_last_ms) */
+    int32_t softmax;      /* BF16 kernel's softmax: FO_SOFTMAX_ONLINE | FO_SOFTMAX_STATIC */
+    int32_t fp32_softmax; /* FP32 tiles' softmax */
+} fo_prefill_options;
+
+typedef struct fo_ctx fo_ctx;
+typedef struct fo_kv_cache fo_kv_cache;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int fo_version(void);
+/* The calling thread's last error message ("" when none). */
+const char *fo_last_error(void);
+
+/* A device context: device index and a CUDA stream (cudaStream_t passed as
+ * void*; NULL is CUDA's default stream).  All work of calls made with this
+ * context is ordered on that stream. */
+int fo_ctx_create(int device, void *stream, fo_ctx **out);
+int fo_ctx_destroy(fo_ctx *ctx);
+int fo_ctx_synchronize(fo_ctx *ctx);
+/* Device milliseconds of the last call's kernels when options.profile was set. */
+int fo_ctx_last_ms(fo_ctx *ctx, float *ms);
+
+/* kernels::attention_with (mod.rs:256-311): any head_dim <= 256, prefix or
+ * mixed caches, any query length.  query_len >= 4 with head_dim 64 runs the
+ * FP32 tiles (options.fp32_softmax, options.exp); other shapes run the
+ * online head.  q and output hold [query_len][n_heads][head_dim]. */
+int fo_attention(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len, fo_geometry geometry,
+                 const float *sinks, float *output, fo_prefill_options options, int mem);
+
+/* kernels::attention_prefill_bf16 (mod.rs:321-349): the tcgen05 BF16 prefill
+ * of a pure prefix (query_offset 0, query_len == prefix_len == total_len,
+ * head_dim 64).  Returns FO_ERR_DECLINED, writing nothing, for other shapes
+ * (the reference returns false).  keys_bf16 [total][n_heads][64] and
+ * values_bf16 [total][n_kv_heads][64] are optional device BF16 copies
+ * (Bf16Kv::Converted); when NULL the call converts kv's FP32 keys and
+ * values into context scratch (Bf16Kv::Convert).  options.softmax selects
+ * online or static shift; the static shift requires every score
+ * |q.k| / 8 to stay below 80 (per-head RMS norms keep it below 8). */
+int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len,
+                              fo_geometry geometry, const float *sinks, float *output, const uint16_t *keys_bf16,
+                              const uint16_t *values_bf16, fo_prefill_options options, int mem);
+
+/* FP32 -> BF16 (round to nearest even) of n device values, the conversion
+ * fo_attention_prefill_bf16 applies to Bf16Kv::Convert inputs. */
+int fo_convert_bf16(fo_ctx *ctx, const float *src, uint16_t *dst, int64_t n);
+
+/* SplitPrefix::from_compact (kv.rs:225-236): seal a compact prefix (k
+ * [prefix_len][n_heads][64], v [prefix_len][n_kv_heads][64]) into
+ * group-major records of `format`, with room for capacity - prefix_len
+ * generated positions.  chunks is the reference's position-chunk request
+ * (0 for its default); it only changes rounding, and the GPU partitions
+ * positions by its own fixed split.  The cache keeps a reference to ctx. */
+int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, int64_t capacity, int64_t n_heads,
+               int64_t n_kv_heads, int64_t head_dim, int32_t format, int32_t chunks, int mem, fo_kv_cache **out);
+int fo_kv_destroy(fo_kv_cache *cache);
+/* SplitPrefix::with_fast_exp (kv.rs:423-426): the softmax's exp becomes
+ * exp_poly (src/kernels/exp.rs:232-277) for single and verify rows alike. */
+int fo_kv_set_fast_exp(fo_kv_cache *cache, int32_t fast);
+/* SplitPrefix::append (kv.rs:430-449): rows of expanded k and v, each
+ * [rows][n_heads][64], identical inside each GQA pair; the pair's first
+ * head is stored.  Non-finite values give NaN blocks (kv.rs:451-455). */
+int fo_kv_append(fo_kv_cache *cache, const float *k, const float *v, int64_t rows, int mem);
+/* SplitPrefix::truncate_tail (kv.rs:846-849). */
+int fo_kv_truncate_tail(fo_kv_cache *cache, int64_t tail_len);
+int64_t fo_kv_tail_len(const fo_kv_cache *cache);
+int64_t fo_kv_prefix_len(const fo_kv_cache *cache);
+/* Allocated record bytes, prefix and tail (kv.rs:523-525). */
+int64_t fo_kv_bytes(const fo_kv_cache *cache);
+/* Device pointers and strides of the records, for tests and tooling:
+ * codes [groups][prefix_stride][160], scales [groups][prefix_stride][5],
+ * tail_codes [groups][tail_stride][128], tail_scales [groups][tail_stride][4]. */
+int fo_kv_records(const fo_kv_cache *cache, void **codes, void **scales, void **tail_codes, void **tail_scales,
+                  int64_t *prefix_stride, int64_t *tail_stride);
+
+/* SplitPrefix::attention_decode (kv.rs:568-576): q and output [n_heads][64];
+ * total_len must equal prefix_len + tail_len. */
+int fo_kv_attention_decode(fo_kv_cache *cache, const float *q, int64_t total_len, const float *sinks, float *output,
+                           int mem);
+/* SplitPrefix::attention_decode_rows (kv.rs:856-865): rows 1..8 (and at most
+ * max(tail_len, 1)); row r sees prefix_len + tail_len - rows + 1 + r
+ * positions and equals its single-row decode bit for bit. */
+int fo_kv_attention_decode_rows(fo_kv_cache *cache, const float *q, int64_t rows, const float *sinks, float *output,
+                                int mem);
+/* One single-row decode per cache (independent pages), in one launch.  All
+ * caches share one context and head shape; q[i], sinks[i], output[i] are
+ * device pointers.  Each page's result equals its fo_kv_attention_decode. */
+int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const float *const *q,
+                                 const float *const *sinks, float *const *output);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
