@@ -1,0 +1,374 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline: full-page prefill attention, 6,544 tokens =
+4,096-token bidirectional image prefix + 2,448 causal text tokens, 16 query
+heads and 8 KV heads of 64, Q/K ~ N(0, 0.5) with RoPE, V ~ N(0, 1), through
+fo_attention_prefill_bf16 (tcgen05, static-shift softmax: the reference's
+fast-mode default).  A step is one prefill of one page; `value` is tokens/s
+over all ranks with inputs resident in HBM (6 distinct input sets rotate, so
+every step reads from DRAM, not L2).  `e2e` times the same call with FP32
+host buffers (pinned): H2D of Q/K/V, BF16 conversion, attention, D2H of the
+output.  `decode` times 5-row speculative-verify decode
+at 16,384 KV positions over BF16 and FP32 split records, rotating over more
+than 4x L2 of distinct caches.  Pages shard across ranks with no collective
+on the data path (weak scaling); timing is the max over ranks of CUDA-event
+time, bracketed by barriers and synchronizes.
+
+--impl reference times the reference's algorithm on the host cores instead:
+the C restatement of its CPU prefill tiles (oracle/, OpenMP over all
+threads), since the Rust reference cannot be built here.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "falcon-ocr-cpu_b200"))
+sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+
+METRIC = "prefill attn tok/s @6,544 ctx; decode attn µs/step @16,384 KV; % of roofline"
+SEQ, IMAGE_END, HEADS, KV_HEADS = 6544, 4096, 16, 8
+# Visible (query, key) pairs per head: 4096^2 + sum_{t=4097}^{6544} t.
+VISIBLE_PAIRS = IMAGE_END * IMAGE_END + sum(range(IMAGE_END + 1, SEQ + 1))
+FLOP_PER_CALL = 4 * 64 * VISIBLE_PAIRS * HEADS  # QK and PV multiply-adds, 2 FLOP each
+DECODE_L, DECODE_ROWS = 16384, 5
+RECORD_BYTES = {"bf16": 8 * 160 * 2, "f32": 8 * 160 * 4}  # per position, all groups (tail records are smaller)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic():
+    """Per-launch DRAM bytes from the committed ncu summaries (or None)."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ------------------------------------------------------------------ CPU arm
+def cpu_prefill_sample(q, k, v, sinks, image_end, groups_in_sample=1):
+    """Time the oracle's BF16 static tiles (the reference's fast-mode prefill,
+    restated in C, OpenMP over all host threads) on `groups_in_sample` KV
+    groups (2 query heads each) of the full page; returns (seconds for the
+    sample, fraction of the page's work it covers)."""
+    import oracle as O
+    h = 2 * groups_in_sample
+    qs = np.ascontiguousarray(q[:, :h])
+    ks = np.ascontiguousarray(k[:, :h])
+    vs = np.ascontiguousarray(v[:, :groups_in_sample])
+    t0 = time.perf_counter()
+    O.prefill_bf16(qs, ks, vs, h, groups_in_sample, (0, image_end), sinks[:h], softmax_static=True)
+    return time.perf_counter() - t0, h / HEADS
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference algorithm on the host cores (rank 0)."""
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import generators as G
+    import oracle as O
+    q, k, v, sinks, geo = G.c2_inputs(seed=1)
+    cores = O.max_threads()
+    for _ in range(args.warmup):
+        cpu_prefill_sample(q, k, v, sinks, IMAGE_END)
+    times = []
+    frac = 1.0
+    for _ in range(args.steps):
+        t, frac = cpu_prefill_sample(q, k, v, sinks, IMAGE_END)
+        times.append(t)
+    per_page = sum(times) / len(times) / frac
+    value = SEQ / per_page
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_page * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C2 full-page prefill attention, 6,544 tokens (4,096 image + 2,448 text), "
+                               "16 heads x 64, 8 KV heads, BF16 static-shift tiles", "global_batch": 1,
+                   "seq_len": SEQ, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"1 KV group (2 of 16 heads) of the full page per step, scaled x{1 / frac:.0f}; "
+                                   "C restatement of prefill64/bf16 static-shift tiles (oracle/fo_oracle.c)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_ours(args, world, rank, local):
+    import torch
+    import fo_cuda as F
+    import generators as G
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ctx = F.Context(local)  # default stream: ordered with torch's allocations and events
+    peaks = load_peaks()
+    traffic = load_traffic()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------------------------------------------------- prefill inputs
+    q, k, v, sinks, geo = G.c2_inputs(seed=1 + rank)  # each rank its own page
+    n_sets = 6  # 6 x (26.8 MB Q + 13.4 MB K + 6.7 MB V + 26.8 MB out) > 3 x L2
+    sets = []
+    for i in range(n_sets):
+        qd = torch.from_numpy(q).to(dev)
+        if i:
+            qd = qd * (1.0 + 1e-3 * i)
+        kd = torch.from_numpy(k).to(dev)
+        vd = torch.from_numpy(v).to(dev)
+        sets.append(dict(q=qd.contiguous(), kb=kd.to(torch.bfloat16), vb=vd.to(torch.bfloat16),
+                         out=torch.empty(SEQ * HEADS * 64, device=dev), k=kd, v=vd))
+    sd = torch.from_numpy(sinks).to(dev)
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
+
+    def prefill_step(i):
+        s = sets[i % n_sets]
+        F.attention_prefill_bf16(s["q"], s["k"], s["v"], geo, sd, s["out"], HEADS, KV_HEADS,
+                                 keys_bf16=s["kb"], values_bf16=s["vb"], options=opts, ctx=ctx)
+
+    for i in range(max(args.warmup, 3)):
+        prefill_step(i)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record()
+    for i in range(args.steps):
+        prefill_step(i)
+    end.record()
+    barrier()
+    ms_total = max_over_ranks(start.elapsed_time(end))
+    clock_info = clocks.stop()
+    ms_per_step = ms_total / args.steps
+    value = world * args.steps * SEQ / (ms_total / 1e3)
+    achieved_tflops = FLOP_PER_CALL / (ms_per_step / 1e3) / 1e12
+    roof = {"bound": "tensor", "achieved": round(achieved_tflops, 1), "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4),
+            "traffic": traffic.get("prefill_bf16_static"),
+            "note": f"{FLOP_PER_CALL / 1e9:.2f} GFLOP algorithmic per launch (476.83M visible scores x 256); "
+                    f"peak = {peaks['source']} burst bf16"}
+
+    # -------------------------------------------------------------- e2e (host)
+    qh = torch.from_numpy(q.reshape(-1)).pin_memory()
+    kh = torch.from_numpy(k.reshape(-1)).pin_memory()
+    vh = torch.from_numpy(v.reshape(-1)).pin_memory()
+    oh = torch.empty(SEQ * HEADS * 64, dtype=torch.float32).pin_memory()
+    sh = torch.from_numpy(sinks).clone()
+
+    def e2e_step():
+        F.attention_prefill_bf16(qh, kh, vh, geo, sh, oh, HEADS, KV_HEADS, options=opts, ctx=ctx)
+
+    for _ in range(3):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 20))
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record()
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2)) / e2e_steps
+    h2d = (q.size + k.size + v.size) * 4 + HEADS * 4
+    e2e = {"value": world * SEQ / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(SEQ * HEADS * 64 * 4), "ms_per_step": round(e2e_ms, 3)}
+    # parity spot check of the timed output against the e2e output (same inputs, set 0)
+    del sets[1:]
+    torch.cuda.empty_cache()
+
+    # ----------------------------------------------------------------- decode
+    decode = {}
+    rng = np.random.default_rng(2 + rank)
+    for fmt, n_caches in (("bf16", 12), ("f32", 6)):
+        caches = []
+        p = DECODE_L - DECODE_ROWS
+        kp = rng.standard_normal((p, HEADS, 64)).astype(np.float32)
+        kp[:, 1::2, :32] = kp[:, 0::2, :32]
+        vp = rng.standard_normal((p, KV_HEADS, 64)).astype(np.float32)
+        kd, vd = torch.from_numpy(kp).to(dev), torch.from_numpy(vp).to(dev)
+        tk = torch.from_numpy(np.repeat(rng.standard_normal((DECODE_ROWS, KV_HEADS, 1, 64)).astype(np.float32), 2,
+                                        axis=2).reshape(-1)).to(dev)
+        for i in range(n_caches):
+            c = F.SplitPrefix.from_compact(kd if i == 0 else kd * (1 + 1e-3 * i), vd, p, DECODE_L, fmt=fmt, ctx=ctx)
+            c.append(tk, tk)
+            caches.append(c)
+        del kd, vd
+        qd = torch.from_numpy(rng.standard_normal(DECODE_ROWS * HEADS * 64).astype(np.float32)).to(dev)
+        od = torch.empty_like(qd)
+        for i in range(5):
+            caches[i % n_caches].attention_decode_rows(qd, DECODE_ROWS, sd, od)
+        barrier()
+        steps = max(args.steps, 50)
+        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s3.record()
+        for i in range(steps):
+            caches[i % n_caches].attention_decode_rows(qd, DECODE_ROWS, sd, od)
+        e3.record()
+        barrier()
+        us = max_over_ranks(s3.elapsed_time(e3)) * 1e3 / steps
+        bytes_step = p * RECORD_BYTES[fmt] + DECODE_ROWS * KV_HEADS * 128 * (2 if fmt == "bf16" else 4)
+        gbs = bytes_step / (us * 1e-6) / 1e9
+        decode[fmt] = {"us_per_step": round(us, 2), "rows": DECODE_ROWS, "kv_len": DECODE_L,
+                       "bytes_per_step": int(bytes_step),
+                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                                    "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                                    "traffic": traffic.get(f"decode_{fmt}")},
+                       "caches_rotated": n_caches, "gpu_launches_per_step": 2}
+        for c in caches:
+            c.close()
+
+    # ----------------------------------------------------------- CPU baseline
+    cpu = None
+    if rank == 0 and world == 1:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        cpu_prefill_sample(q, k, v, sinks, IMAGE_END)  # warm the pages and threads
+        t, frac = cpu_prefill_sample(q, k, v, sinks, IMAGE_END)
+        cpu = {"value": round(SEQ / (t / frac), 1), "unit": "tok/s", "cores": O.max_threads(), "kind": "port",
+               "sample": f"1 KV group (2 of 16 heads) of the full page, {t:.1f} s, scaled x{1 / frac:.0f}; "
+                         "C restatement of the reference's prefill64/bf16 static-shift tiles"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C2 full-page prefill attention, 6,544 tokens (4,096 image + 2,448 text), "
+                                   "16 heads x 64, 8 KV heads, BF16 static-shift softmax, one page per GPU",
+                       "global_batch": world, "seq_len": SEQ, "parallelism": f"pages x{world}",
+                       "l2": "6 distinct input sets rotate (>3x L2)"},
+            "roofline": roof, "e2e": e2e, "gpu_launches": args.steps, "clocks": clock_info,
+            "decode": decode, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -22,7 +22,7 @@
 extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
                                               const float *sinks, float *out, int64_t total, int64_t n_heads,
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
-                                              int softmax_static, int exp_fast, cudaStream_t stream);
+                                              int softmax_static, int exp_fast, unsigned *err, cudaStream_t stream);
 
 namespace {
 
@@ -92,6 +92,7 @@ struct fo_ctx {
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     unsigned *flags = nullptr;                 // seal status bits
+    unsigned *dev_err = nullptr;               // kernel error bits (bounded waits that gave up)
     DevBuf stage[6];                           // prefill host staging: q, prefix_k, generated_k, v, sinks, out
     DevBuf bf16_k, bf16_v;                     // Bf16Kv::Convert scratch
     DevBuf pages;                              // decode batch descriptors
@@ -184,12 +185,24 @@ int stage_compact(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t 
     return FO_OK;
 }
 
+// Reads and clears the context's device error word (after a synchronize).
+int check_device_errors(fo_ctx *ctx) {
+    unsigned bits = 0;
+    FO_CUDA(cudaMemcpy(&bits, ctx->dev_err, sizeof bits, cudaMemcpyDeviceToHost), "cudaMemcpy(error word)");
+    if (bits) {
+        cudaMemset(ctx->dev_err, 0, sizeof bits);
+        return fail(FO_ERR_CUDA, "a kernel wait exceeded its time limit and the kernel unwound (bits 0x%x)", bits);
+    }
+    return FO_OK;
+}
+
 int finish_host(fo_ctx *ctx, float *host_out, const float *dev_out, int64_t n, int mem) {
     if (mem == FO_MEM_HOST) {
         if (n > 0)
             FO_CUDA(cudaMemcpyAsync(host_out, dev_out, (size_t)n * 4, cudaMemcpyDeviceToHost, ctx->stream),
                     "cudaMemcpyAsync(D2H)");
         FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        return check_device_errors(ctx);
     }
     return FO_OK;
 }
@@ -226,6 +239,8 @@ int fo_ctx_create(int device, void *stream, fo_ctx **out) {
     // NULL is CUDA's default stream, as in the runtime API.
     ctx->stream = (cudaStream_t)stream;
     cudaError_t e = cudaMalloc(&ctx->flags, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->dev_err, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev1);
     if (e == cudaSuccess) e = ctx->pages.ensure(sizeof(fo_decode_page) * 1024);
@@ -247,6 +262,7 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     ctx->bf16_v.release();
     ctx->pages.release();
     if (ctx->flags) cudaFree(ctx->flags);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
     if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -258,7 +274,7 @@ int fo_ctx_synchronize(fo_ctx *ctx) {
     if (!ctx) return fail(FO_ERR_INVALID, "null context");
     DeviceGuard guard(ctx->device);
     FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
-    return FO_OK;
+    return check_device_errors(ctx);
 }
 
 int fo_ctx_last_ms(fo_ctx *ctx, float *ms) {
@@ -348,7 +364,8 @@ int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *
     if (!aligned16(kb) || !aligned16(vb) || !aligned16(s.q) || !aligned16(s.out))
         return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
     e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, T, H, G, geometry.image_start, geometry.image_end,
-                               options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->stream);
+                               options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err,
+                               ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
     if ((st = timed_end(ctx, options.profile)) != FO_OK) return st;
     return finish_host(ctx, output, s.out, query_len * H * 64, mem);

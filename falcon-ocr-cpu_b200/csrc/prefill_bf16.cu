@@ -1,7 +1,391 @@
-// prefill_bf16.cu -- placeholder until the tcgen05 kernel lands.
+// prefill_bf16.cu -- BF16 prefill attention on the sm_100a tensor cores
+// (reference: prefill64/bf16.rs:78-481 with the online softmax, and its
+// static-shift softmax, prefill64/bf16/static_shift.rs:1-340).
+//
+// Semantics kept from the reference: Q, K, V and the probabilities are
+// rounded to BF16 (round to nearest even); scores, softmax state, the PV
+// accumulator and the output stay FP32; the prefix-LM mask hides key > query
+// unless both are image tokens (src/kernels/attention/mod.rs:70-75); the
+// sink enters once at the end through sigmoid(lse - sink).  The static shift
+// computes p = 2^(scale * log2(e) * q.k) without a running maximum and sums
+// the BF16-rounded p (bf16/static_shift.rs:8-23); the online softmax sums the
+// unrounded p (bf16.rs:327-356) and, as the reference does, rescales the
+// output and denominator whenever a tile raises the row maximum, so the
+// largest probability is exactly 1 and loses nothing to BF16 rounding.
+//
+// Structure (one CTA = two 128-query tiles of one head, sharing K/V tiles):
+//   warp 8     TMA producer: K and V tiles [128 keys][64] BF16, 128-byte
+//              swizzle, NS-stage ring with full/empty mbarriers;
+//   warp 9     MMA issuer (one thread): S_t = Q_t K^T (M128 N128 K64) into
+//              TMEM, then O_t += P_t V (M128 N64 K128); tcgen05.commit
+//              signals every consumer; it also owns the TMEM allocation;
+//   warps 0-7  two softmax warpgroups, one per Q tile, one thread per query
+//              row: Q row to BF16 in shared memory, S row from TMEM
+//              (tcgen05.ld), mask, exp2, BF16 P row to shared memory, and
+//              the epilogue O / l * sink from TMEM.
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384).
+// Every wait is bounded (sm100.cuh); on a timeout the CTA unwinds, waits for
+// its own copies and MMAs, frees TMEM and reports through the error word.
+#include <cudaTypedefs.h>
+
 #include "fo_common.cuh"
 #include "fo_kernels.h"
-extern "C" cudaError_t fo_launch_prefill_bf16(const float *, const uint16_t *, const uint16_t *, const float *, float *,
-                                              int64_t, int64_t, int64_t, int64_t, int64_t, int, int, cudaStream_t) {
-    return cudaErrorNotSupported;
+#include "sm100.cuh"
+
+namespace fo {
+using namespace sm100;
+
+constexpr int BT_STAGES = 2;
+constexpr int BT_THREADS = 320;
+constexpr uint32_t BT_TILE = 128 * 128;  // one [128][64] BF16 tile, bytes
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = 2 * BT_TILE;
+constexpr uint32_t OFF_V = OFF_K + BT_STAGES * BT_TILE;
+constexpr uint32_t OFF_P = OFF_V + BT_STAGES * BT_TILE;
+constexpr uint32_t OFF_BAR = OFF_P + 4 * BT_TILE;
+// barriers: q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS],
+// s_full[2], s_empty[2], p_full[2], p_empty[2], mma_done
+constexpr int NBAR = 1 + 4 * BT_STAGES + 8 + 1;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+
+struct Bf16Args {
+    const float *q, *sinks;
+    float *out;
+    unsigned *err;
+    int64_t total, n_heads, n_kv_heads, image_start, image_end;
+};
+
+// Bounded wait that ignores the abort flag (for copies/MMAs that complete on
+// their own), used while unwinding.
+__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t phase) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, phase))
+        if (globaltimer() - t0 > FO_WAIT_NS) break;
+}
+
+template <bool STATIC>
+__global__ void __launch_bounds__(BT_THREADS, 1)
+    prefill_bf16_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Bf16Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+    uint64_t *q_full = bars;
+    uint64_t *k_full = bars + 1, *k_empty = k_full + BT_STAGES;
+    uint64_t *v_full = k_empty + BT_STAGES, *v_empty = v_full + BT_STAGES;
+    uint64_t *s_full = v_empty + BT_STAGES, *s_empty = s_full + 2;
+    uint64_t *p_full = s_empty + 2, *p_empty = p_full + 2;
+    uint64_t *mma_done = p_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t T = a.total, H = a.n_heads;
+    const int64_t npairs = (T + 255) / 256;
+    const int64_t pair = npairs - 1 - blockIdx.x;  // heaviest (latest) tiles first
+    const int64_t head = blockIdx.y;
+    const int64_t kv_head = head / (H / a.n_kv_heads);
+    const int64_t q0 = pair * 256;
+    // Tile span over both Q tiles (src/kernels/attention/prefill64/span.rs:9-20).
+    const int64_t last_abs = min64(q0 + 255, T - 1);
+    int64_t tile_end = last_abs + 1;
+    if (q0 < a.image_end && last_abs >= a.image_start) tile_end = max64(tile_end, a.image_end);
+    const int nkv = (int)((tile_end + 127) / 128);
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 256);
+        for (int s = 0; s < BT_STAGES; s++) {
+            mbar_init(k_full + s, 1);
+            mbar_init(k_empty + s, 1);
+            mbar_init(v_full + s, 1);
+            mbar_init(v_empty + s, 1);
+        }
+        for (int t = 0; t < 2; t++) {
+            mbar_init(s_full + t, 1);
+            mbar_init(s_empty + t, 128);
+            mbar_init(p_full + t, 128);
+            mbar_init(p_empty + t, 1);
+        }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 9) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K), sV = smem_u32(smem + OFF_V),
+                   sP = smem_u32(smem + OFF_P);
+
+    if (warp < 8) {
+        // ------------------------------------------------ softmax warpgroups
+        const int t = warp >> 2, wq = warp & 3, r = threadIdx.x & 127;
+        const int64_t row = q0 + 128 * t + r;
+        {
+            // Q row to BF16 (round to nearest even), 128-byte swizzled rows.
+            uint32_t w[32];
+            if (row < T) {
+                const float4 *src = reinterpret_cast<const float4 *>(a.q + (row * H + head) * FO_HD);
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float4 x = __ldg(src + i);
+                    w[2 * i] = pack_bf16(x.x, x.y);
+                    w[2 * i + 1] = pack_bf16(x.z, x.w);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) w[i] = 0;
+            }
+            const uint32_t base = sQ + t * BT_TILE + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; c++)
+                st_shared_v4(base + ((c ^ (r & 7)) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+            fence_proxy_async_smem();
+            mbar_arrive(q_full);
+        }
+        const int64_t vend = row < T ? visible_end(row, a.image_start, a.image_end) : 0;
+        const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
+        const uint32_t s_tm = tmem + lane_base + 128 * t;
+        const uint32_t o_tm = tmem + lane_base + 256 + 64 * t;
+        const uint32_t p_row = sP + t * 2 * BT_TILE + r * 128;
+        const float C = 0.125f * 1.44269504088896340736f;  // scale * log2(e)
+        float l = 0.0f, m2 = -INFINITY;
+        bool ok = true;
+        for (int j = 0; j < nkv; j++) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full + t, j & 1, abort_flag, a.err));
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t s[128];
+            FO_TMEM_LD32(s_tm + 0, (s + 0));
+            FO_TMEM_LD32(s_tm + 32, (s + 32));
+            FO_TMEM_LD32(s_tm + 64, (s + 64));
+            FO_TMEM_LD32(s_tm + 96, (s + 96));
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(s_empty + t);
+            const int nvis = (int)max64(0, min64(128, vend - 128 * (int64_t)j));
+            float shift = 0.0f, factor = 1.0f;
+            if constexpr (!STATIC) {
+                float bm = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 128; c++)
+                    if (c < nvis) bm = fmaxf(bm, __uint_as_float(s[c]) * C);
+                if (bm > m2) {  // also true on the first visible tile
+                    if (m2 != -INFINITY) factor = ex2(m2 - bm);
+                    m2 = bm;
+                }
+                shift = m2 == -INFINITY ? 0.0f : m2;
+                l *= factor;
+            }
+            // P_t is free once PV_t(j-1) has completed.
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(p_empty + t, (j - 1) & 1, abort_flag, a.err));
+                if (!ok) break;
+            }
+            if constexpr (!STATIC) {
+                if (__any_sync(0xffffffffu, factor != 1.0f)) {
+                    // Rescale this row of O_t (PV_t(j-1) is complete).
+                    tc_fence_after();
+                    uint32_t o[32];
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        FO_TMEM_LD32(o_tm + 32 * h, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+                        FO_TMEM_ST32(o_tm + 32 * h, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+#pragma unroll
+            for (int cc = 0; cc < 16; cc++) {  // 16 chunks of 8 keys
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int c = 8 * cc + 2 * e;
+                    float x0, x1;
+                    if constexpr (STATIC) {
+                        x0 = c < nvis ? ex2(__uint_as_float(s[c]) * C) : 0.0f;
+                        x1 = c + 1 < nvis ? ex2(__uint_as_float(s[c + 1]) * C) : 0.0f;
+                    } else {
+                        x0 = c < nvis ? ex2(__uint_as_float(s[c]) * C - shift) : 0.0f;
+                        x1 = c + 1 < nvis ? ex2(__uint_as_float(s[c + 1]) * C - shift) : 0.0f;
+                    }
+                    w[e] = pack_bf16(x0, x1);
+                    if constexpr (STATIC) {  // sum the rounded probabilities PV multiplies
+                        l += __uint_as_float(w[e] << 16);
+                        l += __uint_as_float(w[e] & 0xFFFF0000u);
+                    } else {  // sum the unrounded probabilities
+                        l += x0;
+                        l += x1;
+                    }
+                }
+                const int b = cc >> 3, ch = cc & 7;
+                st_shared_v4(p_row + b * BT_TILE + ((ch ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full + t);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(p_empty + t, (nkv - 1) & 1, abort_flag, a.err));
+        if (ok) {
+            tc_fence_after();
+            uint32_t o[64];
+            FO_TMEM_LD32(o_tm, (o + 0));
+            FO_TMEM_LD32(o_tm + 32, (o + 32));
+            tmem_wait_ld();
+            if (row < T) {
+                const float lse = STATIC ? logf(l) : m2 * 0.69314718055994530942f + logf(l);
+                const float ss = sink_scale(a.sinks[head], lse);
+                float4 *dst = reinterpret_cast<float4 *>(a.out + (row * H + head) * FO_HD);
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    float4 v;
+                    v.x = (__uint_as_float(o[4 * i]) / l) * ss;
+                    v.y = (__uint_as_float(o[4 * i + 1]) / l) * ss;
+                    v.z = (__uint_as_float(o[4 * i + 2]) / l) * ss;
+                    v.w = (__uint_as_float(o[4 * i + 3]) / l) * ss;
+                    dst[i] = v;
+                }
+            }
+        }
+    } else if (warp == 8) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch(&tmk);
+            tma_prefetch(&tmv);
+            int issued = 0;
+            bool ok = true;
+            for (int j = 0; j < nkv && ok; j++) {
+                const int st = j % BT_STAGES, u = j / BT_STAGES;
+                if (u > 0 && !(ok = mbar_wait(k_empty + st, (u - 1) & 1, abort_flag, a.err))) break;
+                mbar_expect_tx(k_full + st, BT_TILE);
+                tma_load_3d(smem + OFF_K + st * BT_TILE, &tmk, k_full + st, 0, (int)head, 128 * j);
+                if (u > 0 && !(ok = mbar_wait(v_empty + st, (u - 1) & 1, abort_flag, a.err))) {
+                    issued = 2 * j + 1;
+                    break;
+                }
+                mbar_expect_tx(v_full + st, BT_TILE);
+                tma_load_3d(smem + OFF_V + st * BT_TILE, &tmv, v_full + st, 0, (int)kv_head, 128 * j);
+                issued = 2 * j + 2;
+            }
+            if (!ok) {
+                // Unwinding: let the copies still in flight land before exit.
+                for (int i = max(0, issued - 2 * BT_STAGES); i < issued; i++) {
+                    const int j = i >> 1, st = j % BT_STAGES;
+                    drain_wait((i & 1) ? v_full + st : k_full + st, (j / BT_STAGES) & 1);
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idS = idesc_bf16(128, 128, 0), idPV = idesc_bf16(128, 64, 1);
+            auto issue_s = [&](int t, int st) {
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    mma_bf16(tmem + 128 * t, sdesc_sw128(sQ + t * BT_TILE + 32 * kk, 16, 1024),
+                             sdesc_sw128(sK + st * BT_TILE + 32 * kk, 16, 1024), idS, kk > 0);
+            };
+            auto issue_pv = [&](int t, int st, int j) {
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++)
+                    mma_bf16(tmem + 256 + 64 * t,
+                             sdesc_sw128(sP + t * 2 * BT_TILE + (kk >> 2) * BT_TILE + (kk & 3) * 32, 16, 1024),
+                             sdesc_sw128(sV + st * BT_TILE + kk * 2048, BT_TILE, 1024), idPV, (j > 0 || kk > 0));
+            };
+            bool ok = mbar_wait(q_full, 0, abort_flag, a.err) && mbar_wait(k_full, 0, abort_flag, a.err);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, 0);
+                mma_commit(s_full + 0);
+                issue_s(1, 0);
+                mma_commit(s_full + 1);
+                mma_commit(k_empty + 0);
+            }
+            for (int j = 0; j < nkv && ok; j++) {
+                if (j + 1 < nkv) {
+                    const int st1 = (j + 1) % BT_STAGES, u1 = (j + 1) / BT_STAGES;
+                    if (!(ok = mbar_wait(k_full + st1, u1 & 1, abort_flag, a.err))) break;
+                    for (int t = 0; t < 2 && ok; t++) {
+                        if (!(ok = mbar_wait(s_empty + t, j & 1, abort_flag, a.err))) break;
+                        tc_fence_after();
+                        issue_s(t, st1);
+                        mma_commit(s_full + t);
+                    }
+                    if (!ok) break;
+                    mma_commit(k_empty + st1);
+                }
+                const int st = j % BT_STAGES, u = j / BT_STAGES;
+                if (!(ok = mbar_wait(v_full + st, u & 1, abort_flag, a.err))) break;
+                for (int t = 0; t < 2 && ok; t++) {
+                    if (!(ok = mbar_wait(p_full + t, j & 1, abort_flag, a.err))) break;
+                    tc_fence_after();
+                    issue_pv(t, st, j);
+                    mma_commit(p_empty + t);
+                }
+                if (!ok) break;
+                mma_commit(v_empty + st);
+            }
+            // Every issued MMA completes before TMEM is released.
+            mma_commit(mma_done);
+            drain_wait(mma_done, 0);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// [rows][heads][64] BF16, box of 128 rows of one head, 128-byte swizzle.
+static bool make_map(CUtensorMap *m, const uint16_t *base, int64_t rows, int64_t heads) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {64, (cuuint64_t)heads, (cuuint64_t)rows};
+    cuuint64_t strides[2] = {64 * 2, (cuuint64_t)heads * 64 * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace fo
+
+extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
+                                              const float *sinks, float *out, int64_t total, int64_t n_heads,
+                                              int64_t n_kv_heads, int64_t image_start, int64_t image_end,
+                                              int softmax_static, int exp_fast, unsigned *err, cudaStream_t stream) {
+    (void)exp_fast;  // the tensor-core softmax always takes the hardware exp2
+    if (total == 0) return cudaSuccess;
+    CUtensorMap mk, mv;
+    if (!fo::make_map(&mk, keys_bf16, total, n_heads) || !fo::make_map(&mv, values_bf16, total, n_kv_heads))
+        return cudaErrorInvalidValue;
+    fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end};
+    dim3 grid((unsigned)((total + 255) / 256), (unsigned)n_heads);
+    auto launch = [&](auto kernel) -> cudaError_t {
+        cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fo::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        kernel<<<grid, fo::BT_THREADS, fo::SMEM_BYTES, stream>>>(mk, mv, args);
+        return cudaGetLastError();
+    };
+    return softmax_static ? launch(fo::prefill_bf16_kernel<true>) : launch(fo::prefill_bf16_kernel<false>);
 }

@@ -150,19 +150,24 @@ def _is_torch(x) -> bool:
     return type(x).__module__.startswith("torch")
 
 
+def _on_device(a) -> bool:
+    return _is_torch(a) and a.is_cuda
+
+
 def _ptr_mem(arrays):
-    """Pointers of a call's arrays and its memory mode; all host or all device."""
-    kinds = {_is_torch(a) for a in arrays if a is not None}
+    """Pointers of a call's arrays and its memory mode: all host (numpy
+    arrays or CPU torch tensors, e.g. pinned) or all device (CUDA tensors)."""
+    kinds = {_on_device(a) for a in arrays if a is not None}
     if len(kinds) > 1:
-        raise FoError("mix of host (numpy) and device (torch) arrays in one call")
+        raise FoError("mix of host and device arrays in one call")
     device = kinds == {True}
     ptrs = []
     for a in arrays:
         if a is None:
             ptrs.append(None)
-        elif device:
-            if not a.is_cuda or not a.is_contiguous():
-                raise FoError("device arrays must be contiguous CUDA tensors")
+        elif _is_torch(a):
+            if not a.is_contiguous():
+                raise FoError("arrays must be contiguous")
             ptrs.append(a.data_ptr())
         else:
             if not (a.flags["C_CONTIGUOUS"]):

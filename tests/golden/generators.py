@@ -201,3 +201,31 @@ SAMPLE_HEADS = (0, 9)
 
 def sample_heads(out, heads=16, dim=64):
     return np.asarray(out).reshape(-1, heads, dim)[:, list(SAMPLE_HEADS), :].reshape(-1)
+
+
+def rope_interleaved(x: np.ndarray, theta: float = 10000.0) -> np.ndarray:
+    """Rotate interleaved pairs (2i, 2i+1) of every 64-wide head of
+    x [S][H][64] by position * theta^(-2i/64), as src/model/rope.rs:55-67
+    applies its [cos, sin] factors."""
+    s = x.shape[0]
+    i = np.arange(32, dtype=np.float64)
+    angle = np.arange(s, dtype=np.float64)[:, None] * theta ** (-2.0 * i / 64.0)[None, :]
+    cos = np.cos(angle).astype(np.float32)[:, None, :]
+    sin = np.sin(angle).astype(np.float32)[:, None, :]
+    a, b = x[..., 0::2], x[..., 1::2]
+    out = np.empty_like(x)
+    out[..., 0::2] = a * cos - b * sin
+    out[..., 1::2] = a * sin + b * cos
+    return out
+
+
+def c2_inputs(seed: int = 1, seq: int = 6544, image_end: int = 4096, heads: int = 16, kv_heads: int = 8):
+    """full-page prefill, 4,096 bidirectional image tokens
+    then causal text; Q, K ~ N(0, 0.5) (0.5 is the variance) rotated by RoPE
+    theta 10,000 at their positions; V ~ N(0, 1); sinks ~ N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    q = rope_interleaved((rng.standard_normal((seq, heads, 64)) * np.sqrt(0.5)).astype(np.float32))
+    k = rope_interleaved((rng.standard_normal((seq, heads, 64)) * np.sqrt(0.5)).astype(np.float32))
+    v = rng.standard_normal((seq, kv_heads, 64)).astype(np.float32)
+    sinks = rng.standard_normal(heads).astype(np.float32)
+    return q, k, v, sinks, (0, 0, image_end)

@@ -110,11 +110,14 @@ def test_fp32_static_shift_tiles(ctx, i):
     close(G.sample_heads(out), GOLD[f"static_{i}"], 1e-5, 0.0)
 
 
-@pytest.mark.parametrize("case", [(4, 137, 141, 137, 1, 129), (9, 128, 137, 128, 1, 129), (33, 100, 133, 100, 1, 90),
-                                  (2, 300, 302, 300, 5, 262), (1, 267, 268, 267, 1, 201)])
+@pytest.mark.parametrize("case", [(4, 137, 141, 137, 1, 129), (9, 128, 137, 128, 1, 128), (33, 100, 133, 100, 1, 90),
+                                  (40, 3, 43, 3, 1, 3), (5, 250, 300, 295, 0, 0), (2, 300, 302, 300, 5, 262),
+                                  (1, 267, 268, 267, 1, 201)])
 def test_mixed_caches(ctx, case):
     """Prefix keys per query head plus generated keys per KV head
-    (src/kernels/attention/prefill64/tests.rs:91-140 shapes)."""
+    (src/kernels/attention/prefill64/tests.rs:96-103 shapes; image ends past
+    the prefix are clamped to it, as CompactKv::validate requires,
+    src/kernels/attention/mod.rs:184-187)."""
     ql, pl, tl, off, ist, ien = case
     q = G.prefill_values(ql * 16 * 64, 5 + ql, 3.0)
     pk = G.prefill_values(pl * 16 * 64, 7 + ql, 3.0)
@@ -320,15 +323,15 @@ def test_baseline_c3_verify_rows(ctx, fmt, length):
     """5 rows (1 accepted + 4 drafts) at 6,544/12,000/16,384,
     N(0,1) seed 2, temporal halves shared inside each pair."""
     rng = np.random.default_rng(2)
-    p = length - 4
+    p = length - 5  # the 5 query rows are the last 5 cached positions (kv.rs:851-855)
     k = rng.standard_normal((p, 16, 64)).astype(np.float32)
     k[:, 1::2, :32] = k[:, 0::2, :32]
     v = rng.standard_normal((p, 8, 64)).astype(np.float32)
     ref = O.SplitCache(k, v, p, length, fmt=fmt, chunks=4)
     gpu = F.SplitPrefix.from_compact(dev(k), dev(v), p, length, fmt=fmt)
-    tk = rng.standard_normal((4, 8, 64)).astype(np.float32)
-    tv = rng.standard_normal((4, 8, 64)).astype(np.float32)
-    for t in range(4):
+    tk = rng.standard_normal((5, 8, 64)).astype(np.float32)
+    tv = rng.standard_normal((5, 8, 64)).astype(np.float32)
+    for t in range(5):
         ref.push(tk[t], tv[t])
     gpu.append(np.repeat(tk[:, :, None], 2, axis=2).reshape(-1), np.repeat(tv[:, :, None], 2, axis=2).reshape(-1))
     q = rng.standard_normal(5 * 1024).astype(np.float32)

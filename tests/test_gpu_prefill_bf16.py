@@ -1,0 +1,95 @@
+"""GPU parity of the tcgen05 BF16 prefill (fo_attention_prefill_bf16) with
+the reference's BF16 bounds and the CPU oracle.
+
+Bounds (reference project): static shift within 3 * 2 * (2^-8 + 7.5e-5) +
+1e-4 of f64 on BF16 operands of norm-8 heads (bf16/static_shift/tests.rs:
+234-285); online within 3 * 2^-9 + 2e-3 of the BF16-operand f64
+(prefill64/bf16.rs:851-926); the full page within 2e-2 * (1 + |b|) of the
+oracle (BASELINE's BF16 tolerance)."""
+
+import numpy as np
+import pytest
+
+import fo_cuda as F
+import generators as G
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+STATIC_BOUND = 3 * 2 * (2.0 ** -8 + 7.5e-5) + 1e-4
+ONLINE_BOUND = 3 * 2.0 ** -9 + 2e-3
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def run(q, k, v, sinks, image, static, heads=16, kv_heads=8, converted=False):
+    out = torch.zeros(q.size, dtype=torch.float32, device="cuda")
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC if static else F.SOFTMAX_ONLINE, F.SOFTMAX_ONLINE)
+    kb = vb = None
+    dq, dk, dv = dev(q), dev(k), dev(v)
+    if converted:
+        kb = dk.to(torch.bfloat16)
+        vb = dv.to(torch.bfloat16)
+    F.attention_prefill_bf16(dq, dk, dv, (0, image[0], image[1]), dev(sinks), out, heads, kv_heads,
+                             keys_bf16=kb, values_bf16=vb, options=opts)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def worst(a, b):
+    return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))))
+
+
+@pytest.mark.parametrize("case", G.BF16_CASES + [(5, 1, 3), (256, 0, 100), (513, 7, 400), (384, 0, 0)])
+def test_static_shift_against_f64(case):
+    ql, ist, ien = case
+    q, k, v, s = G.static_operands(ql, ql)
+    q, k, v = G.bf16_round(q), G.bf16_round(k), G.bf16_round(v)
+    out = run(q, k, v, s, (ist, ien), static=True)
+    ref = G.attention_f64(q, k, v, 16, 8, 64, (0, ist, ien), s)
+    assert worst(out, ref) <= STATIC_BOUND
+    assert worst(out, O.prefill_bf16(q, k, v, 16, 8, (ist, ien), s, softmax_static=True)) <= 2 * STATIC_BOUND
+
+
+@pytest.mark.parametrize("case", G.BF16_CASES + [(5, 1, 3), (256, 0, 100), (513, 7, 400)])
+def test_online_against_f64(case):
+    ql, ist, ien = case
+    q, k, v, s = G.bf16_operands(ql)
+    out = run(q, k, v, s, (ist, ien), static=False)
+    ref = G.attention_f64(q, k, v, 16, 8, 64, (0, ist, ien), s)
+    assert worst(out, ref) <= ONLINE_BOUND
+    assert worst(out, O.prefill_bf16(q, k, v, 16, 8, (ist, ien), s, softmax_static=False)) <= 2 * ONLINE_BOUND
+
+
+def test_converted_operands_equal_converting():
+    """Bf16Kv::Converted and Bf16Kv::Convert give the same bits
+    (prefill64/bf16.rs:781-845)."""
+    q, k, v, s = G.bf16_operands(300)
+    for static in (True, False):
+        a = run(q, k, v, s, (5, 262), static=static)
+        b = run(q, k, v, s, (5, 262), static=static, converted=True)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_deterministic():
+    q, k, v, s = G.bf16_operands(257)
+    a = run(q, k, v, s, (0, 257), static=False)
+    b = run(q, k, v, s, (0, 257), static=False)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("static", [True, False])
+def test_baseline_c2_full_page(static):
+    """6,544 tokens, 4,096-token image prefix, seed 1,
+    against the oracle's BF16 tiles at 2e-2 * (1 + |b|)."""
+    q, k, v, s, geo = G.c2_inputs()
+    out = run(q, k, v, s, geo[1:], static=static)
+    ref = O.prefill_bf16(q, k, v, 16, 8, geo[1:], s, softmax_static=static)
+    err = np.abs(out.astype(np.float64) - ref) - 2e-2 * (1.0 + np.abs(ref))
+    assert (err <= 0).all(), f"worst excess {err.max():.3e}"
+    # and against the FP32 exact tiles of the same inputs, at the same bound
+    fp32 = O.prefill64(q, k, v, 16, 8, geo, s)
+    assert (np.abs(out - fp32) <= 2e-2 * (1.0 + np.abs(fp32))).all()
