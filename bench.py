@@ -183,177 +183,207 @@ def run_reference(args, world, rank):
 
 
 # ------------------------------------------------------------------ GPU arm
-def run_ours(args, world, rank, local):
-    import torch
-    import fo_cuda as F
-    import generators as G
+class Runner:
+    """One rank's device, context and timing helpers."""
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    ctx = F.Context(local)  # default stream: ordered with torch's allocations and events
-    peaks = load_peaks()
-    traffic = load_traffic()
-
-    def barrier():
-        torch.cuda.synchronize()
+    def __init__(self, world, rank, local):
+        import torch
+        import fo_cuda as F
+        self.torch, self.F = torch, F
+        self.world, self.rank, self.local = world, rank, local
+        torch.cuda.set_device(local)
+        self.dev = torch.device("cuda", local)
         if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+        self.ctx = F.Context(local)  # default stream: ordered with torch's allocations and events
+        self.peaks = load_peaks()
+        self.traffic = load_traffic()
+
+    def barrier(self):
+        self.torch.cuda.synchronize()
+        if self.world > 1:
             import torch.distributed as dist
             dist.barrier()
-        torch.cuda.synchronize()
+        self.torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
             return x
         import torch.distributed as dist
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---------------------------------------------------------- prefill inputs
-    q, k, v, sinks, geo = G.c2_inputs(seed=1 + rank)  # each rank its own page
-    n_sets = 6  # 6 x (26.8 MB Q + 13.4 MB K + 6.7 MB V + 26.8 MB out) > 3 x L2
+    def timed(self, step, steps, clocks=False):
+        """Device milliseconds of `steps` calls of step(i), max over ranks."""
+        torch = self.torch
+        sampler = ClockSampler(self.local) if clocks else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        start.record()
+        for i in range(steps):
+            step(i)
+        end.record()
+        self.barrier()
+        ms = self.max_over_ranks(start.elapsed_time(end))
+        return ms, (sampler.stop() if sampler else None)
+
+    def close(self):
+        self.ctx.close()
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def prefill_inputs(rank):
+    import generators as G
+    return G.c2_inputs(seed=1 + rank)  # each rank prefills its own page
+
+
+def time_prefill(run, args, inputs, n_sets):
+    """Device time of the BF16 prefill with Q (FP32) and BF16 K/V resident."""
+    torch, F = run.torch, run.F
+    q, k, v, sinks, geo = inputs
     sets = []
     for i in range(n_sets):
-        qd = torch.from_numpy(q).to(dev)
+        qd = torch.from_numpy(q).to(run.dev)
         if i:
             qd = qd * (1.0 + 1e-3 * i)
-        kd = torch.from_numpy(k).to(dev)
-        vd = torch.from_numpy(v).to(dev)
-        sets.append(dict(q=qd.contiguous(), kb=kd.to(torch.bfloat16), vb=vd.to(torch.bfloat16),
-                         out=torch.empty(SEQ * HEADS * 64, device=dev), k=kd, v=vd))
-    sd = torch.from_numpy(sinks).to(dev)
+        kd, vd = torch.from_numpy(k).to(run.dev), torch.from_numpy(v).to(run.dev)
+        sets.append(dict(q=qd.contiguous(), k=kd, v=vd, kb=kd.to(torch.bfloat16), vb=vd.to(torch.bfloat16),
+                         out=torch.empty(SEQ * HEADS * 64, device=run.dev)))
+    sd = torch.from_numpy(sinks).to(run.dev)
     opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
 
-    def prefill_step(i):
+    def step(i):
         s = sets[i % n_sets]
-        F.attention_prefill_bf16(s["q"], s["k"], s["v"], geo, sd, s["out"], HEADS, KV_HEADS,
-                                 keys_bf16=s["kb"], values_bf16=s["vb"], options=opts, ctx=ctx)
+        F.attention_prefill_bf16(s["q"], s["k"], s["v"], geo, sd, s["out"], HEADS, KV_HEADS, keys_bf16=s["kb"],
+                                 values_bf16=s["vb"], options=opts, ctx=run.ctx)
 
     for i in range(max(args.warmup, 3)):
-        prefill_step(i)
-    barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    start.record()
-    for i in range(args.steps):
-        prefill_step(i)
-    end.record()
-    barrier()
-    ms_total = max_over_ranks(start.elapsed_time(end))
-    clock_info = clocks.stop()
-    ms_per_step = ms_total / args.steps
-    value = world * args.steps * SEQ / (ms_total / 1e3)
-    achieved_tflops = FLOP_PER_CALL / (ms_per_step / 1e3) / 1e12
-    roof = {"bound": "tensor", "achieved": round(achieved_tflops, 1), "peak": peaks["bf16_tflops"],
-            "unit": "TFLOP/s", "frac": round(achieved_tflops / peaks["bf16_tflops"], 4),
-            "traffic": traffic.get("prefill_bf16_static"),
-            "note": f"{FLOP_PER_CALL / 1e9:.2f} GFLOP algorithmic per launch (476.83M visible scores x 256); "
-                    f"peak = {peaks['source']} burst bf16"}
+        step(i)
+    ms, clocks = run.timed(step, args.steps, clocks=True)
+    ms_per_step = ms / args.steps
+    achieved = FLOP_PER_CALL / (ms_per_step / 1e3) / 1e12
+    peak = run.peaks["bf16_tflops"]
+    roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": run.traffic.get("prefill_bf16_static"),
+            "note": f"{FLOP_PER_CALL / 1e9:.2f} GFLOP algorithmic per launch (476.83M visible scores x 256 FLOP); "
+                    f"peak = {run.peaks['source']} burst bf16 (of measured)"}
+    value = run.world * args.steps * SEQ / (ms / 1e3)
+    del sets
+    torch.cuda.empty_cache()
+    return value, ms_per_step, roof, clocks
 
-    # -------------------------------------------------------------- e2e (host)
+
+def time_e2e(run, args, inputs):
+    """The same call through the C ABI with pinned FP32 host buffers: H2D of
+    Q/K/V/sinks, BF16 conversion, attention, D2H of the output."""
+    torch, F = run.torch, run.F
+    q, k, v, sinks, geo = inputs
     qh = torch.from_numpy(q.reshape(-1)).pin_memory()
     kh = torch.from_numpy(k.reshape(-1)).pin_memory()
     vh = torch.from_numpy(v.reshape(-1)).pin_memory()
     oh = torch.empty(SEQ * HEADS * 64, dtype=torch.float32).pin_memory()
     sh = torch.from_numpy(sinks).clone()
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
 
-    def e2e_step():
-        F.attention_prefill_bf16(qh, kh, vh, geo, sh, oh, HEADS, KV_HEADS, options=opts, ctx=ctx)
+    def step(_):
+        F.attention_prefill_bf16(qh, kh, vh, geo, sh, oh, HEADS, KV_HEADS, options=opts, ctx=run.ctx)
 
-    for _ in range(3):
-        e2e_step()
-    e2e_steps = max(3, min(args.steps, 20))
-    barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e2.record()
-    barrier()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2)) / e2e_steps
-    h2d = (q.size + k.size + v.size) * 4 + HEADS * 4
-    e2e = {"value": world * SEQ / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
-           "d2h_bytes_per_step": int(SEQ * HEADS * 64 * 4), "ms_per_step": round(e2e_ms, 3)}
-    # parity spot check of the timed output against the e2e output (same inputs, set 0)
-    del sets[1:]
-    torch.cuda.empty_cache()
+    for i in range(3):
+        step(i)
+    steps = max(3, min(args.steps, 20))
+    ms, _ = run.timed(step, steps)
+    ms /= steps
+    h2d = (q.size + k.size + v.size + sinks.size) * 4
+    return {"value": round(run.world * SEQ / (ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(SEQ * HEADS * 64 * 4), "ms_per_step": round(ms, 3)}
 
-    # ----------------------------------------------------------------- decode
-    decode = {}
-    rng = np.random.default_rng(2 + rank)
+
+def time_decode(run, args):
+    """5-row verify decode at 16,384 positions over BF16 and FP32 records,
+    rotating distinct caches (more than 4x L2)."""
+    torch, F = run.torch, run.F
+    rng = np.random.default_rng(2 + run.rank)
+    sd = torch.from_numpy(rng.standard_normal(HEADS).astype(np.float32)).to(run.dev)
+    out = {}
     for fmt, n_caches in (("bf16", 12), ("f32", 6)):
-        caches = []
         p = DECODE_L - DECODE_ROWS
         kp = rng.standard_normal((p, HEADS, 64)).astype(np.float32)
         kp[:, 1::2, :32] = kp[:, 0::2, :32]
         vp = rng.standard_normal((p, KV_HEADS, 64)).astype(np.float32)
-        kd, vd = torch.from_numpy(kp).to(dev), torch.from_numpy(vp).to(dev)
-        tk = torch.from_numpy(np.repeat(rng.standard_normal((DECODE_ROWS, KV_HEADS, 1, 64)).astype(np.float32), 2,
-                                        axis=2).reshape(-1)).to(dev)
+        kd, vd = torch.from_numpy(kp).to(run.dev), torch.from_numpy(vp).to(run.dev)
+        tail = np.repeat(rng.standard_normal((DECODE_ROWS, KV_HEADS, 1, 64)).astype(np.float32), 2, axis=2)
+        td = torch.from_numpy(tail.reshape(-1)).to(run.dev)
+        caches = []
         for i in range(n_caches):
-            c = F.SplitPrefix.from_compact(kd if i == 0 else kd * (1 + 1e-3 * i), vd, p, DECODE_L, fmt=fmt, ctx=ctx)
-            c.append(tk, tk)
+            c = F.SplitPrefix.from_compact(kd if i == 0 else kd * (1 + 1e-3 * i), vd, p, DECODE_L, fmt=fmt,
+                                           ctx=run.ctx)
+            c.append(td, td)
             caches.append(c)
         del kd, vd
-        qd = torch.from_numpy(rng.standard_normal(DECODE_ROWS * HEADS * 64).astype(np.float32)).to(dev)
+        qd = torch.from_numpy(rng.standard_normal(DECODE_ROWS * HEADS * 64).astype(np.float32)).to(run.dev)
         od = torch.empty_like(qd)
-        for i in range(5):
+
+        def step(i):
             caches[i % n_caches].attention_decode_rows(qd, DECODE_ROWS, sd, od)
-        barrier()
-        steps = max(args.steps, 50)
-        s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s3.record()
-        for i in range(steps):
-            caches[i % n_caches].attention_decode_rows(qd, DECODE_ROWS, sd, od)
-        e3.record()
-        barrier()
-        us = max_over_ranks(s3.elapsed_time(e3)) * 1e3 / steps
+
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        steps = max(args.steps, 50) if args.mode == "full" else args.steps
+        ms, _ = run.timed(step, steps)
+        us = ms * 1e3 / steps
         bytes_step = p * RECORD_BYTES[fmt] + DECODE_ROWS * KV_HEADS * 128 * (2 if fmt == "bf16" else 4)
         gbs = bytes_step / (us * 1e-6) / 1e9
-        decode[fmt] = {"us_per_step": round(us, 2), "rows": DECODE_ROWS, "kv_len": DECODE_L,
-                       "bytes_per_step": int(bytes_step),
-                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
-                                    "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
-                                    "traffic": traffic.get(f"decode_{fmt}")},
-                       "caches_rotated": n_caches, "gpu_launches_per_step": 2}
+        out[fmt] = {"us_per_step": round(us, 2), "rows": DECODE_ROWS, "kv_len": DECODE_L,
+                    "bytes_per_step": int(bytes_step),
+                    "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"],
+                                 "unit": "GB/s", "frac": round(gbs / run.peaks["hbm_gbs"], 4),
+                                 "traffic": run.traffic.get(f"decode_{fmt}")},
+                    "caches_rotated": n_caches, "gpu_launches_per_step": 2}
         for c in caches:
             c.close()
+        torch.cuda.empty_cache()
+    return out
 
-    # ----------------------------------------------------------- CPU baseline
-    cpu = None
-    if rank == 0 and world == 1:
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-        cpu_prefill_sample(q, k, v, sinks, IMAGE_END)  # warm the pages and threads
-        t, frac = cpu_prefill_sample(q, k, v, sinks, IMAGE_END)
-        cpu = {"value": round(SEQ / (t / frac), 1), "unit": "tok/s", "cores": O.max_threads(), "kind": "port",
-               "sample": f"1 KV group (2 of 16 heads) of the full page, {t:.1f} s, scaled x{1 / frac:.0f}; "
-                         "C restatement of the reference's prefill64/bf16 static-shift tiles"}
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+def run_ours(args, world, rank, local):
+    run = Runner(world, rank, local)
+    inputs = prefill_inputs(rank)
+    line = {"metric": METRIC, "value": None, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "C2 full-page prefill attention, 6,544 tokens (4,096 image + 2,448 text), "
                                    "16 heads x 64, 8 KV heads, BF16 static-shift softmax, one page per GPU",
                        "global_batch": world, "seq_len": SEQ, "parallelism": f"pages x{world}",
-                       "l2": "6 distinct input sets rotate (>3x L2)"},
-            "roofline": roof, "e2e": e2e, "gpu_launches": args.steps, "clocks": clock_info,
-            "decode": decode, "cpu_baseline": cpu,
-        }
+                       "l2": "6 distinct input sets rotate (>3x L2)"}}
+    if args.mode in ("full", "prefill"):
+        value, ms_per_step, roof, clocks = time_prefill(run, args, inputs, 6 if args.mode == "full" else 1)
+        line.update(value=round(value, 1), ms_per_step=round(ms_per_step, 4), roofline=roof, clocks=clocks,
+                    gpu_launches=args.steps)
+    if args.mode == "full":
+        line["e2e"] = time_e2e(run, args, inputs)
+    if args.mode in ("full", "decode"):
+        line["decode"] = time_decode(run, args)
+    if args.mode == "full" and rank == 0 and world == 1:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        q, k, v, sinks, _ = inputs
+        cpu_prefill_sample(q, k, v, sinks, IMAGE_END)  # warm the pages and threads
+        t, frac = cpu_prefill_sample(q, k, v, sinks, IMAGE_END)
+        line["cpu_baseline"] = {
+            "value": round(SEQ / (t / frac), 1), "unit": "tok/s", "cores": O.max_threads(), "kind": "port",
+            "sample": f"1 KV group (2 of 16 heads) of the full page, {t:.2f} s, scaled x{1 / frac:.0f}; "
+                      "C restatement of the reference's prefill64/bf16 static-shift tiles"}
+    if rank == 0:
         print(json.dumps(line), flush=True)
-    ctx.close()
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    run.close()
 
 
 def main():
@@ -362,6 +392,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["full", "prefill", "decode"], default="full",
+                    help="full: the contract line; prefill/decode: only that part (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":
