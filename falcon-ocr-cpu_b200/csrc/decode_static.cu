@@ -1,0 +1,117 @@
+// decode_static.cu -- verify-row decode that allocates nothing.
+//
+// Some callers cannot allocate device memory when they decode: a serving
+// runtime that owns every byte of the GPU through its own pool, or a decode
+// loop that must not call cudaMalloc/cudaFree, which can synchronize the
+// whole device and stall the other streams that share it.  This entry point
+// takes the sealed records, the queries, the sinks and the output from the
+// caller, and keeps the split-KV partials (the only scratch the decode
+// kernels need) in one fixed array compiled into this library.
+//
+// Limits: at most FO_STATIC_ROWS rows, FO_STATIC_HEADS query heads and
+// FO_STATIC_POSITIONS cached positions (prefix + tail), the shapes of the
+// reference model (8 verification rows, 16 heads, a 16,384-token context);
+// larger calls are refused.  Every GPU that loads this library holds the
+// array (about 2.1 MiB) until the process exits.
+//
+// The first call on each device looks the array's device address up
+// (cudaGetSymbolAddress, with that device current); make that first call
+// before any stream capture.  All calls share the one array: calls whose
+// kernels overlap on the GPU (other streams, other threads) race on it and
+// must be serialized by the caller.  The decode kernel writes every partial
+// the merge kernel later reads, so nothing has to be cleared between calls.
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/fo_attention.h"
+#include "fo_common.cuh"
+#include "fo_kernels.h"
+
+#define FO_STATIC_ROWS 8
+#define FO_STATIC_HEADS 16
+#define FO_STATIC_POSITIONS 16384
+#define FO_STATIC_SPLITS (FO_STATIC_POSITIONS / FO_SPLIT)
+#define FO_STATIC_O_FLOATS (FO_STATIC_ROWS * FO_STATIC_HEADS * FO_STATIC_SPLITS * FO_HD)
+#define FO_STATIC_ML_FLOATS (FO_STATIC_ROWS * FO_STATIC_HEADS * FO_STATIC_SPLITS * 2)
+
+// The decode partials: [rows][heads][splits][64] outputs, then
+// [rows][heads][splits][2] (max, denominator).
+static __device__ __align__(256) float g_decode_scratch[FO_STATIC_O_FLOATS + FO_STATIC_ML_FLOATS];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_once[kMaxDevices];
+float *g_scratch_ptr[kMaxDevices];
+cudaError_t g_scratch_err[kMaxDevices];
+
+thread_local char g_msg[256];
+
+}  // namespace
+
+// Defined in fo_abi.cu: records a message for fo_last_error().
+extern "C" int fo_internal_fail(int status, const char *msg);
+
+extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *scales, const void *tail_codes,
+                                             const uint16_t *tail_scales, int32_t format, int64_t prefix_len,
+                                             int64_t prefix_stride, int64_t tail_len, int64_t tail_stride,
+                                             int64_t n_heads, int64_t n_kv_heads, const float *q, int64_t rows,
+                                             const float *sinks, int32_t fast_exp, float *output, void *stream) {
+    if (!codes || !q || !sinks || !output || (tail_len > 0 && !tail_codes))
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: null pointer");
+    if ((format == FO_KV_Q8 || format == FO_KV_Q16) && (!scales || (tail_len > 0 && !tail_scales)))
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: coded records need their scales");
+    if (format < FO_KV_F32 || format > FO_KV_BF16)
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: unknown record format");
+    if (!(n_kv_heads >= 1 && n_heads == 2 * n_kv_heads))
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: heads must be paired GQA heads");
+    if (!(prefix_len >= 1 && tail_len >= 0 && prefix_stride >= prefix_len && tail_stride >= tail_len))
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: bad prefix/tail lengths or strides");
+    if (!(rows >= 1 && rows <= FO_STATIC_ROWS && rows <= (tail_len > 1 ? tail_len : 1)))
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: rows must be 1..8 and at most max(tail_len, 1)");
+    const int64_t last = prefix_len + tail_len;
+    if (n_heads > FO_STATIC_HEADS || last > FO_STATIC_POSITIONS) {
+        snprintf(g_msg, sizeof g_msg,
+                 "static-scratch decode: %lld heads and %lld positions exceed the static scratch limit "
+                 "(%d heads, %d positions)",
+                 (long long)n_heads, (long long)last, FO_STATIC_HEADS, FO_STATIC_POSITIONS);
+        return fo_internal_fail(FO_ERR_CAPACITY, g_msg);
+    }
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return fo_internal_fail(FO_ERR_CUDA, "static-scratch decode: no usable current device");
+    // Once per device, with that device current: the array's device address.
+    std::call_once(g_once[dev], [dev] {
+        void *p = nullptr;
+        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_decode_scratch);
+        g_scratch_ptr[dev] = static_cast<float *>(p);
+    });
+    if (g_scratch_err[dev] != cudaSuccess || !g_scratch_ptr[dev]) {
+        snprintf(g_msg, sizeof g_msg, "static-scratch decode: cudaGetSymbolAddress failed: %s",
+                 cudaGetErrorString(g_scratch_err[dev]));
+        return fo_internal_fail(FO_ERR_CUDA, g_msg);
+    }
+    fo_decode_page p{};
+    p.codes = codes;
+    p.scales = scales;
+    p.tail_codes = tail_codes;
+    p.tail_scales = tail_scales;
+    p.q = q;
+    p.sinks = sinks;
+    p.out = output;
+    p.part_o = g_scratch_ptr[dev];
+    p.part_ml = g_scratch_ptr[dev] + FO_STATIC_O_FLOATS;
+    p.prefix_len = prefix_len;
+    p.prefix_stride = prefix_stride;
+    p.tail_stride = tail_stride;
+    p.last = last;
+    p.rows = (int32_t)rows;
+    p.splits = (int32_t)((last + FO_SPLIT - 1) / FO_SPLIT);
+    e = fo_launch_decode_one(&p, format, n_kv_heads, fast_exp != 0, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        snprintf(g_msg, sizeof g_msg, "static-scratch decode launch: %s", cudaGetErrorString(e));
+        return fo_internal_fail(FO_ERR_CUDA, g_msg);
+    }
+    return FO_OK;
+}

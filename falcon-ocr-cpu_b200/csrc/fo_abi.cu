@@ -223,6 +223,9 @@ int timed_end(fo_ctx *ctx, bool on) {
 
 extern "C" {
 
+// Lets other translation units of the library report through fo_last_error().
+int fo_internal_fail(int status, const char *msg) { return fail(status, "%s", msg); }
+
 int fo_version(void) { return 100; }
 
 const char *fo_last_error(void) { return g_last_error.c_str(); }

@@ -92,7 +92,7 @@ EXPORTS = [
     "fo_attention", "fo_attention_prefill_bf16", "fo_convert_bf16", "fo_kv_seal", "fo_kv_destroy",
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
-    "fo_kv_attention_decode_batch",
+    "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -131,6 +131,7 @@ def lib() -> ctypes.CDLL:
         "fo_kv_attention_decode": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_rows": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_batch": (I, [PP, I64, PP, PP, PP]),
+        "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -338,3 +339,15 @@ def decode_batch(caches: Sequence[SplitPrefix], qs, sinks, outputs):
     check(lib().fo_kv_attention_decode_batch(arr([c.handle.value for c in caches]), n, arr([q.data_ptr() for q in qs]),
                                              arr([s.data_ptr() for s in sinks]),
                                              arr([o.data_ptr() for o in outputs])))
+
+
+def decode_rows_static_scratch(cache: SplitPrefix, fmt, q, rows, sinks, output, fast_exp=False, stream=None):
+    """fo_decode_rows_static_scratch over a sealed cache's records: the decode
+    for callers that cannot allocate device memory (q, sinks and output are
+    CUDA tensors; the partials live in the library's static array)."""
+    fmt = KV_FORMATS[fmt] if isinstance(fmt, str) else fmt
+    (codes, scales, tcodes, tscales), ps, ts = cache.records()
+    check(lib().fo_decode_rows_static_scratch(codes, scales, tcodes, tscales, fmt, cache.prefix_len, ps,
+                                              cache.tail_len, ts, cache.heads, cache.heads // 2, q.data_ptr(), rows,
+                                              sinks.data_ptr(), int(bool(fast_exp)), output.data_ptr(), stream))
+    return output

@@ -184,6 +184,24 @@ int fo_kv_attention_decode_rows(fo_kv_cache *cache, const float *q, int64_t rows
 int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const float *const *q,
                                  const float *const *sinks, float *const *output);
 
+/* Verify-row decode that allocates no device memory.  No counterpart in the
+ * reference.  For callers that cannot allocate while they decode: a serving
+ * runtime that owns all GPU memory through its own pool, or a decode loop
+ * that must avoid cudaMalloc/cudaFree because they can synchronize the whole
+ * device.  The caller passes the sealed records (as fo_kv_records describes
+ * them), device q [rows][n_heads][64], sinks and output, and a stream (NULL
+ * is the default stream); results equal fo_kv_attention_decode_rows'.  The
+ * split partials live in one static device array of about 2.1 MiB that every
+ * GPU loading the library holds until exit, which limits a call to 8 rows,
+ * 16 heads and 16,384 positions (FO_ERR_CAPACITY beyond).  The first call on
+ * a device looks the array up and should come before any stream capture;
+ * calls that overlap on the GPU share the array and race. */
+int fo_decode_rows_static_scratch(const void *codes, const uint16_t *scales, const void *tail_codes,
+                                  const uint16_t *tail_scales, int32_t format, int64_t prefix_len,
+                                  int64_t prefix_stride, int64_t tail_len, int64_t tail_stride, int64_t n_heads,
+                                  int64_t n_kv_heads, const float *q, int64_t rows, const float *sinks,
+                                  int32_t fast_exp, float *output, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
