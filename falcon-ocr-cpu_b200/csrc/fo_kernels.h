@@ -43,6 +43,7 @@ struct fo_decode_page {
     float *out;          // [rows][H][64]
     float *part_o;       // [rows][H][splits][64]
     float *part_ml;      // [rows][H][splits][2]
+    unsigned *counters;  // [groups] finished splits; zero between calls
     int64_t prefix_len, prefix_stride, tail_stride, last;  // last = prefix_len + tail_len
     int32_t rows, splits;                                   // splits = ceil(last / FO_SPLIT)
 };
@@ -50,7 +51,7 @@ struct fo_decode_page {
 // Positions per decode split: the GPU's position partition.  Fixed, so a
 // row's partition depends only on its own length (verify rows equal their
 // single-row decodes bit for bit).
-#define FO_SPLIT 256
+#define FO_SPLIT 512
 
 // One page (descriptor read on the host, passed by value).
 cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t groups, int fast_exp,

@@ -21,9 +21,12 @@
 //              signals every consumer; it also owns the TMEM allocation;
 //   warps 0-7  two softmax warpgroups, one per Q tile, one thread per query
 //              row: Q row to BF16 in shared memory, S row from TMEM
-//              (tcgen05.ld), mask, exp2, BF16 P row to shared memory, and
-//              the epilogue O / l * sink from TMEM.
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384).
+//              (tcgen05.ld), mask, exp2, BF16 P row back to TMEM (tcgen05.st),
+//              and the epilogue O / l * sink from TMEM.
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384) P0 [384,448)
+// P1 [448,512).  P_t holds the BF16 probabilities (two per 32-bit column) and
+// is the PV MMA's A operand straight from TMEM, so PV reads only V from
+// shared memory.
 // Every wait is bounded (sm100.cuh); on a timeout the CTA unwinds, waits for
 // its own copies and MMAs, frees TMEM and reports through the error word.
 #include <cudaTypedefs.h>
@@ -35,14 +38,13 @@
 namespace fo {
 using namespace sm100;
 
-constexpr int BT_STAGES = 2;
+constexpr int BT_STAGES = 4;
 constexpr int BT_THREADS = 320;
 constexpr uint32_t BT_TILE = 128 * 128;  // one [128][64] BF16 tile, bytes
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_K = 2 * BT_TILE;
 constexpr uint32_t OFF_V = OFF_K + BT_STAGES * BT_TILE;
-constexpr uint32_t OFF_P = OFF_V + BT_STAGES * BT_TILE;
-constexpr uint32_t OFF_BAR = OFF_P + 4 * BT_TILE;
+constexpr uint32_t OFF_BAR = OFF_V + BT_STAGES * BT_TILE;
 // barriers: q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS],
 // s_full[2], s_empty[2], p_full[2], p_empty[2], mma_done
 constexpr int NBAR = 1 + 4 * BT_STAGES + 8 + 1;
@@ -115,8 +117,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K), sV = smem_u32(smem + OFF_V),
-                   sP = smem_u32(smem + OFF_P);
+    const uint32_t sQ = smem_u32(smem + OFF_Q), sK = smem_u32(smem + OFF_K), sV = smem_u32(smem + OFF_V);
 
     if (warp < 8) {
         // ------------------------------------------------ softmax warpgroups
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         const uint32_t lane_base = (uint32_t)(32 * wq) << 16;
         const uint32_t s_tm = tmem + lane_base + 128 * t;
         const uint32_t o_tm = tmem + lane_base + 256 + 64 * t;
-        const uint32_t p_row = sP + t * 2 * BT_TILE + r * 128;
+        const uint32_t p_tm = tmem + lane_base + 384 + 64 * t;
         const float C = 0.125f * 1.44269504088896340736f;  // scale * log2(e)
         float l = 0.0f, m2 = -INFINITY;
         bool ok = true;
@@ -178,6 +179,34 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                 shift = m2 == -INFINITY ? 0.0f : m2;
                 l *= factor;
             }
+            // The probabilities first, packed to BF16 pairs in registers, so
+            // this overlaps PV_t(j-1), which still reads the P tile.
+            // Whole tile visible for every row of the warp: no per-key mask.
+            const bool full = __all_sync(0xffffffffu, nvis >= 128);
+            float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            uint32_t pk[64];
+#pragma unroll
+            for (int i = 0; i < 64; i++) {
+                const int c = 2 * i;
+                float x0, x1;
+                const float t0 = STATIC ? __uint_as_float(s[c]) * C : __uint_as_float(s[c]) * C - shift;
+                const float t1 = STATIC ? __uint_as_float(s[c + 1]) * C : __uint_as_float(s[c + 1]) * C - shift;
+                x0 = ex2(t0);
+                x1 = ex2(t1);
+                if (!full) {
+                    x0 = c < nvis ? x0 : 0.0f;
+                    x1 = c + 1 < nvis ? x1 : 0.0f;
+                }
+                pk[i] = pack_bf16(x0, x1);
+                if constexpr (STATIC) {  // the static shift sums the rounded probabilities PV multiplies
+                    lsum[i & 3] += __uint_as_float(pk[i] << 16);
+                    lsum[i & 3] += __uint_as_float(pk[i] & 0xFFFF0000u);
+                } else {  // the online softmax sums the unrounded probabilities
+                    lsum[i & 3] += x0;
+                    lsum[i & 3] += x1;
+                }
+            }
+            l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
             // P_t is free once PV_t(j-1) has completed.
             if (j > 0) {
                 ok = __all_sync(0xffffffffu, mbar_wait(p_empty + t, (j - 1) & 1, abort_flag, a.err));
@@ -199,33 +228,10 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                     tmem_wait_st();
                 }
             }
-#pragma unroll
-            for (int cc = 0; cc < 16; cc++) {  // 16 chunks of 8 keys
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int c = 8 * cc + 2 * e;
-                    float x0, x1;
-                    if constexpr (STATIC) {
-                        x0 = c < nvis ? ex2(__uint_as_float(s[c]) * C) : 0.0f;
-                        x1 = c + 1 < nvis ? ex2(__uint_as_float(s[c + 1]) * C) : 0.0f;
-                    } else {
-                        x0 = c < nvis ? ex2(__uint_as_float(s[c]) * C - shift) : 0.0f;
-                        x1 = c + 1 < nvis ? ex2(__uint_as_float(s[c + 1]) * C - shift) : 0.0f;
-                    }
-                    w[e] = pack_bf16(x0, x1);
-                    if constexpr (STATIC) {  // sum the rounded probabilities PV multiplies
-                        l += __uint_as_float(w[e] << 16);
-                        l += __uint_as_float(w[e] & 0xFFFF0000u);
-                    } else {  // sum the unrounded probabilities
-                        l += x0;
-                        l += x1;
-                    }
-                }
-                const int b = cc >> 3, ch = cc & 7;
-                st_shared_v4(p_row + b * BT_TILE + ((ch ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
-            }
-            fence_proxy_async_smem();
+            // P_t row r (keys 2i, 2i+1 in the low, high half of column i).
+            FO_TMEM_ST32(p_tm, (pk + 0));
+            FO_TMEM_ST32(p_tm + 32, (pk + 32));
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_full + t);
         }
@@ -283,18 +289,25 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         // ------------------------------------------------------- MMA issuer
         if (lane == 0) {
             const uint32_t idS = idesc_bf16(128, 128, 0), idPV = idesc_bf16(128, 64, 1);
+            // Descriptors are built once; a K step or stage only moves the
+            // start-address field (16-byte units, no carry below 256 KB).
+            const uint64_t dQ = sdesc_sw128(sQ, 16, 1024), dK = sdesc_sw128(sK, 16, 1024);
+            const uint64_t dV = sdesc_sw128(sV, BT_TILE, 1024);
+            constexpr uint32_t TILE16 = BT_TILE >> 4;
             auto issue_s = [&](int t, int st) {
+                const uint64_t a = dQ + t * TILE16, b = dK + st * TILE16;
+                const uint32_t d = tmem + 128 * t;
+                mma_bf16(d, a, b, idS, 0);
 #pragma unroll
-                for (int kk = 0; kk < 4; kk++)
-                    mma_bf16(tmem + 128 * t, sdesc_sw128(sQ + t * BT_TILE + 32 * kk, 16, 1024),
-                             sdesc_sw128(sK + st * BT_TILE + 32 * kk, 16, 1024), idS, kk > 0);
+                for (int kk = 1; kk < 4; kk++) mma_bf16(d, a + 2 * kk, b + 2 * kk, idS, 1);
             };
             auto issue_pv = [&](int t, int st, int j) {
+                const uint32_t a = tmem + 384 + 64 * t;  // P_t: 8 columns per 16 keys
+                const uint64_t b = dV + st * TILE16;
+                const uint32_t d = tmem + 256 + 64 * t;
+                mma_bf16_ts(d, a, b, idPV, j > 0);
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++)
-                    mma_bf16(tmem + 256 + 64 * t,
-                             sdesc_sw128(sP + t * 2 * BT_TILE + (kk >> 2) * BT_TILE + (kk & 3) * 32, 16, 1024),
-                             sdesc_sw128(sV + st * BT_TILE + kk * 2048, BT_TILE, 1024), idPV, (j > 0 || kk > 0));
+                for (int kk = 1; kk < 8; kk++) mma_bf16_ts(d, a + 8 * kk, b + kk * (2048 >> 4), idPV, 1);
             };
             bool ok = mbar_wait(q_full, 0, abort_flag, a.err) && mbar_wait(k_full, 0, abort_flag, a.err);
             if (ok) {
