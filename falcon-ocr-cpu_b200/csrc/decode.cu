@@ -3,347 +3,759 @@
 // src/quant/kv.rs:565-972; per-group kernels pair / pair_rows,
 // src/quant/kv/decode.rs:305-677; merge, src/quant/kv.rs:775-813).
 //
-// Grid (split, group, page).  A CTA covers FO_SPLIT positions of one KV
-// group and serves both heads of the group and every verification row, as the
-// reference's pair_rows does: each record is loaded and dequantized once
-// (fl(code * scale), decode.rs:151-187) and every row runs over it.  Each of
-// its eight warps streams its own 32-key chunks with no block-wide barrier
-// (lane = key for the loads and logits, lane = two output dimensions for PV)
-// and keeps the reference's online state per row and head (chunk max,
-// rescale before PV, exp(s - max)).  The warps then combine, in warp order,
-// into the split's unnormalized partial.  The last CTA of a group to finish
-// (an atomic counter per group, no waiting) merges the splits of every row in
-// position order with the reference's merge arithmetic and applies the sink;
-// it resets the counter for the next call.  Rows only see their own positions
-// (row r: prefix + tail - rows + 1 + r, kv.rs:851-855) and split boundaries
-// are absolute, so every verification row equals its single-row decode bit
-// for bit.
+// Work items are (page, split, group): FO_SPLIT positions of one KV group,
+// for both heads of the group and every verification row, as the reference's
+// pair_rows serves them (each record is read once and every row runs over
+// it).  Persistent CTAs walk the items.  A split is cut into chunks of 64
+// keys (32 for FP32 records); one warp bulk-copies (cp.async.bulk, one
+// mbarrier per chunk) a chunk's records into shared memory, one padded slot
+// per key laid out [T 32 | S0 32 | S1 32 | V 64] (a tail record's key fills
+// both spatial halves), and two warps compute on it, one per head of the
+// pair: logits with lane = key, the reference's online softmax per row over
+// the chunk (chunk max, rescale, exp(s - max)), and O += P V with lane = two
+// output dimensions, dequantizing exactly as the reference (fl(code * scale),
+// decode.rs:151-187).  Products are accumulated with the packed FP32 FMA
+// (each half an ordinary fmaf).  Once both warps are done with a chunk, the
+// copies for the CTA's next item are issued into its slots, overlapping the
+// combine and merges.  The chunks combine, in chunk order, into the split's
+// unnormalized partial; a merge kernel, launched as a programmatic dependent,
+// combines the splits in order and applies the sink.  Rows only see their own
+// positions (row r: prefix + tail - rows + 1 + r, kv.rs:851-855) and every
+// boundary and order is absolute, so each verification row equals its
+// single-row decode bit for bit.
 #include "fo_common.cuh"
 #include "fo_kernels.h"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
 
 namespace fo {
 
-constexpr int DEC_WARPS = 8;
-constexpr int DEC_THREADS = 32 * DEC_WARPS;
-constexpr int CHUNK = 32;                                        // keys per warp step (one per lane)
-constexpr int CHUNKS_PER_WARP = FO_SPLIT / (CHUNK * DEC_WARPS);  // a split is DEC_WARPS x this many chunks
-constexpr int V_LD = FO_HD + 4;                                  // padded value row (floats)
-// Dynamic shared memory: q [8][2][64], per-warp values [32][V_LD] (reused for
-// the warps' outputs [2 * 8][64]), per-warp probabilities [16][32], per-warp
-// max and sum [16] each.
-constexpr int SM_Q = FO_MAX_ROWS * 2 * FO_HD;
-constexpr int SM_V = DEC_WARPS * CHUNK * V_LD;
-constexpr int SM_P = DEC_WARPS * 2 * FO_MAX_ROWS * CHUNK;
-constexpr int SM_ML = DEC_WARPS * 2 * FO_MAX_ROWS;
-constexpr size_t DEC_SMEM = sizeof(float) * (SM_Q + SM_V + SM_P + 2 * SM_ML) + 16;
-static_assert(DEC_WARPS * 2 * FO_MAX_ROWS * FO_HD <= SM_V, "warp outputs fit the value buffers");
-
 enum { DF32 = 0, DQ16 = 1, DQ8 = 2, DBF16 = 3 };
 
-// 32 consecutive decoded values of a record block starting at element `e`
-// (a multiple of 32): fl(code * bf16 scale) for coded formats.
+// Per-format shape of a CTA: NPAIR pairs of warps; a pair owns whole items
+// and streams their 32-key chunks through two slot buffers; warp 2p + h of
+// pair p computes head h of the item's KV group.
 template <int F>
-__device__ __forceinline__ void load_block(const void *codes, const uint16_t *scales, int64_t e, float *out) {
+struct Shape {
+    static constexpr int E = F == DF32 ? 4 : (F == DQ8 ? 1 : 2);  // bytes per element
+    static constexpr bool CODED = F == DQ16 || F == DQ8;
+    static constexpr int CK = 32;                // keys per chunk (one per lane)
+    static constexpr int KPL = 1;                // keys per lane
+    static constexpr int NCH = FO_SPLIT / CK;    // chunks per item
+    static constexpr int NPAIR = 4;
+    static constexpr int NBUF = 2;               // slot buffers per pair
+    static constexpr int NW = 2 * NPAIR;
+    static constexpr int THREADS = 32 * NW;
+    static constexpr int MIN_CTAS = F == DF32 ? 1 : 2;
+    // Padded slot: 16 bytes past the record, so consecutive keys start on
+    // different banks (slot stride 4, 20 or 12 mod 32 words).
+    static constexpr int SLOT = FO_RECORD * E + 16;
+    static_assert(NCH >= NBUF, "an item spans both buffers");
+};
+
+// Shared-memory layout of one instantiation (bytes).
+template <int F, int R>
+struct Smem {
+    using S = Shape<F>;
+    static constexpr int BUFS = S::NPAIR * S::NBUF;
+    static constexpr int RECS = BUFS * S::CK * S::SLOT;                 // record slots per buffer
+    static constexpr int SCL = S::CODED ? BUFS * S::CK * 5 * 4 : 0;    // decoded scales [key][T, S0, S1, V0, V1]
+    static constexpr int Q = S::NW * R * FO_HD * 4;                     // per-warp q of its head [R][64]
+    static constexpr int P = S::NW * R * S::CK * 4;                     // per-warp probabilities [R][CK]
+    static constexpr int OFF_SCL = RECS;
+    static constexpr int OFF_Q = OFF_SCL + SCL;
+    static constexpr int OFF_P = OFF_Q + Q;
+    static constexpr int OFF_BAR = (OFF_P + P + 7) / 8 * 8;
+    static constexpr int OFF_FLAGS = OFF_BAR + BUFS * 8;
+    static constexpr int BYTES = OFF_FLAGS + 16;
+    static_assert(BYTES <= 227 * 1024, "shared memory per CTA");
+};
+
+// Two consecutive decoded values of a staged slot at element `e` (even).
+template <int F>
+__device__ __forceinline__ float2 slot_pair(const unsigned char *slot, int e, float scale) {
     if constexpr (F == DF32) {
-        const float4 *p = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(codes) + e);
+        return *reinterpret_cast<const float2 *>(slot + 4 * e);
+    } else if constexpr (F == DBF16) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(slot + 2 * e);
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    } else if constexpr (F == DQ16) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(slot + 2 * e);
+        return make_float2(__fmul_rn((float)(int16_t)(w & 0xFFFFu), scale), __fmul_rn((float)(int16_t)(w >> 16), scale));
+    } else {
+        const uint32_t w = *reinterpret_cast<const uint16_t *>(slot + e);
+        return make_float2(__fmul_rn((float)(int8_t)(w & 0xFFu), scale), __fmul_rn((float)(int8_t)(w >> 8), scale));
+    }
+}
+
+// 16 consecutive decoded values of a staged slot at element `e` (a multiple
+// of 16, inside one 32-element scale block).
+template <int F>
+__device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, float scale, float *out) {
+    if constexpr (F == DF32) {
+        const float4 *p = reinterpret_cast<const float4 *>(slot + 4 * e);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const float4 x = __ldg(p + i);
+        for (int i = 0; i < 4; i++) {
+            const float4 x = p[i];
             out[4 * i] = x.x;
             out[4 * i + 1] = x.y;
             out[4 * i + 2] = x.z;
             out[4 * i + 3] = x.w;
         }
-    } else if constexpr (F == DBF16) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(codes) + e);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint4 x = __ldg(p + i);
-            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                out[8 * i + 2 * c] = __uint_as_float(w[c] << 16);
-                out[8 * i + 2 * c + 1] = __uint_as_float(w[c] & 0xFFFF0000u);
-            }
-        }
-    } else if constexpr (F == DQ16) {
-        const float s = bf16_f32(__ldg(scales + e / 32));
-        const uint4 *p = reinterpret_cast<const uint4 *>(reinterpret_cast<const int16_t *>(codes) + e);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint4 x = __ldg(p + i);
-            const uint32_t w[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                out[8 * i + 2 * c] = __fmul_rn((float)(int16_t)(w[c] & 0xFFFFu), s);
-                out[8 * i + 2 * c + 1] = __fmul_rn((float)(int16_t)(w[c] >> 16), s);
-            }
-        }
-    } else {  // DQ8
-        const float s = bf16_f32(__ldg(scales + e / 32));
-        const uint4 *p = reinterpret_cast<const uint4 *>(reinterpret_cast<const int8_t *>(codes) + e);
+    } else if constexpr (F == DBF16 || F == DQ16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(slot + 2 * e);
 #pragma unroll
         for (int i = 0; i < 2; i++) {
-            const uint4 x = __ldg(p + i);
+            const uint4 x = p[i];
             const uint32_t w[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-            for (int c = 0; c < 4; c++)
-#pragma unroll
-                for (int b = 0; b < 4; b++)
-                    out[16 * i + 4 * c + b] = __fmul_rn((float)(int8_t)((w[c] >> (8 * b)) & 0xFFu), s);
+            for (int c = 0; c < 4; c++) {
+                if constexpr (F == DBF16) {
+                    out[8 * i + 2 * c] = __uint_as_float(w[c] << 16);
+                    out[8 * i + 2 * c + 1] = __uint_as_float(w[c] & 0xFFFF0000u);
+                } else {
+                    out[8 * i + 2 * c] = __fmul_rn((float)(int16_t)(w[c] & 0xFFFFu), scale);
+                    out[8 * i + 2 * c + 1] = __fmul_rn((float)(int16_t)(w[c] >> 16), scale);
+                }
+            }
         }
+    } else {
+        const uint4 x = *reinterpret_cast<const uint4 *>(slot + e);
+        const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) out[4 * c + b] = __fmul_rn((float)(int8_t)((w[c] >> (8 * b)) & 0xFFu), scale);
     }
 }
 
-template <int F, bool FAST, int R>
-__global__ void __launch_bounds__(DEC_THREADS, 2) decode_kernel(fo_decode_page page0, const fo_decode_page *pages,
-                                                                int64_t groups) {
-    extern __shared__ __align__(16) float dsm[];
-    float(*q_s)[2][FO_HD] = reinterpret_cast<float(*)[2][FO_HD]>(dsm);
-    float *v_base = dsm + SM_Q;
-    float *p_base = v_base + SM_V;
-    float *m_base = p_base + SM_P;
-    float *l_base = m_base + SM_ML;
-    int *last_flag = reinterpret_cast<int *>(l_base + SM_ML);
+// The values at dimensions e, e + 1 (e even) of two staged keys a and b, as
+// (a[e], b[e]) and (a[e + 1], b[e + 1]): operands of the packed FMA whose two
+// halves accumulate even and odd keys.
+template <int F>
+__device__ __forceinline__ void slot_vpair2(const unsigned char *sa, const unsigned char *sb, int e, float ca, float cb,
+                                            float2 &lo, float2 &hi) {
+    if constexpr (F == DF32) {
+        lo = make_float2(*reinterpret_cast<const float *>(sa + 4 * e), *reinterpret_cast<const float *>(sb + 4 * e));
+        hi = make_float2(*reinterpret_cast<const float *>(sa + 4 * e + 4),
+                         *reinterpret_cast<const float *>(sb + 4 * e + 4));
+    } else if constexpr (F == DBF16) {
+        const uint32_t wa = *reinterpret_cast<const uint32_t *>(sa + 2 * e);
+        const uint32_t wb = *reinterpret_cast<const uint32_t *>(sb + 2 * e);
+        lo = make_float2(__uint_as_float(wa << 16), __uint_as_float(wb << 16));
+        hi = make_float2(__uint_as_float(wa & 0xFFFF0000u), __uint_as_float(wb & 0xFFFF0000u));
+    } else if constexpr (F == DQ16) {
+        const uint32_t wa = *reinterpret_cast<const uint32_t *>(sa + 2 * e);
+        const uint32_t wb = *reinterpret_cast<const uint32_t *>(sb + 2 * e);
+        lo = make_float2(__fmul_rn((float)(int16_t)(wa & 0xFFFFu), ca), __fmul_rn((float)(int16_t)(wb & 0xFFFFu), cb));
+        hi = make_float2(__fmul_rn((float)(int16_t)(wa >> 16), ca), __fmul_rn((float)(int16_t)(wb >> 16), cb));
+    } else {
+        const uint32_t wa = *reinterpret_cast<const uint16_t *>(sa + e);
+        const uint32_t wb = *reinterpret_cast<const uint16_t *>(sb + e);
+        lo = make_float2(__fmul_rn((float)(int8_t)(wa & 0xFFu), ca), __fmul_rn((float)(int8_t)(wb & 0xFFu), cb));
+        hi = make_float2(__fmul_rn((float)(int8_t)(wa >> 8), ca), __fmul_rn((float)(int8_t)(wb >> 8), cb));
+    }
+}
 
-    const fo_decode_page pg = pages ? pages[blockIdx.z] : page0;
-    const int s = blockIdx.x;
-    if (s >= pg.splits) return;
-    const int64_t g = blockIdx.y;
-    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int64_t H = 2 * groups;
-    const int64_t p0 = (int64_t)s * FO_SPLIT;
-    const int64_t p_end = min64(p0 + FO_SPLIT, pg.last);
+// Stages one key's record into its slot: a prefix record as it is, a tail
+// record [K 64 | V 64] as [K | K[32:64] | V].  Returns the bytes copied.
+// Coded formats: the key's scales, decoded, in slot order [T, S0, S1, V0, V1].
+template <int F>
+__device__ __forceinline__ uint32_t stage_key(const fo_decode_page &pg, int64_t g, int64_t pos, unsigned char *slot,
+                                              float *scl, uint64_t *bar) {
+    constexpr int E = Shape<F>::E;
+    if (pos < pg.prefix_len) {
+        const int64_t r = g * pg.prefix_stride + pos;
+        sm100::bulk_g2s(slot, reinterpret_cast<const unsigned char *>(pg.codes) + r * FO_RECORD * E, FO_RECORD * E, bar);
+        if constexpr (Shape<F>::CODED) {
+            const uint16_t *s = pg.scales + r * 5;
+#pragma unroll
+            for (int i = 0; i < 5; i++) scl[i] = bf16_f32(__ldg(s + i));
+        }
+    } else {
+        const int64_t r = g * pg.tail_stride + (pos - pg.prefix_len);
+        const unsigned char *rec = reinterpret_cast<const unsigned char *>(pg.tail_codes) + r * FO_TAIL_RECORD * E;
+        sm100::bulk_g2s(slot, rec, 64 * E, bar);
+        sm100::bulk_g2s(slot + 64 * E, rec + 32 * E, 32 * E, bar);
+        sm100::bulk_g2s(slot + 96 * E, rec + 64 * E, 64 * E, bar);
+        if constexpr (Shape<F>::CODED) {
+            const uint16_t *s = pg.tail_scales + r * 4;
+            const float kt = bf16_f32(__ldg(s)), ks = bf16_f32(__ldg(s + 1));
+            scl[0] = kt;
+            scl[1] = ks;
+            scl[2] = ks;
+            scl[3] = bf16_f32(__ldg(s + 2));
+            scl[4] = bf16_f32(__ldg(s + 3));
+        }
+    }
+    return FO_RECORD * E;
+}
 
-    for (int i = t; i < R * 2 * FO_HD; i += DEC_THREADS) {
-        const int r = i / (2 * FO_HD), h = (i / FO_HD) & 1, d = i % FO_HD;
-        q_s[r][h][d] = pg.q[(r * H + 2 * g + h) * FO_HD + d];
+// Bulk L2 prefetch of [addr, addr + bytes), trimmed inward to 16-byte
+// boundaries (the prefetch's alignment rule); never reaches outside the range.
+__device__ __forceinline__ void prefetch_l2(const void *addr, int64_t bytes) {
+    const uint64_t a = reinterpret_cast<uint64_t>(addr);
+    const uint64_t lo = (a + 15) & ~15ull, hi = (a + (uint64_t)bytes) & ~15ull;
+    if (hi > lo)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo)) : "memory");
+}
+
+// Asks L2 for every record (and scale) of split s of group g, so that a
+// later item's copies find their lines already on chip.
+template <int F>
+__device__ __forceinline__ void prefetch_item(const fo_decode_page &pg, int64_t g, int s) {
+    using S = Shape<F>;
+    const int64_t a = (int64_t)s * FO_SPLIT, b = min64(a + FO_SPLIT, pg.last);
+    const int64_t pa = a, pb = min64(b, pg.prefix_len);
+    if (pb > pa) {
+        const int64_t r0 = g * pg.prefix_stride + pa;
+        prefetch_l2(reinterpret_cast<const char *>(pg.codes) + r0 * FO_RECORD * S::E, (pb - pa) * FO_RECORD * S::E);
+        if (S::CODED) prefetch_l2(pg.scales + r0 * 5, (pb - pa) * 10);
     }
-    // Per (row, head): the online state (warp-uniform, in shared memory) and
-    // this lane's two output dimensions 2*lane, 2*lane + 1 (registers).
-    float *mr = m_base + warp * 2 * FO_MAX_ROWS, *lr = l_base + warp * 2 * FO_MAX_ROWS;
-    if (lane < 2 * R) {
-        mr[lane] = -INFINITY;
-        lr[lane] = 0.0f;
+    const int64_t ta = max64(a, pg.prefix_len), tb = b;
+    if (tb > ta) {
+        const int64_t r0 = g * pg.tail_stride + (ta - pg.prefix_len);
+        prefetch_l2(reinterpret_cast<const char *>(pg.tail_codes) + r0 * FO_TAIL_RECORD * S::E,
+                    (tb - ta) * FO_TAIL_RECORD * S::E);
+        if (S::CODED) prefetch_l2(pg.tail_scales + r0 * 4, (tb - ta) * 8);
     }
-    __syncthreads();
-    float o0[2 * R], o1[2 * R];
+}
+
+// Stages the records of chunk c of split s of group g (the issuing warp's
+// lanes each arrive once on the chunk's barrier) and returns this lane's
+// decoded scales.  A chunk of prefix records only is one TMA tile load
+// through the page's tensor map (rows padded to the slot by the box's
+// out-of-bounds fill); a chunk that reaches the tail copies record by record.
+template <int F>
+__device__ __forceinline__ void stage_chunk(const fo_decode_page &pg, int64_t g, int s, int c, int lane,
+                                            unsigned char *crec, uint64_t *bar, float (*sc)[5]) {
+    using S = Shape<F>;
+    const int64_t k0 = (int64_t)s * FO_SPLIT + (int64_t)c * S::CK;
+    const int64_t w1 = min64(k0 + S::CK, min64((int64_t)s * FO_SPLIT + FO_SPLIT, pg.last));
+    const int nk = (int)max64(0, w1 - k0);
+    if (pg.has_map && nk > 0 && w1 <= pg.prefix_len) {
+        const uint32_t bytes = lane == 0 ? (uint32_t)(S::CK * S::SLOT) : 0u;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
+                     : "memory");
+        if (lane == 0) sm100::tma_load_3d(crec, &pg.rec_map, bar, 0, (int)k0, (int)g);
+        if constexpr (S::CODED) {
 #pragma unroll
-    for (int rh = 0; rh < 2 * R; rh++) {
-        o0[rh] = 0.0f;
-        o1[rh] = 0.0f;
-    }
-    float(*vw)[V_LD] = reinterpret_cast<float(*)[V_LD]>(v_base + warp * CHUNK * V_LD);
-    float(*pw)[CHUNK] = reinterpret_cast<float(*)[CHUNK]>(p_base + warp * 2 * FO_MAX_ROWS * CHUNK);
-    for (int c = 0; c < CHUNKS_PER_WARP; c++) {
-        const int64_t k0 = p0 + (int64_t)(warp * CHUNKS_PER_WARP + c) * CHUNK;
-        if (k0 >= p_end) break;  // warp-uniform
-        const int64_t pos = k0 + lane;
-        const bool live = pos < p_end;
-        const bool prefix = pos < pg.prefix_len;
-        const int64_t rec = prefix ? (g * pg.prefix_stride + pos) * FO_RECORD
-                                   : (g * pg.tail_stride + (pos - pg.prefix_len)) * FO_TAIL_RECORD;
-        const void *codes = prefix ? pg.codes : pg.tail_codes;
-        const uint16_t *scales = prefix ? pg.scales : pg.tail_scales;
-        // This lane's value row, dequantized once for every row and head.
-        {
-            float vals[32];
+            for (int j = 0; j < S::KPL; j++) {
+                const int key = lane + 32 * j;
+                if (key < nk) {
+                    const uint16_t *p = pg.scales + (g * pg.prefix_stride + k0 + key) * 5;
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                if (live)
-                    load_block<F>(codes, scales, rec + (prefix ? 96 : 64) + 32 * half, vals);
-                else
-#pragma unroll
-                    for (int i = 0; i < 32; i++) vals[i] = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 8; i++)
-                    *reinterpret_cast<float4 *>(&vw[lane][32 * half + 4 * i]) =
-                        make_float4(vals[4 * i], vals[4 * i + 1], vals[4 * i + 2], vals[4 * i + 3]);
+                    for (int i = 0; i < 5; i++) sc[j][i] = bf16_f32(__ldg(p + i));
+                }
             }
         }
-        // Logits of every (row, head): the shared temporal half once for both
-        // heads, then each head's spatial half (a tail record has one key for
-        // both heads).
-        float lg[2 * R];
-        {
-            float key[32];
-            if (live)
-                load_block<F>(codes, scales, rec, key);
-            else
+        return;
+    }
+    uint32_t bytes = 0;
 #pragma unroll
-                for (int i = 0; i < 32; i++) key[i] = 0.0f;
+    for (int j = 0; j < S::KPL; j++)
+        if (lane + 32 * j < nk) bytes += FO_RECORD * S::E;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
+                 : "memory");
 #pragma unroll
-            for (int rh = 0; rh < 2 * R; rh++) {
-                const float *qv = q_s[rh >> 1][rh & 1];
-                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+    for (int j = 0; j < S::KPL; j++) {
+        const int key = lane + 32 * j;
+        if (key < nk) stage_key<F>(pg, g, k0 + key, crec + key * S::SLOT, sc[j], bar);
+    }
+}
+
+// Waits on a pair's named barrier (id 1 + pair, 64 threads) and returns
+// whether `ok` holds in both warps.
+__device__ __forceinline__ bool pair_sync_and(int pair, bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.and.pred q, %2, 64, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)ok), "r"(1 + pair)
+        : "memory");
+    return r != 0;
+}
+
+// Persistent CTAs: every pair of warps walks the work items (page, split,
+// group) with a stride of all pairs of the grid.
+template <int F, bool FAST, int R>
+__global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
+    decode_kernel(const __grid_constant__ fo_decode_page page0, const fo_decode_page *pages, int64_t n_pages,
+                  int64_t groups, int max_splits) {
+    using S = Shape<F>;
+    using L = Smem<F, R>;
+    constexpr int CK = S::CK, NCH = S::NCH, NPAIR = S::NPAIR;
+    extern __shared__ __align__(128) unsigned char dsm[];
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int pair = warp >> 1, hd = warp & 1;
+    const bool stager = hd == 0;  // the head-0 warp stages the pair's chunks
+    uint64_t *bars = reinterpret_cast<uint64_t *>(dsm + L::OFF_BAR);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(dsm + L::OFF_FLAGS);
+    // Buffer b of this pair: slots and decoded scales.
+    auto brec = [&](int b) { return dsm + (size_t)(pair * S::NBUF + b) * CK * S::SLOT; };
+    auto bscl = [&](int b) { return reinterpret_cast<float *>(dsm + L::OFF_SCL) + (pair * S::NBUF + b) * CK * 5; };
+    uint64_t *pbar = bars + pair * S::NBUF;
+    float(*qw)[FO_HD] = reinterpret_cast<float(*)[FO_HD]>(dsm + L::OFF_Q) + warp * R;
+    float(*pw)[CK] = reinterpret_cast<float(*)[CK]>(dsm + L::OFF_P) + warp * R;
+    const int64_t H = 2 * groups;
+    const int64_t n_items = n_pages * max_splits * groups;
+    const int64_t n_pairs = (int64_t)gridDim.x * NPAIR;
+
+    if (t < NPAIR * S::NBUF) sm100::mbar_init(&bars[t], 32);
+    if (t == 0) *abort_flag = 0;
+    __syncthreads();
+    // The merge kernel may launch now; it waits for this grid to finish.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    struct Item {
+        const fo_decode_page *pp;  // the page (kernel parameter or device array; read in place)
+        int s;
+        int64_t g;
+        int64_t it;
+    };
+    // The next valid item at or after it (splits past a page's own count
+    // are skipped).
+    auto find = [&](Item &x, int64_t it) -> bool {
+        for (; it < n_items; it += n_pairs) {
+            x.g = it % groups;
+            const int64_t rest = it / groups;
+            x.s = (int)(rest % max_splits);
+            x.pp = pages ? pages + rest / max_splits : &page0;
+            x.it = it;
+            if (x.s < x.pp->splits) return true;
+        }
+        return false;
+    };
+    // This warp's head rows of the item's queries: dims 2 lane, 2 lane + 1.
+    auto load_q = [&](const Item &x, float2 *qv) {
 #pragma unroll
-                for (int d = 0; d < 32; d += 4) {
-                    const float4 x = *reinterpret_cast<const float4 *>(qv + d);
-                    d0 = fmaf(x.x, key[d], d0);
-                    d1 = fmaf(x.y, key[d + 1], d1);
-                    d2 = fmaf(x.z, key[d + 2], d2);
-                    d3 = fmaf(x.w, key[d + 3], d3);
-                }
-                lg[rh] = (d0 + d1) + (d2 + d3);
+        for (int r = 0; r < R; r++)
+            qv[r] = __ldg(reinterpret_cast<const float2 *>(x.pp->q + (r * H + 2 * x.g + hd) * FO_HD) + lane);
+    };
+
+    Item cur, nxt;
+    // Pair ids run across the CTAs first, so that items spread over every SM.
+    bool have = find(cur, (int64_t)pair * gridDim.x + blockIdx.x);
+    bool have_n = have && find(nxt, cur.it + n_pairs);
+    float2 qv[R];
+    float sc_next[1][5], sc_new[1][5];  // scales of chunk u + 1 (staged, unpublished) and of a new stage
+    if (have) {
+        load_q(cur, qv);  // ahead of the bulk copies in the memory queues
+        if (stager) {
+            stage_chunk<F>(*cur.pp, cur.g, cur.s, 0, lane, brec(0), &pbar[0], sc_new);
+            stage_chunk<F>(*cur.pp, cur.g, cur.s, 1, lane, brec(1), &pbar[1], sc_next);
+            if constexpr (S::CODED) {
+                if (lane < min64(CK, cur.pp->last - (int64_t)cur.s * FO_SPLIT))
+#pragma unroll
+                    for (int i = 0; i < 5; i++) bscl(0)[lane * 5 + i] = sc_new[0][i];
             }
+        }
+    }
+    pair_sync_and(pair, true);  // chunk 0's scales are visible
+    uint32_t u = 0;             // chunks consumed by this pair
+    bool prefetched = false;
+    bool ok = true;
+    while (have && ok) {
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                if (live) load_block<F>(codes, scales, rec + (prefix ? 32 + 32 * h : 32), key);
+        for (int r = 0; r < R; r++) *reinterpret_cast<float2 *>(&qw[r][2 * lane]) = qv[r];
+        __syncwarp();
+        const fo_decode_page &pg = *cur.pp;
+        const int64_t p0 = (int64_t)cur.s * FO_SPLIT;
+        const int64_t p_end = min64(p0 + FO_SPLIT, pg.last);
+        // Row r sees positions [0, last - R + 1 + r) (kv.rs:851-855).
+        const int64_t len0 = pg.last - R + 1;
+        // Per row: the running max (warp-uniform), this lane's share of the
+        // denominator, and this lane's output dimensions 2*lane (oa) and
+        // 2*lane + 1 (ob), each as an (even keys, odd keys) pair of sums.
+        float m_st[R], l_st[R];
+        float2 oa[R], ob[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            m_st[r] = -INFINITY;
+            l_st[r] = 0.0f;
+            oa[r] = make_float2(0.0f, 0.0f);
+            ob[r] = make_float2(0.0f, 0.0f);
+        }
+        for (int c = 0; c < NCH && ok; c++, u++) {
+            const int b = u & 1;
+            const int64_t k0 = p0 + (int64_t)c * CK;
+            const int64_t w1 = min64(k0 + CK, p_end);
+            const int nk = (int)max64(0, w1 - k0);  // the chunk's keys (warp-uniform)
+            const bool staged = sm100::mbar_wait(&pbar[b], (u >> 1) & 1, abort_flag, pg.err);
+            if (!prefetched && stager && lane == 0) {
+                // The pair's later items stream into L2 once its first data
+                // has landed, keeping DRAM busy behind the first wave.
+                prefetched = true;
+                Item x;
+                for (int64_t it2 = cur.it + n_pairs; find(x, it2); it2 = x.it + n_pairs) prefetch_item<F>(*x.pp, x.g, x.s);
+            }
+            if (c == NCH - 1 && have_n) load_q(nxt, qv);  // the next item's queries, early
+            const unsigned char *crec = brec(b);
+            const float *cscl = bscl(b);
+            if (nk > 0 && staged) {
+                // Logit of this lane's key for each row of this warp's head.
+                // The packed FMA pairs dimensions (d, d + 1) into (even, odd)
+                // partial sums, each half an ordinary fmaf.
+                const int key = min(lane, nk - 1);  // idle lanes read a staged key, masked below
+                const unsigned char *ks = crec + key * S::SLOT;
+                const float *kscl = cscl + key * 5;
+                float lg[R];
+                {
+                    float2 acc[R];
+#pragma unroll
+                    for (int r = 0; r < R; r++) acc[r] = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int part = 0; part < 4; part++) {  // T[0:16], T[16:32], S_h[0:16], S_h[16:32]
+                        const int e = part < 2 ? 16 * part : 32 + 32 * hd + 16 * (part - 2);
+                        const int blk = part < 2 ? 0 : 1 + hd;
+                        float kv[16];
+                        slot_span16<F>(ks, e, S::CODED ? kscl[blk] : 1.0f, kv);
+#pragma unroll
+                        for (int d = 0; d < 16; d += 4) {
+#pragma unroll
+                            for (int r = 0; r < R; r++) {
+                                const float4 x = *reinterpret_cast<const float4 *>(&qw[r][16 * part + d]);
+                                acc[r] = __ffma2_rn(make_float2(x.x, x.y), make_float2(kv[d], kv[d + 1]), acc[r]);
+                                acc[r] =
+                                    __ffma2_rn(make_float2(x.z, x.w), make_float2(kv[d + 2], kv[d + 3]), acc[r]);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int r = 0; r < R; r++) lg[r] = __fadd_rn(acc[r].x, acc[r].y);
+                }
+                // Online softmax of the chunk per row (the reference's tile
+                // step: chunk max, rescale, exp(s - max)), the rows interleaved
+                // so their shuffles overlap.  Branch-free: a row with no
+                // position in the chunk keeps its state.  Each lane keeps the
+                // denominator of its own keys; the lanes add up once per item.
+                // A full chunk (every row sees all of its keys) takes a path
+                // without masks and with constant slot offsets.
+                const bool full = nk == CK && k0 + CK <= len0;
+                float ev[R], cm[R];
 #pragma unroll
                 for (int r = 0; r < R; r++) {
-                    const float *qv = q_s[r][h] + 32;
-                    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+                    const int lim = full ? CK : (int)min64(nk, max64(0, len0 + r - k0));  // the row's keys: [0, lim)
+                    ev[r] = lane < lim ? __fmul_rn(lg[r], 0.125f) : -INFINITY;
+                    cm[r] = ev[r];
+                }
 #pragma unroll
-                    for (int d = 0; d < 32; d += 4) {
-                        const float4 x = *reinterpret_cast<const float4 *>(qv + d);
-                        d0 = fmaf(x.x, key[d], d0);
-                        d1 = fmaf(x.y, key[d + 1], d1);
-                        d2 = fmaf(x.z, key[d + 2], d2);
-                        d3 = fmaf(x.w, key[d + 3], d3);
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int r = 0; r < R; r++) cm[r] = fmaxf(cm[r], __shfl_xor_sync(0xffffffffu, cm[r], o));
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const bool empty = cm[r] == -INFINITY;
+                    const float m_old = m_st[r];
+                    const float m_new = rmax(m_old, cm[r]);
+                    const float alpha = empty ? 1.0f : (m_old == -INFINITY ? 0.0f : expf(__fsub_rn(m_old, m_new)));
+                    ev[r] = (ev[r] != -INFINITY && !empty) ? softmax_exp<FAST>(__fsub_rn(ev[r], m_new)) : 0.0f;
+                    pw[r][lane] = ev[r];
+                    m_st[r] = m_new;
+                    l_st[r] = __fadd_rn(__fmul_rn(l_st[r], alpha), ev[r]);
+                    oa[r] = __fmul2_rn(oa[r], make_float2(alpha, alpha));
+                    ob[r] = __fmul2_rn(ob[r], make_float2(alpha, alpha));
+                }
+                __syncwarp();
+                // O += P V in key order: even keys into the .x halves, odd
+                // keys into the .y halves; this lane's two dimensions.  Keys
+                // before len0 are visible to every row; the last R - 1
+                // positions only to the rows that see them (a row never
+                // touches a value it does not see, so a NaN there stays out).
+                const int vblk = 3 + (lane >> 4);  // this lane's value scale block
+                auto pv4 = [&](int j) {           // keys j .. j + 3, all rows
+                    float2 va[2], vb[2];          // (key j + 2i, key j + 2i + 1) at dims 2 lane, 2 lane + 1
+#pragma unroll
+                    for (int i = 0; i < 2; i++)
+                        slot_vpair2<F>(crec + (j + 2 * i) * S::SLOT, crec + (j + 2 * i + 1) * S::SLOT, 96 + 2 * lane,
+                                       S::CODED ? cscl[(j + 2 * i) * 5 + vblk] : 1.0f,
+                                       S::CODED ? cscl[(j + 2 * i + 1) * 5 + vblk] : 1.0f, va[i], vb[i]);
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        const float4 p = *reinterpret_cast<const float4 *>(&pw[r][j]);
+                        oa[r] = __ffma2_rn(make_float2(p.x, p.y), va[0], oa[r]);
+                        ob[r] = __ffma2_rn(make_float2(p.x, p.y), vb[0], ob[r]);
+                        oa[r] = __ffma2_rn(make_float2(p.z, p.w), va[1], oa[r]);
+                        ob[r] = __ffma2_rn(make_float2(p.z, p.w), vb[1], ob[r]);
                     }
-                    lg[2 * r + h] = (lg[2 * r + h] + ((d0 + d1) + (d2 + d3))) * 0.125f;
+                };
+                if (full) {
+#pragma unroll
+                    for (int j = 0; j < CK; j += 4) pv4(j);
+                } else {
+                    const int n_all = (int)max64(0, min64(w1, len0) - k0);
+                    int j = 0;
+                    for (; j + 4 <= n_all; j += 4) pv4(j);
+                    for (; j < nk; j++) {
+                        const float2 v =
+                            slot_pair<F>(crec + j * S::SLOT, 96 + 2 * lane, S::CODED ? cscl[j * 5 + vblk] : 1.0f);
+                        const bool all = j < n_all;
+#pragma unroll
+                        for (int r = 0; r < R; r++) {
+                            if (all || k0 + j < len0 + r) {
+                                const float p = pw[r][j];
+                                if (j & 1) {
+                                    oa[r].y = fmaf(p, v.x, oa[r].y);
+                                    ob[r].y = fmaf(p, v.y, ob[r].y);
+                                } else {
+                                    oa[r].x = fmaf(p, v.x, oa[r].x);
+                                    ob[r].x = fmaf(p, v.y, ob[r].x);
+                                }
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            // Chunk u + 1's scales become visible with the pair barrier.
+            if constexpr (S::CODED) {
+                if (stager) {
+                    const bool next_in_item = c + 1 < NCH;
+                    if (next_in_item || have_n) {
+                        const Item &x = next_in_item ? cur : nxt;
+                        const int c1 = next_in_item ? c + 1 : 0;
+                        if (lane < min64(CK, x.pp->last - (int64_t)x.s * FO_SPLIT - (int64_t)c1 * CK))
+#pragma unroll
+                            for (int i = 0; i < 5; i++) bscl(b ^ 1)[lane * 5 + i] = sc_next[0][i];
+                    }
+                }
+            }
+            // Both warps are done with buffer b (and agree whether their
+            // waits succeeded); the stager refills it with chunk u + 2.
+            ok = pair_sync_and(pair, staged);
+            if (ok && stager) {
+                const int c2 = c + 2;
+                const bool in_item = c2 < NCH;
+                if (in_item || have_n) {
+                    const Item &x = in_item ? cur : nxt;
+                    sm100::fence_proxy_async_smem();  // the slot reads before the copies' writes
+                    stage_chunk<F>(*x.pp, x.g, x.s, in_item ? c2 : c2 - NCH, lane, brec(b), &pbar[b], sc_new);
+                    if constexpr (S::CODED) {
+#pragma unroll
+                        for (int i = 0; i < 5; i++) sc_next[0][i] = sc_new[0][i];
+                    }
                 }
             }
         }
-        // Online softmax of the chunk per (row, head).
+        if (!ok) break;
+        // This warp's head: the split's unnormalized partial (the lanes'
+        // denominators added in a fixed order).
 #pragma unroll
-        for (int rh = 0; rh < 2 * R; rh++) {
-            const int64_t row_len = pg.last - R + 1 + (rh >> 1);
-            const bool valid = pos < row_len;
-            const float x = valid ? lg[rh] : -INFINITY;
-            const float bm = warp_max(x);
-            if (bm == -INFINITY) {  // no position of this row in the chunk (warp-uniform)
-                pw[rh][lane] = 0.0f;
-                continue;
-            }
-            const float m_old = mr[rh];
-            const float m_new = rmax(m_old, bm);
-            const float alpha = m_old == -INFINITY ? 0.0f : expf(m_old - m_new);
-            const float p = valid ? softmax_exp<FAST>(x - m_new) : 0.0f;
-            pw[rh][lane] = p;
-            const float l_new = lr[rh] * alpha + warp_sum(p);
-            __syncwarp();
-            if (lane == 0) {
-                lr[rh] = l_new;
-                mr[rh] = m_new;
-            }
-            o0[rh] *= alpha;
-            o1[rh] *= alpha;
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int r = 0; r < R; r++) l_st[r] = __fadd_rn(l_st[r], __shfl_xor_sync(0xffffffffu, l_st[r], o));
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int64_t row_head = (int64_t)r * H + 2 * cur.g + hd;
+            *reinterpret_cast<float2 *>(pg.part_o + (row_head * pg.splits + cur.s) * FO_HD + 2 * lane) =
+                make_float2(__fadd_rn(oa[r].x, oa[r].y), __fadd_rn(ob[r].x, ob[r].y));
+            if (lane == 0)
+                *reinterpret_cast<float2 *>(pg.part_ml + (row_head * pg.splits + cur.s) * 2) =
+                    make_float2(m_st[r], l_st[r]);
         }
-        __syncwarp();
-        // O += P V in key order; this lane's two dimensions.
-#pragma unroll
-        for (int j4 = 0; j4 < CHUNK / 4; j4++) {
-            float2 v[4];
-#pragma unroll
-            for (int jj = 0; jj < 4; jj++) v[jj] = *reinterpret_cast<const float2 *>(&vw[4 * j4 + jj][2 * lane]);
-#pragma unroll
-            for (int rh = 0; rh < 2 * R; rh++) {
-                const float4 p = *reinterpret_cast<const float4 *>(&pw[rh][4 * j4]);
-                o0[rh] = fmaf(p.x, v[0].x, o0[rh]);
-                o1[rh] = fmaf(p.x, v[0].y, o1[rh]);
-                o0[rh] = fmaf(p.y, v[1].x, o0[rh]);
-                o1[rh] = fmaf(p.y, v[1].y, o1[rh]);
-                o0[rh] = fmaf(p.z, v[2].x, o0[rh]);
-                o1[rh] = fmaf(p.z, v[2].y, o1[rh]);
-                o0[rh] = fmaf(p.w, v[3].x, o0[rh]);
-                o1[rh] = fmaf(p.w, v[3].y, o1[rh]);
-            }
-        }
-        __syncwarp();
-    }
-    // Combine the warps in warp order (kv.rs:775-813 arithmetic) into this
-    // split's partial.
-    float *ow = v_base;  // [DEC_WARPS][2 * FO_MAX_ROWS][FO_HD]
-    __syncthreads();
-#pragma unroll
-    for (int rh = 0; rh < 2 * R; rh++)
-        *reinterpret_cast<float2 *>(&ow[(warp * 2 * FO_MAX_ROWS + rh) * FO_HD + 2 * lane]) = make_float2(o0[rh], o1[rh]);
-    __syncthreads();
-    for (int e = t; e < 2 * R * FO_HD; e += DEC_THREADS) {
-        const int rh = e / FO_HD, d = e % FO_HD;
-        float m = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < DEC_WARPS; w++) m = rmax(m, m_base[w * 2 * FO_MAX_ROWS + rh]);
-        float den = 0.0f, acc = 0.0f;
-        if (m != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < DEC_WARPS; w++) {
-                const float mw = m_base[w * 2 * FO_MAX_ROWS + rh];
-                if (mw == -INFINITY) continue;
-                const float f = expf(mw - m);
-                den = fmaf(l_base[w * 2 * FO_MAX_ROWS + rh], f, den);
-                acc = fmaf(ow[(w * 2 * FO_MAX_ROWS + rh) * FO_HD + d], f, acc);
-            }
-        }
-        const int64_t row_head = (int64_t)(rh >> 1) * H + 2 * g + (rh & 1);
-        pg.part_o[(row_head * pg.splits + s) * FO_HD + d] = acc;
-        if (d == 0) {
-            pg.part_ml[(row_head * pg.splits + s) * 2] = m;
-            pg.part_ml[(row_head * pg.splits + s) * 2 + 1] = den;
+        have = have_n;
+        if (have) {
+            cur = nxt;
+            have_n = find(nxt, cur.it + n_pairs);
         }
     }
-    // The group's last split to finish merges (threadfence reduction: no
-    // CTA ever waits for another).
-    __threadfence();
+    if (!ok && stager) {
+        // A wait that gave up (error word raised) at chunk u - 1: let the
+        // pair's copies in flight (chunks u - 1 and u) land before the CTA
+        // can exit; a phase that was never issued gives up after the bound.
+        sm100::mbar_wait_drain(&pbar[(u - 1) & 1], ((u - 1) >> 1) & 1);
+        sm100::mbar_wait_drain(&pbar[u & 1], (u >> 1) & 1);
+    }
+}
+
+// Merges the split partials of every (row, head) of a page, in split order,
+// and applies the sink (the reference's merge and epilogue,
+// kv.rs:775-813).  Launched as a programmatic dependent of the decode
+// kernel: it starts early and waits (griddepcontrol.wait) until every
+// partial is written.  CTA per (row, head): the splits' (max, denominator)
+// pairs go to shared memory, then thread (4 dimensions, slice) sums the
+// slice's splits k = slice, slice + SLICES, ... with its loads in flight
+// together, and the slices add in order.  A split whose max is -inf saw no
+// position and is skipped.  Everything depends only on the row's own length.
+constexpr int MERGE_SLICES = 16;
+constexpr int MERGE_THREADS = (FO_HD / 4) * MERGE_SLICES;
+
+__global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_constant__ fo_decode_page page0,
+                                                              const fo_decode_page *pages, int64_t H) {
+    extern __shared__ __align__(16) float msm[];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const fo_decode_page *pp = pages ? pages + blockIdx.y : &page0;
+    const int64_t row_head = blockIdx.x;
+    const int64_t r = row_head / H, h = row_head % H;
+    if (r >= pp->rows) return;
+    const int splits = pp->splits;
+    const int64_t row_len = pp->last - pp->rows + 1 + r;
+    const int n = (int)((row_len + FO_SPLIT - 1) / FO_SPLIT);
+    float *fk = msm;                                     // [splits] factors exp(m_k - M); -1 skips
+    float *lk = msm + splits;                            // [splits] denominators
+    float4 *part = reinterpret_cast<float4 *>(lk + splits + 4 - (2 * splits) % 4);  // [SLICES][16]
+    const float *ml = pp->part_ml + row_head * splits * 2;
+    const int t = threadIdx.x;
+    for (int k = t; k < n; k += MERGE_THREADS) {
+        const float2 x = __ldcg(reinterpret_cast<const float2 *>(ml) + k);
+        fk[k] = x.x;
+        lk[k] = x.y;
+    }
     __syncthreads();
-    if (t == 0) *last_flag = atomicAdd(pg.counters + g, 1u) == (unsigned)(pg.splits - 1);
+    float m = -INFINITY;
+    for (int k = 0; k < n; k++) m = rmax(m, fk[k]);
     __syncthreads();
-    if (!*last_flag) return;
-    __threadfence();
-    for (int e = t; e < 2 * R * FO_HD; e += DEC_THREADS) {
-        const int rh = e / FO_HD, d = e % FO_HD;
-        const int64_t r = rh >> 1, h = 2 * g + (rh & 1);
-        const int64_t row_head = r * H + h;
-        const int64_t row_len = pg.last - R + 1 + r;
-        const int n = (int)((row_len + FO_SPLIT - 1) / FO_SPLIT);
-        const float *po = pg.part_o + row_head * pg.splits * FO_HD;
-        const float *pml = pg.part_ml + row_head * pg.splits * 2;
-        float m = -INFINITY;
-        for (int k = 0; k < n; k++) m = rmax(m, __ldcg(pml + 2 * k));
-        float den = 0.0f, acc = 0.0f;
-        for (int k = 0; k < n; k++) {
-            const float pm = __ldcg(pml + 2 * k);
-            if (pm == -INFINITY) continue;
-            const float f = expf(pm - m);
-            den = fmaf(__ldcg(pml + 2 * k + 1), f, den);
-            acc = fmaf(__ldcg(po + k * FO_HD + d), f, acc);
+    for (int k = t; k < n; k += MERGE_THREADS) fk[k] = fk[k] == -INFINITY ? -1.0f : expf(fk[k] - m);
+    __syncthreads();
+    const int dq = t % (FO_HD / 4), sl = t / (FO_HD / 4);
+    const float4 *po = reinterpret_cast<const float4 *>(pp->part_o + row_head * splits * FO_HD) + dq;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = sl; k0 < n; k0 += 8 * MERGE_SLICES) {
+        float4 o[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int k = k0 + i * MERGE_SLICES;
+            o[i] = k < n ? __ldcg(po + (int64_t)k * (FO_HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int k = k0 + i * MERGE_SLICES;
+            if (k < n && fk[k] >= 0.0f) {
+                acc.x = fmaf(o[i].x, fk[k], acc.x);
+                acc.y = fmaf(o[i].y, fk[k], acc.y);
+                acc.z = fmaf(o[i].z, fk[k], acc.z);
+                acc.w = fmaf(o[i].w, fk[k], acc.w);
+            }
+        }
+    }
+    part[sl * (FO_HD / 4) + dq] = acc;
+    __syncthreads();
+    if (t < FO_HD) {
+        float den = 0.0f;
+        for (int j = 0; j < n; j++)
+            if (fk[j] >= 0.0f) den = fmaf(lk[j], fk[j], den);
+        const float *pf = reinterpret_cast<const float *>(part);
+        float o = 0.0f;
+#pragma unroll
+        for (int i = 0; i < MERGE_SLICES; i++) o = __fadd_rn(o, pf[i * FO_HD + t]);
         const float lse = m + logf(den);
-        pg.out[row_head * FO_HD + d] = (acc / den) * sink_scale(pg.sinks[h], lse);
+        pp->out[row_head * FO_HD + t] = (o / den) * sink_scale(pp->sinks[h], lse);
     }
-    if (t == 0) pg.counters[g] = 0u;  // ready for the next call on this cache
 }
 
 }  // namespace fo
 
-// Launches one instantiation, raising its dynamic shared-memory limit once.
-template <int F, bool FAST, int R>
-static cudaError_t launch_one(dim3 grid, const fo_decode_page &page0, const fo_decode_page *dev_pages,
-                              int64_t groups, cudaStream_t stream) {
+static PFN_cuTensorMapEncodeTiled_v12000 record_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+template <int F>
+static bool record_map(CUtensorMap *map, const void *codes, int64_t prefix_len, int64_t prefix_stride,
+                       int64_t groups, CUtensorMapDataType type) {
+    using S = fo::Shape<F>;
+    auto fn = record_map_encoder();
+    if (!fn || prefix_len <= 0 || prefix_len >= (int64_t(1) << 31)) return false;
+    cuuint64_t dims[3] = {FO_RECORD, (cuuint64_t)prefix_len, (cuuint64_t)groups};
+    cuuint64_t strides[2] = {(cuuint64_t)FO_RECORD * S::E, (cuuint64_t)prefix_stride * FO_RECORD * S::E};
+    cuuint32_t box[3] = {(cuuint32_t)(S::SLOT / S::E), (cuuint32_t)S::CK, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, type, 3, const_cast<void *>(codes), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t prefix_len, int64_t prefix_stride,
+                        int64_t groups) {
+    if ((reinterpret_cast<uintptr_t>(codes) & 15) != 0) return false;
+    switch (format) {
+    case fo::DF32: return record_map<fo::DF32>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    case fo::DQ16: return record_map<fo::DQ16>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_UINT16);
+    case fo::DQ8: return record_map<fo::DQ8>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    case fo::DBF16: return record_map<fo::DBF16>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    }
+    return false;
+}
+
+// The merge kernel, as a programmatic dependent of the decode kernel just
+// launched on `stream`.
+static cudaError_t launch_merge(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
+                                int64_t groups, int max_splits, int rows, cudaStream_t stream) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(fo::decode_kernel<F, FAST, R>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fo::DEC_SMEM);
+        cudaError_t e = cudaFuncSetAttribute(fo::merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    fo::decode_kernel<F, FAST, R><<<grid, fo::DEC_THREADS, fo::DEC_SMEM, stream>>>(page0, dev_pages, groups);
-    return cudaGetLastError();
+    const size_t smem = (size_t)(2 * max_splits + 4 + fo::MERGE_SLICES * FO_HD) * sizeof(float);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    const int64_t H = 2 * groups;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(rows * H), (unsigned)n_pages);
+    cfg.blockDim = dim3(fo::MERGE_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fo::merge_kernel, page0, dev_pages, H);
+}
+
+// Launches one instantiation as persistent CTAs (as many as fit on the
+// device at once, at most one per item), raising its dynamic shared-memory
+// limit once.
+template <int F, bool FAST, int R>
+static cudaError_t launch_one(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
+                              int64_t groups, int max_splits, cudaStream_t stream) {
+    constexpr int smem = fo::Smem<F, R>::BYTES;
+    constexpr int threads = fo::Shape<F>::THREADS;
+    static int resident = 0;  // CTAs of this instantiation the device holds at once
+    if (!resident) {
+        cudaError_t e =
+            cudaFuncSetAttribute(fo::decode_kernel<F, FAST, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        int dev = 0, sms = 0, per_sm = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fo::decode_kernel<F, FAST, R>, threads, smem);
+        if (e != cudaSuccess) return e;
+        resident = std::max(1, sms * per_sm);
+    }
+    const int64_t items = n_pages * (int64_t)max_splits * groups;
+    const unsigned grid = (unsigned)std::min<int64_t>(items, resident);
+    fo::decode_kernel<F, FAST, R><<<grid, threads, smem, stream>>>(page0, dev_pages, n_pages, groups, max_splits);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_merge(page0, dev_pages, n_pages, groups, max_splits, R, stream);
 }
 
 template <int F, bool FAST>
-static cudaError_t launch_rows(dim3 grid, int rows, const fo_decode_page &page0, const fo_decode_page *dev_pages,
-                               int64_t groups, cudaStream_t stream) {
+static cudaError_t launch_rows(int rows, const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
+                               int64_t groups, int max_splits, cudaStream_t stream) {
     switch (rows) {
-    case 1: return launch_one<F, FAST, 1>(grid, page0, dev_pages, groups, stream);
-    case 2: return launch_one<F, FAST, 2>(grid, page0, dev_pages, groups, stream);
-    case 3: return launch_one<F, FAST, 3>(grid, page0, dev_pages, groups, stream);
-    case 4: return launch_one<F, FAST, 4>(grid, page0, dev_pages, groups, stream);
-    case 5: return launch_one<F, FAST, 5>(grid, page0, dev_pages, groups, stream);
-    case 6: return launch_one<F, FAST, 6>(grid, page0, dev_pages, groups, stream);
-    case 7: return launch_one<F, FAST, 7>(grid, page0, dev_pages, groups, stream);
-    case 8: return launch_one<F, FAST, 8>(grid, page0, dev_pages, groups, stream);
+    case 1: return launch_one<F, FAST, 1>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 2: return launch_one<F, FAST, 2>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 3: return launch_one<F, FAST, 3>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 4: return launch_one<F, FAST, 4>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 5: return launch_one<F, FAST, 5>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 6: return launch_one<F, FAST, 6>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 7: return launch_one<F, FAST, 7>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 8: return launch_one<F, FAST, 8>(page0, dev_pages, n_pages, groups, max_splits, stream);
     }
     return cudaErrorInvalidValue;
 }
@@ -352,17 +764,18 @@ static cudaError_t launch_decode(const fo_decode_page &page0, const fo_decode_pa
                                  int format, int64_t groups, int fast_exp, int64_t max_splits, int rows,
                                  cudaStream_t stream) {
     if (n_pages <= 0 || max_splits <= 0) return cudaSuccess;
-    dim3 grid((unsigned)max_splits, (unsigned)groups, (unsigned)n_pages);
+    const int ms = (int)max_splits;
+#define FO_DEC_CASE(FMT)                                                                        \
+    case FMT:                                                                                   \
+        return fast_exp ? launch_rows<FMT, true>(rows, page0, dev_pages, n_pages, groups, ms, stream) \
+                        : launch_rows<FMT, false>(rows, page0, dev_pages, n_pages, groups, ms, stream);
     switch (format) {
-    case fo::DF32: return fast_exp ? launch_rows<fo::DF32, true>(grid, rows, page0, dev_pages, groups, stream)
-                                   : launch_rows<fo::DF32, false>(grid, rows, page0, dev_pages, groups, stream);
-    case fo::DQ16: return fast_exp ? launch_rows<fo::DQ16, true>(grid, rows, page0, dev_pages, groups, stream)
-                                   : launch_rows<fo::DQ16, false>(grid, rows, page0, dev_pages, groups, stream);
-    case fo::DQ8: return fast_exp ? launch_rows<fo::DQ8, true>(grid, rows, page0, dev_pages, groups, stream)
-                                  : launch_rows<fo::DQ8, false>(grid, rows, page0, dev_pages, groups, stream);
-    case fo::DBF16: return fast_exp ? launch_rows<fo::DBF16, true>(grid, rows, page0, dev_pages, groups, stream)
-                                    : launch_rows<fo::DBF16, false>(grid, rows, page0, dev_pages, groups, stream);
+        FO_DEC_CASE(fo::DF32)
+        FO_DEC_CASE(fo::DQ16)
+        FO_DEC_CASE(fo::DQ8)
+        FO_DEC_CASE(fo::DBF16)
     }
+#undef FO_DEC_CASE
     return cudaErrorInvalidValue;
 }
 

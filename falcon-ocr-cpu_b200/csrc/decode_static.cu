@@ -12,17 +12,15 @@
 // FO_STATIC_POSITIONS cached positions (prefix + tail), the shapes of the
 // reference model (8 verification rows, 16 heads, a 16,384-token context);
 // larger calls are refused.  Every GPU that loads this library holds the
-// array (about 1.1 MiB) until the process exits.
+// array (about 2.1 MiB) until the process exits.
 //
 // The first call on each device looks the array's device address up
 // (cudaGetSymbolAddress, with that device current); make that first call
 // before any stream capture.  All calls share the one array: calls whose
 // kernels overlap on the GPU (other streams, other threads) race on it and
 // must be serialized by the caller.  The decode kernel writes every partial
-// it later merges; the per-group split counters at the end of the array must
-// start at zero, which they do (device arrays are zero-initialized when the
-// library's module loads) and every call leaves them at zero again (the CTA
-// that merges a group resets its counter).
+// that the merge kernel after it reads, so nothing in the array needs
+// initializing or clearing between calls.
 #include <cstdio>
 #include <mutex>
 
@@ -36,12 +34,11 @@
 #define FO_STATIC_SPLITS (FO_STATIC_POSITIONS / FO_SPLIT)
 #define FO_STATIC_O_FLOATS (FO_STATIC_ROWS * FO_STATIC_HEADS * FO_STATIC_SPLITS * FO_HD)
 #define FO_STATIC_ML_FLOATS (FO_STATIC_ROWS * FO_STATIC_HEADS * FO_STATIC_SPLITS * 2)
-#define FO_STATIC_GROUPS (FO_STATIC_HEADS / 2)
+#define FO_STATIC_FLOATS (FO_STATIC_O_FLOATS + FO_STATIC_ML_FLOATS)
 
-// The decode partials: [rows][heads][splits][64] outputs, then
-// [rows][heads][splits][2] (max, denominator), then one split counter per KV
-// group (zero bits are the unsigned 0).
-static __device__ __align__(256) float g_decode_scratch[FO_STATIC_O_FLOATS + FO_STATIC_ML_FLOATS + FO_STATIC_GROUPS];
+// The decode partials: split outputs [rows][heads][splits][64], then their
+// (max, denominator) [rows][heads][splits][2].
+static __device__ __align__(256) float g_decode_scratch[FO_STATIC_FLOATS];
 
 namespace {
 
@@ -105,9 +102,10 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
     p.q = q;
     p.sinks = sinks;
     p.out = output;
-    p.part_o = g_scratch_ptr[dev];
-    p.part_ml = g_scratch_ptr[dev] + FO_STATIC_O_FLOATS;
-    p.counters = reinterpret_cast<unsigned *>(g_scratch_ptr[dev] + FO_STATIC_O_FLOATS + FO_STATIC_ML_FLOATS);
+    float *base = g_scratch_ptr[dev];
+    p.part_o = base;
+    p.part_ml = base + FO_STATIC_O_FLOATS;
+    p.has_map = fo_make_record_map(&p.rec_map, codes, format, prefix_len, prefix_stride, n_kv_heads) ? 1 : 0;
     p.prefix_len = prefix_len;
     p.prefix_stride = prefix_stride;
     p.tail_stride = tail_stride;

@@ -111,12 +111,14 @@ struct fo_kv_cache {
     int64_t prefix_stride = 0, tail_stride = 0, max_splits = 0;
     void *codes = nullptr, *tail_codes = nullptr;
     uint16_t *scales = nullptr, *tail_scales = nullptr;
-    float *part_o = nullptr, *part_ml = nullptr;     // decode partials, rows <= 8
-    unsigned *counters = nullptr;                    // [groups] finished splits (zero between calls)
+    float *part_o = nullptr, *part_ml = nullptr;     // decode split partials, rows <= 8
+
     float *q_stage = nullptr, *out_stage = nullptr;  // [8][H][64] host-mode staging
     float *sinks_stage = nullptr;                    // [H]
     float *rows_stage = nullptr;                     // [2][8][H][64] append staging
     size_t bytes = 0;                                // record bytes
+    alignas(64) CUtensorMap rec_map;                 // prefix records for the decode kernel's TMA loads
+    int has_map = 0;
 };
 
 namespace {
@@ -380,7 +382,7 @@ int fo_kv_destroy(fo_kv_cache *c) {
     DeviceGuard guard(c->ctx->device);
     cudaStreamSynchronize(c->ctx->stream);
     void *ptrs[] = {c->codes,   c->tail_codes, c->scales,    c->tail_scales, c->part_o,    c->part_ml,
-                    c->counters, c->q_stage,   c->out_stage, c->sinks_stage, c->rows_stage};
+                    c->q_stage, c->out_stage,  c->sinks_stage, c->rows_stage};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete c;
@@ -428,7 +430,6 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
     alloc((void **)&c->tail_scales, tscale_bytes);
     alloc((void **)&c->part_o, (size_t)FO_MAX_ROWS_ABI * H * c->max_splits * 64 * 4);
     alloc((void **)&c->part_ml, (size_t)FO_MAX_ROWS_ABI * H * c->max_splits * 2 * 4);
-    alloc((void **)&c->counters, (size_t)G * sizeof(unsigned));
     alloc((void **)&c->q_stage, (size_t)FO_MAX_ROWS_ABI * H * 64 * 4);
     alloc((void **)&c->out_stage, (size_t)FO_MAX_ROWS_ABI * H * 64 * 4);
     alloc((void **)&c->sinks_stage, (size_t)H * 4);
@@ -438,7 +439,8 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
         return cuda_fail(e, "fo_kv_seal: cudaMalloc");
     }
     c->bytes = code_bytes + tail_bytes + (coded(format) ? scale_bytes + tscale_bytes : 0);
-    if (e == cudaSuccess) e = cudaMemsetAsync(c->counters, 0, (size_t)G * sizeof(unsigned), ctx->stream);
+    // Without a tensor map the decode kernel copies record by record.
+    c->has_map = fo_make_record_map(&c->rec_map, c->codes, format, prefix_len, c->prefix_stride, G) ? 1 : 0;
     if (e == cudaSuccess) e = cudaMemsetAsync(c->tail_codes, 0, tail_bytes, ctx->stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(c->tail_scales, 0, tscale_bytes, ctx->stream);
     const float *dk = k, *dv = v;
@@ -545,7 +547,9 @@ static fo_decode_page make_page(const fo_kv_cache *c, const float *q, const floa
     p.out = out;
     p.part_o = c->part_o;
     p.part_ml = c->part_ml;
-    p.counters = c->counters;
+    p.err = c->ctx->dev_err;
+    p.rec_map = c->rec_map;
+    p.has_map = c->has_map;
     p.prefix_len = c->prefix_len;
     p.prefix_stride = c->prefix_stride;
     p.tail_stride = c->tail_stride;
@@ -620,7 +624,7 @@ int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const fl
         if (c->ctx != ctx || c->format != c0->format || c->groups != c0->groups || c->fast_exp != c0->fast_exp)
             return fail(FO_ERR_INVALID, "decode batch: caches must share context, format, heads and exp");
     }
-    {  // each page's partials and counters belong to its cache: pages must be distinct caches
+    {  // each page's partials belong to its cache: pages must be distinct caches
         std::vector<const fo_kv_cache *> seen(caches, caches + n);
         std::sort(seen.begin(), seen.end());
         if (std::adjacent_find(seen.begin(), seen.end()) != seen.end())

@@ -2,6 +2,7 @@
 // the public boundary is include/fo_attention.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,7 +34,8 @@ cudaError_t fo_launch_append(const float *k, const float *v, int64_t rows, int64
                              cudaStream_t stream);
 
 // One decode page: a cache's records and the query rows against it.
-struct fo_decode_page {
+struct alignas(64) fo_decode_page {
+    CUtensorMap rec_map;  // prefix records as padded slots (fo_make_record_map); valid when has_map
     const void *codes;
     const uint16_t *scales;
     const void *tail_codes;
@@ -41,17 +43,25 @@ struct fo_decode_page {
     const float *q;      // [rows][H][64]
     const float *sinks;  // [H]
     float *out;          // [rows][H][64]
-    float *part_o;       // [rows][H][splits][64]
-    float *part_ml;      // [rows][H][splits][2]
-    unsigned *counters;  // [groups] finished splits; zero between calls
+    float *part_o;       // [rows][H][splits][64] split partials
+    float *part_ml;      // [rows][H][splits][2] (max, denominator)
+    unsigned *err;       // error word for bounded waits that gave up (may be null)
     int64_t prefix_len, prefix_stride, tail_stride, last;  // last = prefix_len + tail_len
     int32_t rows, splits;                                   // splits = ceil(last / FO_SPLIT)
+    int32_t has_map;
 };
+
+// The tensor map the decode kernel loads prefix records through: records
+// [groups][stride][160] of `format`, rows past prefix_len out of bounds, a
+// box of one chunk of keys whose rows are padded to the kernel's slot size.
+// Returns false if the driver's encoder is unavailable or refuses.
+bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t prefix_len, int64_t prefix_stride,
+                        int64_t groups);
 
 // Positions per decode split: the GPU's position partition.  Fixed, so a
 // row's partition depends only on its own length (verify rows equal their
 // single-row decodes bit for bit).
-#define FO_SPLIT 512
+#define FO_SPLIT 128
 
 // One page (descriptor read on the host, passed by value).
 cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t groups, int fast_exp,

@@ -81,6 +81,25 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte
+// aligned) from global into shared memory; completion on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Waits for `phase` of `bar` for at most FO_WAIT_NS, ignoring any abort
+// (used to let a CTA's own copies land before it exits).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t phase) {
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, phase)) return true;
+        if ((it & 63) == 63 && globaltimer() - t0 > FO_WAIT_NS) return false;
+    }
+}
+
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),

@@ -274,6 +274,35 @@ def test_nonfinite_tail_values_reach_the_output(ctx, fmt):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
+def test_nonfinite_draft_reaches_only_the_rows_that_see_it(ctx, fmt):
+    """A NaN value in the last drafted position: the verify rows before it do
+    not see that position (kv.rs:851-855) and stay finite and equal to their
+    single-row decodes; the last row is NaN on the pair's heads."""
+    p, rows = 700, 4
+    k, v, _ = G.kv_fixture(p, 5)
+    gpu = F.SplitPrefix.from_compact(k, v, p, p + rows, fmt=fmt)
+    tk, tv = G.kv_tail(rows)
+    tk = np.repeat(tk.reshape(rows, 8, 1, 64), 2, axis=2).reshape(-1)
+    tv = np.repeat(tv.reshape(rows, 8, 1, 64), 2, axis=2).reshape(-1)
+    for x in (tk, tv):
+        x[(rows - 1) * 1024 + 5] = np.nan
+        x[(rows - 1) * 1024 + 64 + 5] = np.nan
+    gpu.append(tk, tv)
+    q = G.kv_rows_query(rows)
+    sinks = np.full(16, 0.5, np.float32)
+    joint = np.zeros(rows * 1024, np.float32)
+    gpu.attention_decode_rows(q, rows, sinks, joint)
+    assert np.isfinite(joint[:(rows - 1) * 1024]).all()
+    assert np.isnan(joint[(rows - 1) * 1024:(rows - 1) * 1024 + 128]).all()
+    assert np.isfinite(joint[(rows - 1) * 1024 + 128:]).all()
+    for r in reversed(range(rows - 1)):
+        gpu.truncate_tail(r + 1)
+        single = np.zeros(1024, np.float32)
+        gpu.attention_decode(q[r * 1024:(r + 1) * 1024], p + gpu.tail_len, sinks, single)
+        assert np.array_equal(joint[r * 1024:(r + 1) * 1024].view(np.uint32), single.view(np.uint32)), r
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
 def test_truncated_tails_take_new_positions_like_fresh_ones(ctx, fmt):
     """src/quant/kv/tests.rs:326-353"""
     p, generated, kept = 37, 6, 2
