@@ -44,6 +44,7 @@ SEQ, IMAGE_END, HEADS, KV_HEADS = 6544, 4096, 16, 8
 VISIBLE_PAIRS = IMAGE_END * IMAGE_END + sum(range(IMAGE_END + 1, SEQ + 1))
 FLOP_PER_CALL = 4 * 64 * VISIBLE_PAIRS * HEADS  # QK and PV multiply-adds, 2 FLOP each
 DECODE_L, DECODE_ROWS = 16384, 5
+SHARDED_T = 16384  # C5b page
 RECORD_BYTES = {"bf16": 8 * 160 * 2, "f32": 8 * 160 * 4}  # per position, all groups (tail records are smaller)
 
 
@@ -306,6 +307,49 @@ def time_e2e(run, args, inputs):
             "d2h_bytes_per_step": int(SEQ * HEADS * 64 * 4), "ms_per_step": round(ms, 3)}
 
 
+def time_sharded(run, args):
+    """C5b: one 16,384-token causal prefill (BF16 static shift, seed 4)
+    sharded by KV group over the ranks, the output gathered (BF16, rank-major
+    bands) over NCCL while the next band computes.  Every rank builds the
+    same page and keeps its own heads."""
+    import generators as G
+    import sharded as S
+    torch, F = run.torch, run.F
+    T = SHARDED_T
+    q, k, v, sinks, geo = G.c2_inputs(seed=4, seq=T, image_end=0)
+    qd = torch.from_numpy(q.reshape(T, HEADS, 64)).to(run.dev)
+    kd = torch.from_numpy(k.reshape(T, HEADS, 64)).to(run.dev)
+    vd = torch.from_numpy(v.reshape(T, KV_HEADS, 64)).to(run.dev)
+    sd = torch.from_numpy(sinks).to(run.dev)
+    sp = S.ShardedPrefill(qd, kd, vd, sd, geo, HEADS, KV_HEADS, run.rank, run.world, n_bands=4)
+    for _ in range(max(args.warmup, 3)):
+        sp.run()
+    steps = max(3, min(args.steps, 20))
+    ms, _ = run.timed(lambda i: sp.run(), steps)
+    ms /= steps
+    flop = S.flops(T, HEADS, geo)
+    # Parity of the gathered page with the whole page on one GPU (bitwise:
+    # every head's arithmetic is the same).
+    check = None
+    if run.rank == 0:
+        kb, vb = kd.to(torch.bfloat16), vd.to(torch.bfloat16)
+        whole = torch.empty(T * HEADS * 64, device=run.dev)
+        F.attention_prefill_bf16(qd, kd, vd, geo, sd, whole, HEADS, KV_HEADS, keys_bf16=kb, values_bf16=vb,
+                                 ctx=run.ctx)
+        got = S.token_major(sp.gathered).float()
+        check = float((got - whole.view(T, HEADS, 64).to(torch.bfloat16).float()).abs().max().item())
+    gathered_bytes = T * HEADS * 64 * 2
+    achieved = flop / (ms / 1e3) / 1e12
+    out = {"workload": "C5b: 16,384-token causal prefill, heads sharded by KV group, BF16 output all-gathered",
+           "tokens": T, "ranks": run.world, "bands": len(sp.bands), "ms_per_step": round(ms, 4),
+           "tok_per_s": round(T / (ms / 1e3), 1), "gflop": round(flop / 1e9, 1), "tflops": round(achieved, 1),
+           "frac_of_world_peak": round(achieved / (run.world * run.peaks["bf16_tflops"]), 4),
+           "gather_bytes": gathered_bytes, "max_abs_diff_vs_one_gpu": check}
+    del sp, qd, kd, vd
+    torch.cuda.empty_cache()
+    return out
+
+
 def time_decode(run, args):
     """5-row verify decode at 16,384 positions over BF16 and FP32 records,
     rotating distinct caches (more than 4x L2).  The K calls are captured once
@@ -394,6 +438,8 @@ def run_ours(args, world, rank, local):
         line["e2e"] = time_e2e(run, args, inputs)
     if args.mode in ("full", "decode"):
         line["decode"] = time_decode(run, args)
+    if args.mode in ("full", "sharded"):
+        line["sharded_prefill"] = time_sharded(run, args)
     if args.mode == "full" and rank == 0 and world == 1:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
@@ -415,7 +461,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["full", "prefill", "decode"], default="full",
+    ap.add_argument("--mode", choices=["full", "prefill", "decode", "sharded"], default="full",
                     help="full: the contract line; prefill/decode: only that part (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()

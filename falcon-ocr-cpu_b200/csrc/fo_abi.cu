@@ -22,7 +22,10 @@
 extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
                                               const float *sinks, float *out, int64_t total, int64_t n_heads,
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
-                                              int softmax_static, int exp_fast, unsigned *err, cudaStream_t stream);
+                                              int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
+                                              unsigned *err, cudaStream_t stream);
+
+#define FO_WAIT_LIMIT_MAX_NS 10000000000ull
 
 namespace {
 
@@ -276,6 +279,16 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     return FO_OK;
 }
 
+int fo_selftest_bounded_wait(fo_ctx *ctx, uint64_t limit_ns) {
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    if (limit_ns == 0 || limit_ns > FO_WAIT_LIMIT_MAX_NS) return fail(FO_ERR_INVALID, "limit_ns must be 1..10^10");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = fo_launch_bounded_wait(ctx->dev_err, (unsigned long long)limit_ns, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "bounded-wait self-test launch");
+    FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return check_device_errors(ctx);
+}
+
 int fo_ctx_synchronize(fo_ctx *ctx) {
     if (!ctx) return fail(FO_ERR_INVALID, "null context");
     DeviceGuard guard(ctx->device);
@@ -369,12 +382,37 @@ int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *
     }
     if (!aligned16(kb) || !aligned16(vb) || !aligned16(s.q) || !aligned16(s.out))
         return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
-    e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, T, H, G, geometry.image_start, geometry.image_end,
+    e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, T, H, G, geometry.image_start, geometry.image_end, 0, T,
                                options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err,
                                ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
     if ((st = timed_end(ctx, options.profile)) != FO_OK) return st;
     return finish_host(ctx, output, s.out, query_len * H * 64, mem);
+}
+
+int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *keys_bf16,
+                                   const uint16_t *values_bf16, int64_t total_len, int64_t n_heads, int64_t n_kv_heads,
+                                   fo_geometry geometry, const float *sinks, float *output, int64_t query_begin,
+                                   int64_t query_end, fo_prefill_options options) {
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    if (!q || !keys_bf16 || !values_bf16 || !sinks || !output) return fail(FO_ERR_INVALID, "null argument");
+    if (!(total_len >= 4 && n_kv_heads >= 1 && n_heads >= n_kv_heads && n_heads % n_kv_heads == 0))
+        return fail(FO_ERR_INVALID, "bad shape");
+    if (geometry.query_offset != 0 || geometry.image_start < 0 || geometry.image_start > geometry.image_end ||
+        geometry.image_end > total_len)
+        return fail(FO_ERR_INVALID, "geometry must describe a pure prefix");
+    if (!(query_begin >= 0 && query_begin <= query_end && query_end <= total_len && query_begin % 256 == 0 &&
+          (query_end % 256 == 0 || query_end == total_len)))
+        return fail(FO_ERR_INVALID, "query rows must be [begin, end) with begin and end multiples of 256 (or end = total)");
+    if (!aligned16(keys_bf16) || !aligned16(values_bf16) || !aligned16(q) || !aligned16(output))
+        return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = fo_launch_prefill_bf16(q, keys_bf16, values_bf16, sinks, output, total_len, n_heads, n_kv_heads,
+                                           geometry.image_start, geometry.image_end, query_begin, query_end,
+                                           options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST,
+                                           ctx->dev_err, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
+    return FO_OK;
 }
 
 int fo_kv_destroy(fo_kv_cache *c) {

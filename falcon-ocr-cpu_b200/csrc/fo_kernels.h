@@ -70,6 +70,9 @@ cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t
 cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format, int64_t groups,
                                    int fast_exp, int64_t max_splits, int max_rows, cudaStream_t stream);
 
+// The bounded-wait self-test kernel (selftest.cu).
+cudaError_t fo_launch_bounded_wait(unsigned *err, unsigned long long limit_ns, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

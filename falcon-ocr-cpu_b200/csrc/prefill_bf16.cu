@@ -56,6 +56,7 @@ struct Bf16Args {
     float *out;
     unsigned *err;
     int64_t total, n_heads, n_kv_heads, image_start, image_end;
+    int64_t pair_begin, pair_end;  // the 256-query pairs [begin, end) this launch computes
 };
 
 // Bounded wait that ignores the abort flag (for copies/MMAs that complete on
@@ -83,8 +84,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t T = a.total, H = a.n_heads;
-    const int64_t npairs = (T + 255) / 256;
-    const int64_t pair = npairs - 1 - blockIdx.x;  // heaviest (latest) tiles first
+    const int64_t pair = a.pair_end - 1 - blockIdx.x;  // heaviest (latest) tiles first
     const int64_t head = blockIdx.y;
     const int64_t kv_head = head / (H / a.n_kv_heads);
     const int64_t q0 = pair * 256;
@@ -385,14 +385,16 @@ static bool make_map(CUtensorMap *m, const uint16_t *base, int64_t rows, int64_t
 extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
                                               const float *sinks, float *out, int64_t total, int64_t n_heads,
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
-                                              int softmax_static, int exp_fast, unsigned *err, cudaStream_t stream) {
+                                              int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
+                                              unsigned *err, cudaStream_t stream) {
     (void)exp_fast;  // the tensor-core softmax always takes the hardware exp2
-    if (total == 0) return cudaSuccess;
+    if (total == 0 || query_end <= query_begin) return cudaSuccess;
     CUtensorMap mk, mv;
     if (!fo::make_map(&mk, keys_bf16, total, n_heads) || !fo::make_map(&mv, values_bf16, total, n_kv_heads))
         return cudaErrorInvalidValue;
-    fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end};
-    dim3 grid((unsigned)((total + 255) / 256), (unsigned)n_heads);
+    const int64_t pb = query_begin / 256, pe = (query_end + 255) / 256;
+    fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe};
+    dim3 grid((unsigned)(pe - pb), (unsigned)n_heads);
     auto launch = [&](auto kernel) -> cudaError_t {
         cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fo::SMEM_BYTES);

@@ -50,16 +50,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
 }
 
 // Waits for `phase` of `bar`.  Returns false (and leaves the barrier) when
-// the CTA aborted or the wait exceeded FO_WAIT_NS; in the latter case it
-// raises the abort flag and the error bit.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, volatile int *abort_flag, unsigned *err) {
+// the CTA aborted or the wait exceeded limit_ns (FO_WAIT_NS unless given);
+// in the latter case it raises the abort flag and the error bit.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, volatile int *abort_flag, unsigned *err,
+                                          uint64_t limit_ns = FO_WAIT_NS) {
     if (mbar_try_wait(bar, phase)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, phase)) return true;
         if ((it & 63) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer() - t0 > FO_WAIT_NS) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
                 if (err) atomicOr(err, FO_DEVERR_WAIT_TIMEOUT);
                 return false;

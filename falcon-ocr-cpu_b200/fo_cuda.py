@@ -92,7 +92,8 @@ EXPORTS = [
     "fo_attention", "fo_attention_prefill_bf16", "fo_convert_bf16", "fo_kv_seal", "fo_kv_destroy",
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
-    "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch",
+    "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch", "fo_selftest_bounded_wait",
+    "fo_attention_prefill_bf16_rows",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -132,6 +133,8 @@ def lib() -> ctypes.CDLL:
         "fo_kv_attention_decode_rows": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_batch": (I, [PP, I64, PP, PP, PP]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
+        "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
+        "fo_attention_prefill_bf16_rows": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64, PrefillOptions]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -211,6 +214,11 @@ class Context:
         check(lib().fo_ctx_last_ms(self.handle, ctypes.byref(v)))
         return v.value
 
+    def selftest_bounded_wait(self, limit_ns: int) -> int:
+        """fo_selftest_bounded_wait: the raw status (FO_ERR_CUDA when the
+        device wait gave up after limit_ns, as designed)."""
+        return lib().fo_selftest_bounded_wait(self.handle, limit_ns)
+
 
 _default: Optional[Context] = None
 
@@ -254,6 +262,24 @@ def attention_prefill_bf16(q, k, v, geometry, sinks, output, n_heads, n_kv_heads
         options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
     check(lib().fo_attention_prefill_bf16(ctx.handle, pq, ctypes.byref(kv), total, Geometry(*geometry), ps, po, kb, vb,
                                           options, mem))
+    return output
+
+
+def attention_prefill_bf16_rows(q, keys_bf16, values_bf16, geometry, sinks, output, n_heads, n_kv_heads, query_begin,
+                                query_end, options=None, ctx=None):
+    """fo_attention_prefill_bf16_rows: the BF16 prefill of query rows
+    [query_begin, query_end) of a pure prefix (CUDA tensors; BF16 keys and
+    values already converted).  Rows outside the range are left as they are."""
+    ctx = ctx or default_context()
+    for a in (q, keys_bf16, values_bf16, sinks, output):
+        if not _on_device(a) or not a.is_contiguous():
+            raise FoError("fo_attention_prefill_bf16_rows takes contiguous CUDA tensors")
+    total = q.numel() // (n_heads * 64)
+    if options is None:
+        options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
+    check(lib().fo_attention_prefill_bf16_rows(ctx.handle, q.data_ptr(), keys_bf16.data_ptr(), values_bf16.data_ptr(),
+                                               total, n_heads, n_kv_heads, Geometry(*geometry), sinks.data_ptr(),
+                                               output.data_ptr(), query_begin, query_end, options))
     return output
 
 

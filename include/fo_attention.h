@@ -117,6 +117,14 @@ int fo_ctx_synchronize(fo_ctx *ctx);
 /* Device milliseconds of the last call's kernels when options.profile was set. */
 int fo_ctx_last_ms(fo_ctx *ctx, float *ms);
 
+/* Self-test of the kernels' bounded waits (no counterpart in the reference):
+ * runs one CTA whose mbarrier wait never completes, so it gives up after
+ * limit_ns nanoseconds, raises the context's error word and returns.  The
+ * call synchronizes and returns FO_ERR_CUDA with the timeout message when
+ * the wait gave up as designed (FO_OK would mean it did not); the context
+ * stays usable. */
+int fo_selftest_bounded_wait(fo_ctx *ctx, uint64_t limit_ns);
+
 /* kernels::attention_with (mod.rs:256-311): any head_dim <= 256, prefix or
  * mixed caches, any query length.  query_len >= 4 with head_dim 64 runs the
  * FP32 tiles (options.fp32_softmax, options.exp); other shapes run the
@@ -136,6 +144,20 @@ int fo_attention(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t q
 int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len,
                               fo_geometry geometry, const float *sinks, float *output, const uint16_t *keys_bf16,
                               const uint16_t *values_bf16, fo_prefill_options options, int mem);
+
+/* The BF16 prefill of query rows [query_begin, query_end) only (no
+ * counterpart in the reference, which prefills a page whole): a pure prefix
+ * of total_len positions with pre-converted BF16 keys [total][n_heads][64]
+ * and values [total][n_kv_heads][64], device pointers only, q and output
+ * FP32 [total][n_heads][64] (rows outside the range are not written).
+ * query_begin is a multiple of 256 and query_end a multiple of 256 or
+ * total_len.  It lets a caller pipeline the output: the head-sharded
+ * multi-GPU prefill gathers each finished band of rows while the next one
+ * computes. */
+int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *keys_bf16,
+                                   const uint16_t *values_bf16, int64_t total_len, int64_t n_heads, int64_t n_kv_heads,
+                                   fo_geometry geometry, const float *sinks, float *output, int64_t query_begin,
+                                   int64_t query_end, fo_prefill_options options);
 
 /* FP32 -> BF16 (round to nearest even) of n device values, the conversion
  * fo_attention_prefill_bf16 applies to Bf16Kv::Convert inputs. */

@@ -123,5 +123,6 @@ def test_null_handles_are_rejected():
     assert L.fo_kv_attention_decode_rows(None, None, 1, None, None, F.MEM_HOST) == F.ERR_INVALID
     assert L.fo_kv_tail_len(None) == -1 and L.fo_kv_bytes(None) == -1
     assert L.fo_ctx_destroy(None) == F.OK and L.fo_kv_destroy(None) == F.OK
+    assert L.fo_selftest_bounded_wait(None, 1000) == F.ERR_INVALID
     h = ctypes.c_void_p()
     assert L.fo_ctx_create(-1, None, ctypes.byref(h)) != F.OK

@@ -387,3 +387,19 @@ def test_batch_decode_equals_single_pages(ctx):
     torch.cuda.synchronize()
     for a, b in zip(outs, singles):
         assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+# ------------------------------------------------------------ bounded waits
+def test_a_wait_that_runs_out_returns_an_error_and_the_context_survives(ctx):
+    """A device wait on a barrier nothing completes gives up after its limit
+    (1 ms here), raises the context's error word and returns; the host reads
+    FO_ERR_CUDA and the same context then runs a decode correctly."""
+    status = ctx.selftest_bounded_wait(1_000_000)
+    assert status == F.ERR_CUDA
+    assert "time limit" in F.lib().fo_last_error().decode()
+    ref, gpu, q = sealed_pair(F.KV_Q8, 300, 2, 3)
+    sinks = np.full(16, 0.5, np.float32)
+    out = np.zeros(1024, np.float32)
+    gpu.attention_decode(q, 302, sinks, out)
+    close(out, ref.decode_rows(q, 1, sinks), 1e-5, 1e-5)
+    gpu.close()

@@ -25,6 +25,14 @@ def dev(x):
     return torch.from_numpy(np.ascontiguousarray(x)).cuda()
 
 
+@pytest.fixture(scope="module")
+def ctx():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    c = F.Context(0)
+    yield c
+    c.close()
+
+
 def run(q, k, v, sinks, image, static, heads=16, kv_heads=8, converted=False):
     out = torch.zeros(q.size, dtype=torch.float32, device="cuda")
     opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC if static else F.SOFTMAX_ONLINE, F.SOFTMAX_ONLINE)
@@ -93,3 +101,42 @@ def test_baseline_c2_full_page(static):
     # and against the FP32 exact tiles of the same inputs, at the same bound
     fp32 = O.prefill64(q, k, v, 16, 8, geo, s)
     assert (np.abs(out - fp32) <= 2e-2 * (1.0 + np.abs(fp32))).all()
+
+
+def test_row_bands_equal_the_whole_page(ctx):
+    """fo_attention_prefill_bf16_rows over bands of query rows writes exactly
+    the whole-page kernel's rows (every query pair is computed the same way
+    whatever the launch covers)."""
+    T = 1000
+    q, k, v, s = (torch.from_numpy(x).cuda() for x in G.bf16_operands(T))
+    kb, vb = k.to(torch.bfloat16), v.to(torch.bfloat16)
+    whole = torch.zeros(T * 16 * 64, device="cuda")
+    F.attention_prefill_bf16(q, k, v, (0, 5, 262), s, whole, 16, 8, keys_bf16=kb, values_bf16=vb, ctx=ctx)
+    banded = torch.full((T * 16 * 64,), float("nan"), device="cuda")
+    for b, e in [(768, 1000), (0, 256), (256, 768)]:
+        F.attention_prefill_bf16_rows(q, kb, vb, (0, 5, 262), s, banded, 16, 8, b, e, ctx=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(whole, banded)
+    part = torch.full((T * 16 * 64,), float("nan"), device="cuda")
+    F.attention_prefill_bf16_rows(q, kb, vb, (0, 5, 262), s, part, 16, 8, 256, 512, ctx=ctx)
+    torch.cuda.synchronize()
+    rows = part.view(T, 16, 64)
+    assert torch.isnan(rows[:256]).all() and torch.isnan(rows[512:]).all()
+    assert torch.equal(rows[256:512], whole.view(T, 16, 64)[256:512])
+    with pytest.raises(F.FoError):
+        F.attention_prefill_bf16_rows(q, kb, vb, (0, 5, 262), s, part, 16, 8, 100, 512, ctx=ctx)
+
+
+def test_sharded_prefill_on_one_rank_matches_the_whole_page(ctx):
+    """The head-sharded prefill's GPU path (bands, BF16 output, gather) on a
+    world of one, against the whole-page kernel rounded to BF16."""
+    import sharded as S
+    T = 1100
+    q, k, v, s = (torch.from_numpy(x).cuda() for x in G.bf16_operands(T))
+    sp = S.ShardedPrefill(q.view(T, 16, 64), k.view(T, 16, 64), v.view(T, 8, 64), s, (0, 0, 300), 16, 8, 0, 1,
+                          n_bands=3)
+    got = S.token_major(sp.run())
+    whole = torch.zeros(T * 16 * 64, device="cuda")
+    F.attention_prefill_bf16(q, k, v, (0, 0, 300), s, whole, 16, 8, ctx=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(got, whole.view(T, 16, 64).to(torch.bfloat16))
