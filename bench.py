@@ -45,6 +45,7 @@ VISIBLE_PAIRS = IMAGE_END * IMAGE_END + sum(range(IMAGE_END + 1, SEQ + 1))
 FLOP_PER_CALL = 4 * 64 * VISIBLE_PAIRS * HEADS  # QK and PV multiply-adds, 2 FLOP each
 DECODE_L, DECODE_ROWS = 16384, 5
 SHARDED_T = 16384  # C5b page
+C4_L, C4_PAGES = 16384, 8
 RECORD_BYTES = {"bf16": 8 * 160 * 2, "f32": 8 * 160 * 4}  # per position, all groups (tail records are smaller)
 
 
@@ -307,6 +308,83 @@ def time_e2e(run, args, inputs):
             "d2h_bytes_per_step": int(SEQ * HEADS * 64 * 4), "ms_per_step": round(ms, 3)}
 
 
+def time_c4(run, args):
+    """C4: one decode row per page over 8 independent pages of 16,384
+    positions, in one batched call: the reference's Q8 records (1,360 B per
+    position) and BASELINE's INT8 format (int8 per head, FP32 scale per head
+    and 64 positions; 2,048 B + scales per position).  BF16-valued queries,
+    seed 3; two page sets rotate (> 2x L2 each step)."""
+    torch, F = run.torch, run.F
+    rng = np.random.default_rng(3 + run.rank)
+    L, n_pages = C4_L, C4_PAGES
+    out = {}
+    stream = torch.cuda.Stream(device=run.dev)
+    dctx = F.Context(run.local, stream=stream.cuda_stream)
+
+    def bf16_round(x):
+        return torch.from_numpy(x).to(torch.bfloat16).float()
+
+    qs = [bf16_round(rng.standard_normal(HEADS * 64).astype(np.float32)).to(run.dev) for _ in range(n_pages)]
+    ss = [torch.from_numpy(rng.standard_normal(HEADS).astype(np.float32)).to(run.dev) for _ in range(n_pages)]
+    os_ = [torch.empty(HEADS * 64, device=run.dev) for _ in range(n_pages)]
+    for fmt in ("q8", "int8"):
+        sets = []
+        for _ in range(2):
+            pages = []
+            for _ in range(n_pages):
+                k = torch.randn(L, HEADS, 64, device=run.dev)
+                v = torch.randn(L, HEADS if fmt == "int8" else KV_HEADS, 64, device=run.dev)
+                if fmt == "q8":
+                    k[:, 1::2, :32] = k[:, 0::2, :32]
+                    pages.append(F.SplitPrefix.from_compact(k, v, L, L, fmt="q8", ctx=dctx))
+                else:
+                    pages.append(F.Int8Cache(k, v, ctx=dctx))
+                del k, v
+            sets.append(pages)
+        torch.cuda.synchronize()
+
+        def step(i):
+            pages = sets[i % 2]
+            if fmt == "q8":
+                F.decode_batch(pages, qs, ss, os_)
+            else:
+                F.int8_decode_batch(pages, qs, ss, os_)
+
+        with torch.cuda.stream(stream):
+            for i in range(max(args.warmup, 3)):
+                step(i)
+            stream.synchronize()
+            steps = max(args.steps, 20)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            run.barrier()
+            start.record(stream)
+            for i in range(steps):
+                step(i)
+            end.record(stream)
+            run.barrier()
+        us = run.max_over_ranks(start.elapsed_time(end)) * 1e3 / steps
+        if fmt == "q8":
+            bytes_step = n_pages * L * 8 * (160 + 10)
+        else:
+            bytes_step = n_pages * (L * HEADS * 128 + 2 * HEADS * ((L + 63) // 64) * 4)
+        gbs = bytes_step / (us * 1e-6) / 1e9
+        out[fmt] = {"us_per_step": round(us, 2), "pages": n_pages, "kv_len": L, "rows": 1,
+                    "bytes_per_step": int(bytes_step),
+                    "format": "reference Q8 records (BF16 block scales)" if fmt == "q8"
+                              else "BASELINE int8 (per head, FP32 scale per 64 positions)",
+                    "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"],
+                                 "unit": "GB/s", "frac": round(gbs / run.peaks["hbm_gbs"], 4),
+                                 "traffic": run.traffic.get(f"c4_{fmt}")},
+                    "gpu_launches_per_step": 2, "timing": "back-to-back batched calls (no host sync)"}
+        for pages in sets:
+            for c in pages:
+                c.close()
+        del sets
+        torch.cuda.empty_cache()
+    dctx.close()
+    return out
+
+
 def time_sharded(run, args):
     """C5b: one 16,384-token causal prefill (BF16 static shift, seed 4)
     sharded by KV group over the ranks, the output gathered (BF16, rank-major
@@ -438,6 +516,8 @@ def run_ours(args, world, rank, local):
         line["e2e"] = time_e2e(run, args, inputs)
     if args.mode in ("full", "decode"):
         line["decode"] = time_decode(run, args)
+    if args.mode in ("full", "c4"):
+        line["decode_c4"] = time_c4(run, args)
     if args.mode in ("full", "sharded"):
         line["sharded_prefill"] = time_sharded(run, args)
     if args.mode == "full" and rank == 0 and world == 1:
@@ -461,7 +541,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--mode", choices=["full", "prefill", "decode", "sharded"], default="full",
+    ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded"], default="full",
                     help="full: the contract line; prefill/decode: only that part (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()

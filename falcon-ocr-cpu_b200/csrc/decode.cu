@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <type_traits>
 
 namespace fo {
 
@@ -83,11 +84,13 @@ __device__ __forceinline__ float2 slot_pair(const unsigned char *slot, int e, fl
         const uint32_t w = *reinterpret_cast<const uint32_t *>(slot + 2 * e);
         return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
     } else if constexpr (F == DQ16) {
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(slot + 2 * e);
-        return make_float2(__fmul_rn((float)(int16_t)(w & 0xFFFFu), scale), __fmul_rn((float)(int16_t)(w >> 16), scale));
+        float lo, hi;
+        s16x2_f32(*reinterpret_cast<const uint32_t *>(slot + 2 * e), lo, hi);
+        return make_float2(__fmul_rn(lo, scale), __fmul_rn(hi, scale));
     } else {
-        const uint32_t w = *reinterpret_cast<const uint16_t *>(slot + e);
-        return make_float2(__fmul_rn((float)(int8_t)(w & 0xFFu), scale), __fmul_rn((float)(int8_t)(w >> 8), scale));
+        float lo, hi;
+        s8x2_f32(*reinterpret_cast<const uint16_t *>(slot + e), lo, hi);
+        return make_float2(__fmul_rn(lo, scale), __fmul_rn(hi, scale));
     }
 }
 
@@ -117,8 +120,10 @@ __device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, fl
                     out[8 * i + 2 * c] = __uint_as_float(w[c] << 16);
                     out[8 * i + 2 * c + 1] = __uint_as_float(w[c] & 0xFFFF0000u);
                 } else {
-                    out[8 * i + 2 * c] = __fmul_rn((float)(int16_t)(w[c] & 0xFFFFu), scale);
-                    out[8 * i + 2 * c + 1] = __fmul_rn((float)(int16_t)(w[c] >> 16), scale);
+                    float lo, hi;
+                    s16x2_f32(w[c], lo, hi);
+                    out[8 * i + 2 * c] = __fmul_rn(lo, scale);
+                    out[8 * i + 2 * c + 1] = __fmul_rn(hi, scale);
                 }
             }
         }
@@ -126,9 +131,12 @@ __device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, fl
         const uint4 x = *reinterpret_cast<const uint4 *>(slot + e);
         const uint32_t w[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-        for (int c = 0; c < 4; c++)
+        for (int c = 0; c < 4; c++) {
+            float f[4];
+            s8x4_f32(w[c], f);
 #pragma unroll
-            for (int b = 0; b < 4; b++) out[4 * c + b] = __fmul_rn((float)(int8_t)((w[c] >> (8 * b)) & 0xFFu), scale);
+            for (int b = 0; b < 4; b++) out[4 * c + b] = __fmul_rn(f[b], scale);
+        }
     }
 }
 
@@ -147,51 +155,57 @@ __device__ __forceinline__ void slot_vpair2(const unsigned char *sa, const unsig
         const uint32_t wb = *reinterpret_cast<const uint32_t *>(sb + 2 * e);
         lo = make_float2(__uint_as_float(wa << 16), __uint_as_float(wb << 16));
         hi = make_float2(__uint_as_float(wa & 0xFFFF0000u), __uint_as_float(wb & 0xFFFF0000u));
-    } else if constexpr (F == DQ16) {
-        const uint32_t wa = *reinterpret_cast<const uint32_t *>(sa + 2 * e);
-        const uint32_t wb = *reinterpret_cast<const uint32_t *>(sb + 2 * e);
-        lo = make_float2(__fmul_rn((float)(int16_t)(wa & 0xFFFFu), ca), __fmul_rn((float)(int16_t)(wb & 0xFFFFu), cb));
-        hi = make_float2(__fmul_rn((float)(int16_t)(wa >> 16), ca), __fmul_rn((float)(int16_t)(wb >> 16), cb));
     } else {
-        const uint32_t wa = *reinterpret_cast<const uint16_t *>(sa + e);
-        const uint32_t wb = *reinterpret_cast<const uint16_t *>(sb + e);
-        lo = make_float2(__fmul_rn((float)(int8_t)(wa & 0xFFu), ca), __fmul_rn((float)(int8_t)(wb & 0xFFu), cb));
-        hi = make_float2(__fmul_rn((float)(int8_t)(wa >> 8), ca), __fmul_rn((float)(int8_t)(wb >> 8), cb));
+        float a0, a1, b0, b1;
+        if constexpr (F == DQ16) {
+            s16x2_f32(*reinterpret_cast<const uint32_t *>(sa + 2 * e), a0, a1);
+            s16x2_f32(*reinterpret_cast<const uint32_t *>(sb + 2 * e), b0, b1);
+        } else {
+            s8x2_f32(*reinterpret_cast<const uint16_t *>(sa + e), a0, a1);
+            s8x2_f32(*reinterpret_cast<const uint16_t *>(sb + e), b0, b1);
+        }
+        lo = make_float2(__fmul_rn(a0, ca), __fmul_rn(b0, cb));
+        hi = make_float2(__fmul_rn(a1, ca), __fmul_rn(b1, cb));
     }
 }
 
 // Stages one key's record into its slot: a prefix record as it is, a tail
-// record [K 64 | V 64] as [K | K[32:64] | V].  Returns the bytes copied.
-// Coded formats: the key's scales, decoded, in slot order [T, S0, S1, V0, V1].
+// record [K 64 | V 64] as [K | K[32:64] | V].
 template <int F>
-__device__ __forceinline__ uint32_t stage_key(const fo_decode_page &pg, int64_t g, int64_t pos, unsigned char *slot,
-                                              float *scl, uint64_t *bar) {
+__device__ __forceinline__ void stage_key(const fo_decode_page &pg, int64_t g, int64_t pos, unsigned char *slot,
+                                          uint64_t *bar) {
     constexpr int E = Shape<F>::E;
     if (pos < pg.prefix_len) {
         const int64_t r = g * pg.prefix_stride + pos;
         sm100::bulk_g2s(slot, reinterpret_cast<const unsigned char *>(pg.codes) + r * FO_RECORD * E, FO_RECORD * E, bar);
-        if constexpr (Shape<F>::CODED) {
-            const uint16_t *s = pg.scales + r * 5;
-#pragma unroll
-            for (int i = 0; i < 5; i++) scl[i] = bf16_f32(__ldg(s + i));
-        }
     } else {
         const int64_t r = g * pg.tail_stride + (pos - pg.prefix_len);
         const unsigned char *rec = reinterpret_cast<const unsigned char *>(pg.tail_codes) + r * FO_TAIL_RECORD * E;
         sm100::bulk_g2s(slot, rec, 64 * E, bar);
         sm100::bulk_g2s(slot + 64 * E, rec + 32 * E, 32 * E, bar);
         sm100::bulk_g2s(slot + 96 * E, rec + 64 * E, 64 * E, bar);
-        if constexpr (Shape<F>::CODED) {
-            const uint16_t *s = pg.tail_scales + r * 4;
-            const float kt = bf16_f32(__ldg(s)), ks = bf16_f32(__ldg(s + 1));
-            scl[0] = kt;
-            scl[1] = ks;
-            scl[2] = ks;
-            scl[3] = bf16_f32(__ldg(s + 2));
-            scl[4] = bf16_f32(__ldg(s + 3));
-        }
     }
-    return FO_RECORD * E;
+}
+
+// Coded formats: the decoded scales of this lane's key of chunk c of split s
+// of group g, in slot order [T, S0, S1, V0, V1] (a tail key's spatial scale
+// serves both heads).  Lanes past the chunk's keys load nothing.
+template <int F>
+__device__ __forceinline__ void load_chunk_scales(const fo_decode_page &pg, int64_t g, int s, int c, int lane,
+                                                  float *sc) {
+    const int64_t pos = (int64_t)s * FO_SPLIT + (int64_t)c * Shape<F>::CK + lane;
+    if (pos >= min64((int64_t)(s + 1) * FO_SPLIT, pg.last)) return;
+    if (pos < pg.prefix_len) {
+        const uint16_t *p = pg.scales + (g * pg.prefix_stride + pos) * 5;
+#pragma unroll
+        for (int i = 0; i < 5; i++) sc[i] = bf16_f32(__ldg(p + i));
+    } else {
+        const uint16_t *p = pg.tail_scales + (g * pg.tail_stride + (pos - pg.prefix_len)) * 4;
+        sc[0] = bf16_f32(__ldg(p));
+        sc[1] = sc[2] = bf16_f32(__ldg(p + 1));
+        sc[3] = bf16_f32(__ldg(p + 2));
+        sc[4] = bf16_f32(__ldg(p + 3));
+    }
 }
 
 // Bulk L2 prefetch of [addr, addr + bytes), trimmed inward to 16-byte
@@ -225,13 +239,13 @@ __device__ __forceinline__ void prefetch_item(const fo_decode_page &pg, int64_t 
 }
 
 // Stages the records of chunk c of split s of group g (the issuing warp's
-// lanes each arrive once on the chunk's barrier) and returns this lane's
-// decoded scales.  A chunk of prefix records only is one TMA tile load
-// through the page's tensor map (rows padded to the slot by the box's
-// out-of-bounds fill); a chunk that reaches the tail copies record by record.
+// lanes each arrive once on the chunk's barrier).  A chunk of prefix records
+// only is one TMA tile load through the page's tensor map (rows padded to the
+// slot by the box's out-of-bounds fill); a chunk that reaches the tail copies
+// record by record.
 template <int F>
 __device__ __forceinline__ void stage_chunk(const fo_decode_page &pg, int64_t g, int s, int c, int lane,
-                                            unsigned char *crec, uint64_t *bar, float (*sc)[5]) {
+                                            unsigned char *crec, uint64_t *bar) {
     using S = Shape<F>;
     const int64_t k0 = (int64_t)s * FO_SPLIT + (int64_t)c * S::CK;
     const int64_t w1 = min64(k0 + S::CK, min64((int64_t)s * FO_SPLIT + FO_SPLIT, pg.last));
@@ -241,30 +255,12 @@ __device__ __forceinline__ void stage_chunk(const fo_decode_page &pg, int64_t g,
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
                      : "memory");
         if (lane == 0) sm100::tma_load_3d(crec, &pg.rec_map, bar, 0, (int)k0, (int)g);
-        if constexpr (S::CODED) {
-#pragma unroll
-            for (int j = 0; j < S::KPL; j++) {
-                const int key = lane + 32 * j;
-                if (key < nk) {
-                    const uint16_t *p = pg.scales + (g * pg.prefix_stride + k0 + key) * 5;
-#pragma unroll
-                    for (int i = 0; i < 5; i++) sc[j][i] = bf16_f32(__ldg(p + i));
-                }
-            }
-        }
         return;
     }
-    uint32_t bytes = 0;
-#pragma unroll
-    for (int j = 0; j < S::KPL; j++)
-        if (lane + 32 * j < nk) bytes += FO_RECORD * S::E;
+    const uint32_t bytes = lane < nk ? FO_RECORD * S::E : 0u;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
                  : "memory");
-#pragma unroll
-    for (int j = 0; j < S::KPL; j++) {
-        const int key = lane + 32 * j;
-        if (key < nk) stage_key<F>(pg, g, k0 + key, crec + key * S::SLOT, sc[j], bar);
-    }
+    if (lane < nk) stage_key<F>(pg, g, k0 + lane, crec + lane * S::SLOT, bar);
 }
 
 // Waits on a pair's named barrier (id 1 + pair, 64 threads) and returns
@@ -344,22 +340,24 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
     bool have = find(cur, (int64_t)pair * gridDim.x + blockIdx.x);
     bool have_n = have && find(nxt, cur.it + n_pairs);
     float2 qv[R];
-    float sc_next[1][5], sc_new[1][5];  // scales of chunk u + 1 (staged, unpublished) and of a new stage
     if (have) {
         load_q(cur, qv);  // ahead of the bulk copies in the memory queues
         if (stager) {
-            stage_chunk<F>(*cur.pp, cur.g, cur.s, 0, lane, brec(0), &pbar[0], sc_new);
-            stage_chunk<F>(*cur.pp, cur.g, cur.s, 1, lane, brec(1), &pbar[1], sc_next);
-            if constexpr (S::CODED) {
-                if (lane < min64(CK, cur.pp->last - (int64_t)cur.s * FO_SPLIT))
 #pragma unroll
-                    for (int i = 0; i < 5; i++) bscl(0)[lane * 5 + i] = sc_new[0][i];
+            for (int c = 0; c < 2; c++) {
+                stage_chunk<F>(*cur.pp, cur.g, cur.s, c, lane, brec(c), &pbar[c]);
+                if constexpr (S::CODED) {
+                    float sc[5];
+                    load_chunk_scales<F>(*cur.pp, cur.g, cur.s, c, lane, sc);
+                    if (lane < min64(CK, cur.pp->last - (int64_t)cur.s * FO_SPLIT - (int64_t)c * CK))
+#pragma unroll
+                        for (int i = 0; i < 5; i++) bscl(c)[lane * 5 + i] = sc[i];
+                }
             }
         }
     }
-    pair_sync_and(pair, true);  // chunk 0's scales are visible
+    pair_sync_and(pair, true);  // chunks 0 and 1's scales are visible
     uint32_t u = 0;             // chunks consumed by this pair
-    bool prefetched = false;
     bool ok = true;
     while (have && ok) {
 #pragma unroll
@@ -384,16 +382,25 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
         }
         for (int c = 0; c < NCH && ok; c++, u++) {
             const int b = u & 1;
+            // The stager asks for chunk u + 2's scales now; they land while
+            // this chunk computes and are published with its copies below.
+            const int c2 = c + 2;
+            const bool in_item = c2 < NCH;
+            const Item &x2 = in_item ? cur : nxt;
+            const bool has2 = in_item || have_n;
+            float sc_pre[5];
+            if constexpr (S::CODED) {
+                if (stager && has2) load_chunk_scales<F>(*x2.pp, x2.g, x2.s, in_item ? c2 : c2 - NCH, lane, sc_pre);
+            }
             const int64_t k0 = p0 + (int64_t)c * CK;
             const int64_t w1 = min64(k0 + CK, p_end);
             const int nk = (int)max64(0, w1 - k0);  // the chunk's keys (warp-uniform)
             const bool staged = sm100::mbar_wait(&pbar[b], (u >> 1) & 1, abort_flag, pg.err);
-            if (!prefetched && stager && lane == 0) {
-                // The pair's later items stream into L2 once its first data
-                // has landed, keeping DRAM busy behind the first wave.
-                prefetched = true;
-                Item x;
-                for (int64_t it2 = cur.it + n_pairs; find(x, it2); it2 = x.it + n_pairs) prefetch_item<F>(*x.pp, x.g, x.s);
+            if (c == 0 && have_n && stager && lane == 0) {
+                // The pair's next item streams into L2 while this one
+                // computes (one item ahead: a whole batch of pages would
+                // not fit in L2).
+                prefetch_item<F>(*nxt.pp, nxt.g, nxt.s);
             }
             if (c == NCH - 1 && have_n) load_q(nxt, qv);  // the next item's queries, early
             const unsigned char *crec = brec(b);
@@ -513,34 +520,20 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
                 }
                 __syncwarp();
             }
-            // Chunk u + 1's scales become visible with the pair barrier.
-            if constexpr (S::CODED) {
-                if (stager) {
-                    const bool next_in_item = c + 1 < NCH;
-                    if (next_in_item || have_n) {
-                        const Item &x = next_in_item ? cur : nxt;
-                        const int c1 = next_in_item ? c + 1 : 0;
-                        if (lane < min64(CK, x.pp->last - (int64_t)x.s * FO_SPLIT - (int64_t)c1 * CK))
-#pragma unroll
-                            for (int i = 0; i < 5; i++) bscl(b ^ 1)[lane * 5 + i] = sc_next[0][i];
-                    }
-                }
-            }
             // Both warps are done with buffer b (and agree whether their
-            // waits succeeded); the stager refills it with chunk u + 2.
+            // waits succeeded); the stager refills it with chunk u + 2 and
+            // its scales (read by both warps two chunks later, after the
+            // next pair barrier).
             ok = pair_sync_and(pair, staged);
-            if (ok && stager) {
-                const int c2 = c + 2;
-                const bool in_item = c2 < NCH;
-                if (in_item || have_n) {
-                    const Item &x = in_item ? cur : nxt;
-                    sm100::fence_proxy_async_smem();  // the slot reads before the copies' writes
-                    stage_chunk<F>(*x.pp, x.g, x.s, in_item ? c2 : c2 - NCH, lane, brec(b), &pbar[b], sc_new);
-                    if constexpr (S::CODED) {
+            if (ok && stager && has2) {
+                const int cc = in_item ? c2 : c2 - NCH;
+                if constexpr (S::CODED) {
+                    if (lane < min64(CK, x2.pp->last - (int64_t)x2.s * FO_SPLIT - (int64_t)cc * CK))
 #pragma unroll
-                        for (int i = 0; i < 5; i++) sc_next[0][i] = sc_new[0][i];
-                    }
+                        for (int i = 0; i < 5; i++) bscl(b)[lane * 5 + i] = sc_pre[i];
                 }
+                sm100::fence_proxy_async_smem();  // the slot reads before the copies' writes
+                stage_chunk<F>(*x2.pp, x2.g, x2.s, cc, lane, brec(b), &pbar[b]);
             }
         }
         if (!ok) break;

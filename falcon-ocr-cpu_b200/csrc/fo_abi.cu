@@ -26,6 +26,7 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
                                               unsigned *err, cudaStream_t stream);
 
 #define FO_WAIT_LIMIT_MAX_NS 10000000000ull
+#define FO_BATCH_PAGES 1024  // pages per batched launch
 
 namespace {
 
@@ -72,6 +73,45 @@ struct DevBuf {
     }
 };
 
+// Pinned host staging for the descriptors of batched launches, two slots:
+// a slot is rewritten only after its previous upload has completed, so a call
+// never waits for the kernels it launched before.
+struct HostDesc {
+    void *ptr[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    size_t bytes = 0;
+    int next = 0;
+    cudaError_t ensure(size_t need) {
+        if (need <= bytes) return cudaSuccess;
+        release();
+        for (int i = 0; i < 2; i++) {
+            cudaError_t e = cudaHostAlloc(&ptr[i], need, cudaHostAllocDefault);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming);
+            if (e != cudaSuccess) return e;
+        }
+        bytes = need;
+        return cudaSuccess;
+    }
+    // A free slot (its last upload finished) and its index.
+    void *acquire(int &slot) {
+        slot = next;
+        next ^= 1;
+        if (done[slot]) cudaEventSynchronize(done[slot]);
+        return ptr[slot];
+    }
+    cudaError_t uploaded(int slot, cudaStream_t st) { return cudaEventRecord(done[slot], st); }
+    void release() {
+        for (int i = 0; i < 2; i++) {
+            if (done[i]) cudaEventSynchronize(done[i]);
+            if (ptr[i]) cudaFreeHost(ptr[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+            ptr[i] = nullptr;
+            done[i] = nullptr;
+        }
+        bytes = 0;
+    }
+};
+
 // Keeps the caller's current device and restores it on exit.
 struct DeviceGuard {
     int prev = -1;
@@ -98,8 +138,10 @@ struct fo_ctx {
     unsigned *dev_err = nullptr;               // kernel error bits (bounded waits that gave up)
     DevBuf stage[6];                           // prefill host staging: q, prefix_k, generated_k, v, sinks, out
     DevBuf bf16_k, bf16_v;                     // Bf16Kv::Convert scratch
-    DevBuf pages;                              // decode batch descriptors
-    std::vector<fo_decode_page> host_pages;
+    DevBuf pages;                              // decode batch descriptors (device)
+    HostDesc host_pages;                       // and their pinned staging
+    DevBuf i8_pages;                           // INT8-format decode descriptors (device)
+    HostDesc host_i8_pages;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
 };
@@ -122,6 +164,15 @@ struct fo_kv_cache {
     size_t bytes = 0;                                // record bytes
     alignas(64) CUtensorMap rec_map;                 // prefix records for the decode kernel's TMA loads
     int has_map = 0;
+};
+
+struct fo_i8_cache {
+    fo_ctx *ctx = nullptr;
+    int64_t len = 0, heads = 0, splits = 0;
+    int8_t *k_codes = nullptr, *v_codes = nullptr;
+    float *k_scales = nullptr, *v_scales = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;  // decode partials [heads][splits][64], [..][2]
+    size_t bytes = 0;                             // codes and scales
 };
 
 namespace {
@@ -252,12 +303,14 @@ int fo_ctx_create(int device, void *stream, fo_ctx **out) {
     if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev1);
-    if (e == cudaSuccess) e = ctx->pages.ensure(sizeof(fo_decode_page) * 1024);
+    if (e == cudaSuccess) e = ctx->pages.ensure(sizeof(fo_decode_page) * FO_BATCH_PAGES);
+    if (e == cudaSuccess) e = ctx->host_pages.ensure(sizeof(fo_decode_page) * FO_BATCH_PAGES);
+    if (e == cudaSuccess) e = ctx->i8_pages.ensure(sizeof(fo_i8_page) * FO_BATCH_PAGES);
+    if (e == cudaSuccess) e = ctx->host_i8_pages.ensure(sizeof(fo_i8_page) * FO_BATCH_PAGES);
     if (e != cudaSuccess) {
         fo_ctx_destroy(ctx);
         return cuda_fail(e, "fo_ctx_create");
     }
-    ctx->host_pages.reserve(1024);
     *out = ctx;
     return FO_OK;
 }
@@ -270,6 +323,9 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     ctx->bf16_k.release();
     ctx->bf16_v.release();
     ctx->pages.release();
+    ctx->host_pages.release();
+    ctx->i8_pages.release();
+    ctx->host_i8_pages.release();
     if (ctx->flags) cudaFree(ctx->flags);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
@@ -669,23 +725,140 @@ int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const fl
             return fail(FO_ERR_INVALID, "decode batch: a cache appears twice");
     }
     DeviceGuard guard(ctx->device);
-    const int64_t cap = (int64_t)(ctx->pages.bytes / sizeof(fo_decode_page));
-    for (int64_t base = 0; base < n; base += cap) {
-        const int64_t m = std::min<int64_t>(cap, n - base);
-        ctx->host_pages.resize((size_t)m);
+    for (int64_t base = 0; base < n; base += FO_BATCH_PAGES) {
+        const int64_t m = std::min<int64_t>(FO_BATCH_PAGES, n - base);
+        int slot = 0;
+        fo_decode_page *hp = static_cast<fo_decode_page *>(ctx->host_pages.acquire(slot));
         int64_t max_splits = 1;
         for (int64_t i = 0; i < m; i++) {
-            ctx->host_pages[i] = make_page(caches[base + i], q[base + i], sinks[base + i], output[base + i], 1);
-            max_splits = std::max<int64_t>(max_splits, ctx->host_pages[i].splits);
+            hp[i] = make_page(caches[base + i], q[base + i], sinks[base + i], output[base + i], 1);
+            max_splits = std::max<int64_t>(max_splits, hp[i].splits);
         }
-        FO_CUDA(cudaMemcpyAsync(ctx->pages.ptr, ctx->host_pages.data(), (size_t)m * sizeof(fo_decode_page),
-                                cudaMemcpyHostToDevice, ctx->stream),
+        FO_CUDA(cudaMemcpyAsync(ctx->pages.ptr, hp, (size_t)m * sizeof(fo_decode_page), cudaMemcpyHostToDevice,
+                                ctx->stream),
                 "H2D(pages)");
+        FO_CUDA(ctx->host_pages.uploaded(slot, ctx->stream), "cudaEventRecord");
         cudaError_t e = fo_launch_decode_batch((const fo_decode_page *)ctx->pages.ptr, m, c0->format, c0->groups,
                                                c0->fast_exp, max_splits, 1, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "decode batch launch");
-        // The descriptor copy reads host memory the next chunk overwrites.
-        FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    }
+    return FO_OK;
+}
+
+int fo_i8_destroy(fo_i8_cache *c) {
+    if (!c) return FO_OK;
+    DeviceGuard guard(c->ctx->device);
+    cudaStreamSynchronize(c->ctx->stream);
+    void *ptrs[] = {c->k_codes, c->v_codes, c->k_scales, c->v_scales, c->part_o, c->part_ml};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    delete c;
+    return FO_OK;
+}
+
+int fo_i8_seal(fo_ctx *ctx, const float *k, const float *v, int64_t len, int64_t n_heads, int mem,
+               fo_i8_cache **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_i8_seal: null output pointer");
+    *out = nullptr;
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    if (!k || !v) return fail(FO_ERR_INVALID, "fo_i8_seal: null keys or values");
+    if (!(len >= 1 && n_heads >= 1)) return fail(FO_ERR_INVALID, "fo_i8_seal: length and heads must be positive");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    DeviceGuard guard(ctx->device);
+    fo_i8_cache *c = new fo_i8_cache();
+    c->ctx = ctx;
+    c->len = len;
+    c->heads = n_heads;
+    c->splits = (len + FO_I8_SPLIT - 1) / FO_I8_SPLIT;
+    const int64_t groups = (len + 63) / 64;
+    const size_t n = (size_t)len * n_heads * 64;
+    cudaError_t e = cudaSuccess;
+    auto alloc = [&](void **p, size_t bytes) {
+        if (e == cudaSuccess) e = cudaMalloc(p, bytes);
+    };
+    alloc((void **)&c->k_codes, n);
+    alloc((void **)&c->v_codes, n);
+    alloc((void **)&c->k_scales, (size_t)n_heads * groups * 4);
+    alloc((void **)&c->v_scales, (size_t)n_heads * groups * 4);
+    alloc((void **)&c->part_o, (size_t)n_heads * c->splits * 64 * 4);
+    alloc((void **)&c->part_ml, (size_t)n_heads * c->splits * 2 * 4);
+    if (e != cudaSuccess) {
+        fo_i8_destroy(c);
+        return cuda_fail(e, "fo_i8_seal: cudaMalloc");
+    }
+    c->bytes = 2 * n + 2 * (size_t)n_heads * groups * 4;
+    const float *dk = k, *dv = v;
+    if (mem == FO_MEM_HOST) {
+        e = ctx->stage[1].ensure(n * 4);
+        if (e == cudaSuccess) e = ctx->stage[3].ensure(n * 4);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(ctx->stage[1].ptr, k, n * 4, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(ctx->stage[3].ptr, v, n * 4, cudaMemcpyHostToDevice, ctx->stream);
+        dk = (const float *)ctx->stage[1].ptr;
+        dv = (const float *)ctx->stage[3].ptr;
+    }
+    if (e == cudaSuccess) e = fo_launch_quantize_i8(dk, len, n_heads, c->k_codes, c->k_scales, ctx->stream);
+    if (e == cudaSuccess) e = fo_launch_quantize_i8(dv, len, n_heads, c->v_codes, c->v_scales, ctx->stream);
+    if (e == cudaSuccess && mem == FO_MEM_HOST) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        fo_i8_destroy(c);
+        return cuda_fail(e, "fo_i8_seal");
+    }
+    *out = c;
+    return FO_OK;
+}
+
+int64_t fo_i8_bytes(const fo_i8_cache *c) { return c ? (int64_t)c->bytes : -1; }
+
+int fo_i8_records(const fo_i8_cache *c, const int8_t **k_codes, const float **k_scales, const int8_t **v_codes,
+                  const float **v_scales) {
+    if (!c) return fail(FO_ERR_INVALID, "null cache");
+    if (k_codes) *k_codes = c->k_codes;
+    if (k_scales) *k_scales = c->k_scales;
+    if (v_codes) *v_codes = c->v_codes;
+    if (v_scales) *v_scales = c->v_scales;
+    return FO_OK;
+}
+
+int fo_i8_decode_batch(fo_i8_cache *const *caches, int64_t n, const float *const *q, const float *const *sinks,
+                       float *const *output, int32_t fast_exp) {
+    if (!caches || !q || !sinks || !output || n < 0) return fail(FO_ERR_INVALID, "i8 decode batch: null argument");
+    if (n == 0) return FO_OK;
+    fo_ctx *ctx = caches[0] ? caches[0]->ctx : nullptr;
+    if (!ctx) return fail(FO_ERR_INVALID, "i8 decode batch: null cache");
+    const int64_t heads = caches[0]->heads;
+    for (int64_t i = 0; i < n; i++) {
+        const fo_i8_cache *c = caches[i];
+        if (!c || !q[i] || !sinks[i] || !output[i])
+            return fail(FO_ERR_INVALID, "i8 decode batch: null entry %lld", (long long)i);
+        if (c->ctx != ctx || c->heads != heads)
+            return fail(FO_ERR_INVALID, "i8 decode batch: caches must share context and heads");
+        if (!aligned16(q[i])) return fail(FO_ERR_INVALID, "i8 decode batch: queries must be 16-byte aligned");
+    }
+    {  // each page's partials belong to its cache: pages must be distinct caches
+        std::vector<const fo_i8_cache *> seen(caches, caches + n);
+        std::sort(seen.begin(), seen.end());
+        if (std::adjacent_find(seen.begin(), seen.end()) != seen.end())
+            return fail(FO_ERR_INVALID, "i8 decode batch: a cache appears twice");
+    }
+    DeviceGuard guard(ctx->device);
+    for (int64_t base = 0; base < n; base += FO_BATCH_PAGES) {
+        const int64_t m = std::min<int64_t>(FO_BATCH_PAGES, n - base);
+        int slot = 0;
+        fo_i8_page *hp = static_cast<fo_i8_page *>(ctx->host_i8_pages.acquire(slot));
+        int32_t max_splits = 1;
+        for (int64_t i = 0; i < m; i++) {
+            const fo_i8_cache *c = caches[base + i];
+            hp[i] = fo_i8_page{c->k_codes, c->v_codes, c->k_scales,  c->v_scales, q[base + i], sinks[base + i],
+                               output[base + i], c->part_o, c->part_ml, ctx->dev_err, c->len, (int32_t)c->splits};
+            max_splits = std::max<int32_t>(max_splits, (int32_t)c->splits);
+        }
+        FO_CUDA(cudaMemcpyAsync(ctx->i8_pages.ptr, hp, (size_t)m * sizeof(fo_i8_page), cudaMemcpyHostToDevice,
+                                ctx->stream),
+                "H2D(i8 pages)");
+        FO_CUDA(ctx->host_i8_pages.uploaded(slot, ctx->stream), "cudaEventRecord");
+        cudaError_t e = fo_launch_decode_i8((const fo_i8_page *)ctx->i8_pages.ptr, m, heads, max_splits, fast_exp,
+                                            ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "i8 decode launch");
     }
     return FO_OK;
 }

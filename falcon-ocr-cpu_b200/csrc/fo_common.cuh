@@ -78,6 +78,30 @@ __device__ __forceinline__ float softmax_exp(float x) {
     if constexpr (FAST) return exp_poly(x); else return expf(x);
 }
 
+// Exact integer codes as floats without the conversion unit (which runs at
+// a fraction of the FMA rate): a code c, offset to be non-negative, is
+// placed in the mantissa of 2^23 (byte permute) and 2^23 plus the offset is
+// subtracted; every step is exact.
+// The four signed bytes of w.
+__device__ __forceinline__ void s8x4_f32(uint32_t w, float *out) {
+    const uint32_t u = w ^ 0x80808080u;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        out[j] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + j)), 8388736.0f);
+}
+// The two signed bytes in the low half of w (as a 16-bit load returns them).
+__device__ __forceinline__ void s8x2_f32(uint32_t w, float &lo, float &hi) {
+    const uint32_t u = w ^ 0x8080u;
+    lo = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)), 8388736.0f);
+    hi = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u)), 8388736.0f);
+}
+// The two signed 16-bit halves of w.
+__device__ __forceinline__ void s16x2_f32(uint32_t w, float &lo, float &hi) {
+    const uint32_t u = w ^ 0x80008000u;
+    lo = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7510u)), 8421376.0f);
+    hi = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7532u)), 8421376.0f);
+}
+
 // Rust f32::max: the non-NaN operand when one is NaN (fmaxf semantics).
 __device__ __forceinline__ float rmax(float a, float b) { return fmaxf(a, b); }
 

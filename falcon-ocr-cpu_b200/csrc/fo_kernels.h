@@ -70,6 +70,27 @@ cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t
 cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format, int64_t groups,
                                    int fast_exp, int64_t max_splits, int max_rows, cudaStream_t stream);
 
+// One page of BASELINE's INT8 KV format (decode_i8.cu): codes
+// [heads][len][64], FP32 scales [heads][ceil(len / 64)], for keys and values.
+struct fo_i8_page {
+    const int8_t *k_codes, *v_codes;
+    const float *k_scales, *v_scales;
+    const float *q;      // [heads][64]
+    const float *sinks;  // [heads]
+    float *out;          // [heads][64]
+    float *part_o;       // [heads][splits][64]
+    float *part_ml;      // [heads][splits][2]
+    unsigned *err;       // error word for bounded waits that gave up (may be null)
+    int64_t len;
+    int32_t splits;      // ceil(len / FO_I8_SPLIT)
+};
+#define FO_I8_SPLIT 1024
+
+cudaError_t fo_launch_quantize_i8(const float *x, int64_t len, int64_t heads, int8_t *codes, float *scales,
+                                  cudaStream_t stream);
+cudaError_t fo_launch_decode_i8(const fo_i8_page *dev_pages, int64_t n_pages, int64_t heads, int32_t max_splits,
+                                int fast_exp, cudaStream_t stream);
+
 // The bounded-wait self-test kernel (selftest.cu).
 cudaError_t fo_launch_bounded_wait(unsigned *err, unsigned long long limit_ns, cudaStream_t stream);
 

@@ -93,7 +93,8 @@ EXPORTS = [
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
     "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch", "fo_selftest_bounded_wait",
-    "fo_attention_prefill_bf16_rows",
+    "fo_attention_prefill_bf16_rows", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
+    "fo_i8_decode_batch",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -135,6 +136,11 @@ def lib() -> ctypes.CDLL:
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
         "fo_attention_prefill_bf16_rows": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64, PrefillOptions]),
+        "fo_i8_seal": (I, [P, P, P, I64, I64, I, ctypes.POINTER(P)]),
+        "fo_i8_destroy": (I, [P]),
+        "fo_i8_bytes": (I64, [P]),
+        "fo_i8_records": (I, [P, PP, PP, PP, PP]),
+        "fo_i8_decode_batch": (I, [PP, I64, PP, PP, PP, I32]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -365,6 +371,50 @@ def decode_batch(caches: Sequence[SplitPrefix], qs, sinks, outputs):
     check(lib().fo_kv_attention_decode_batch(arr([c.handle.value for c in caches]), n, arr([q.data_ptr() for q in qs]),
                                              arr([s.data_ptr() for s in sinks]),
                                              arr([o.data_ptr() for o in outputs])))
+
+
+class Int8Cache:
+    """BASELINE config 4's INT8 KV format on the device (fo_i8_seal): keys
+    and values [len][heads][64] quantized per (head, 64-position group)."""
+
+    def __init__(self, k, v, heads=16, ctx=None):
+        ctx = ctx or default_context()
+        k, v = _f32(k), _f32(v)
+        (pk, pv), mem = _ptr_mem([k, v])
+        n = k.numel() if _is_torch(k) else k.size
+        self.len, self.heads, self.ctx = n // (heads * 64), heads, ctx
+        h = ctypes.c_void_p()
+        check(lib().fo_i8_seal(ctx.handle, pk, pv, self.len, heads, mem, ctypes.byref(h)))
+        self.handle = h
+
+    def bytes(self) -> int:
+        return lib().fo_i8_bytes(self.handle)
+
+    def records(self):
+        """Device pointers (k_codes, k_scales, v_codes, v_scales)."""
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        check(lib().fo_i8_records(self.handle, *[ctypes.byref(p) for p in ptrs]))
+        return tuple(p.value for p in ptrs)
+
+    def close(self):
+        if self.handle:
+            lib().fo_i8_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def int8_decode_batch(caches: Sequence[Int8Cache], qs, sinks, outputs, fast_exp=False):
+    """One decode row per page in one launch (CUDA tensors)."""
+    n = len(caches)
+    arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
+    check(lib().fo_i8_decode_batch(arr([c.handle.value for c in caches]), n, arr([q.data_ptr() for q in qs]),
+                                   arr([s.data_ptr() for s in sinks]), arr([o.data_ptr() for o in outputs]),
+                                   int(bool(fast_exp))))
 
 
 def decode_rows_static_scratch(cache: SplitPrefix, fmt, q, rows, sinks, output, fast_exp=False, stream=None):

@@ -224,6 +224,26 @@ int fo_decode_rows_static_scratch(const void *codes, const uint16_t *scales, con
                                   int64_t n_kv_heads, const float *q, int64_t rows, const float *sinks,
                                   int32_t fast_exp, float *output, void *stream);
 
+/* BASELINE config 4's INT8 KV format (no counterpart in the reference,
+ * whose INT8 KV is the Q8 record format above): keys and values of every head
+ * stored apart as int8 codes [n_heads][len][64] with one FP32 scale per
+ * (head, 64-position group) each; code = round-to-nearest-even(x / scale)
+ * clamped to [-127, 127], scale = max |x| of the group / 127.  k and v are
+ * [len][n_heads][64] FP32 (host or device per `mem`). */
+typedef struct fo_i8_cache fo_i8_cache;
+int fo_i8_seal(fo_ctx *ctx, const float *k, const float *v, int64_t len, int64_t n_heads, int mem,
+               fo_i8_cache **out);
+int fo_i8_destroy(fo_i8_cache *cache);
+int64_t fo_i8_bytes(const fo_i8_cache *cache);
+/* Device pointers to the cache's codes and scales (for tests and tools). */
+int fo_i8_records(const fo_i8_cache *cache, const int8_t **k_codes, const float **k_scales, const int8_t **v_codes,
+                  const float **v_scales);
+/* One decode row per page, all pages in one launch: q[i] [n_heads][64],
+ * sinks[i] [n_heads], output[i] [n_heads][64], device pointers; every head
+ * attends over all len positions of its page. */
+int fo_i8_decode_batch(fo_i8_cache *const *caches, int64_t n, const float *const *q, const float *const *sinks,
+                       float *const *output, int32_t fast_exp);
+
 #ifdef __cplusplus
 }
 #endif

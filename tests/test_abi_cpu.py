@@ -124,5 +124,8 @@ def test_null_handles_are_rejected():
     assert L.fo_kv_tail_len(None) == -1 and L.fo_kv_bytes(None) == -1
     assert L.fo_ctx_destroy(None) == F.OK and L.fo_kv_destroy(None) == F.OK
     assert L.fo_selftest_bounded_wait(None, 1000) == F.ERR_INVALID
+    assert L.fo_i8_seal(None, None, None, 1, 16, F.MEM_HOST, ctypes.byref(ctypes.c_void_p())) == F.ERR_INVALID
+    assert L.fo_i8_decode_batch(None, 1, None, None, None, 0) == F.ERR_INVALID
+    assert L.fo_i8_bytes(None) == -1 and L.fo_i8_destroy(None) == F.OK
     h = ctypes.c_void_p()
     assert L.fo_ctx_create(-1, None, ctypes.byref(h)) != F.OK
