@@ -287,7 +287,10 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
         }
     } else {
         // ------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        // The whole warp runs the loop and its waits, so descriptors and
+        // addresses stay warp-uniform (uniform registers); one elected lane
+        // issues each group of MMAs and its commits.
+        {
             const uint32_t idS = idesc_bf16(128, 128, 0), idPV = idesc_bf16(128, 64, 1);
             // Descriptors are built once; a K step or stage only moves the
             // start-address field (16-byte units, no carry below 256 KB).
@@ -297,54 +300,64 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             auto issue_s = [&](int t, int st) {
                 const uint64_t a = dQ + t * TILE16, b = dK + st * TILE16;
                 const uint32_t d = tmem + 128 * t;
-                mma_bf16(d, a, b, idS, 0);
+                if (elect_one()) {
+                    mma_bf16(d, a, b, idS, 0);
 #pragma unroll
-                for (int kk = 1; kk < 4; kk++) mma_bf16(d, a + 2 * kk, b + 2 * kk, idS, 1);
+                    for (int kk = 1; kk < 4; kk++) mma_bf16(d, a + 2 * kk, b + 2 * kk, idS, 1);
+                    mma_commit(s_full + t);
+                }
+                __syncwarp();
             };
             auto issue_pv = [&](int t, int st, int j) {
                 const uint32_t a = tmem + 384 + 64 * t;  // P_t: 8 columns per 16 keys
                 const uint64_t b = dV + st * TILE16;
                 const uint32_t d = tmem + 256 + 64 * t;
-                mma_bf16_ts(d, a, b, idPV, j > 0);
+                if (elect_one()) {
+                    mma_bf16_ts(d, a, b, idPV, j > 0);
 #pragma unroll
-                for (int kk = 1; kk < 8; kk++) mma_bf16_ts(d, a + 8 * kk, b + kk * (2048 >> 4), idPV, 1);
+                    for (int kk = 1; kk < 8; kk++) mma_bf16_ts(d, a + 8 * kk, b + kk * (2048 >> 4), idPV, 1);
+                    mma_commit(p_empty + t);
+                }
+                __syncwarp();
+            };
+            auto commit = [&](uint64_t *bar) {
+                if (elect_one()) mma_commit(bar);
+                __syncwarp();
             };
             bool ok = mbar_wait(q_full, 0, abort_flag, a.err) && mbar_wait(k_full, 0, abort_flag, a.err);
+            ok = __all_sync(0xffffffffu, ok);
             if (ok) {
                 tc_fence_after();
                 issue_s(0, 0);
-                mma_commit(s_full + 0);
                 issue_s(1, 0);
-                mma_commit(s_full + 1);
-                mma_commit(k_empty + 0);
+                commit(k_empty + 0);
             }
             for (int j = 0; j < nkv && ok; j++) {
                 if (j + 1 < nkv) {
                     const int st1 = (j + 1) % BT_STAGES, u1 = (j + 1) / BT_STAGES;
-                    if (!(ok = mbar_wait(k_full + st1, u1 & 1, abort_flag, a.err))) break;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(k_full + st1, u1 & 1, abort_flag, a.err)))) break;
                     for (int t = 0; t < 2 && ok; t++) {
-                        if (!(ok = mbar_wait(s_empty + t, j & 1, abort_flag, a.err))) break;
+                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_empty + t, j & 1, abort_flag, a.err)))) break;
                         tc_fence_after();
                         issue_s(t, st1);
-                        mma_commit(s_full + t);
                     }
                     if (!ok) break;
-                    mma_commit(k_empty + st1);
+                    commit(k_empty + st1);
                 }
                 const int st = j % BT_STAGES, u = j / BT_STAGES;
-                if (!(ok = mbar_wait(v_full + st, u & 1, abort_flag, a.err))) break;
+                if (!(ok = __all_sync(0xffffffffu, mbar_wait(v_full + st, u & 1, abort_flag, a.err)))) break;
                 for (int t = 0; t < 2 && ok; t++) {
-                    if (!(ok = mbar_wait(p_full + t, j & 1, abort_flag, a.err))) break;
+                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(p_full + t, j & 1, abort_flag, a.err)))) break;
                     tc_fence_after();
                     issue_pv(t, st, j);
-                    mma_commit(p_empty + t);
                 }
                 if (!ok) break;
-                mma_commit(v_empty + st);
+                commit(v_empty + st);
             }
             // Every issued MMA completes before TMEM is released.
-            mma_commit(mma_done);
-            drain_wait(mma_done, 0);
+            commit(mma_done);
+            if (lane == 0) drain_wait(mma_done, 0);
+            __syncwarp();
         }
     }
     tc_fence_before();

@@ -101,6 +101,18 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t phase) {
     }
 }
 
+// One lane of the (fully active) warp, the same one on every call in a
+// converged warp: the lane that issues a warp's single-thread operations.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // --------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
