@@ -166,47 +166,60 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             tc_fence_before();
             mbar_arrive(s_empty + t);
             const int nvis = (int)max64(0, min64(128, vend - 128 * (int64_t)j));
-            float shift = 0.0f, factor = 1.0f;
+            // Whole tile visible for every row of the warp: the common case
+            // runs without any per-key mask (a separate copy of the loop).
+            const bool full = __all_sync(0xffffffffu, nvis >= 128);
+            // Scaled scores, two at a time: t = s * (scale * log2 e).
+            float2 tt[64];
+#pragma unroll
+            for (int i = 0; i < 64; i++)
+                tt[i] = __fmul2_rn(make_float2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])),
+                                   make_float2(C, C));
+            float factor = 1.0f;
             if constexpr (!STATIC) {
                 float bm = -INFINITY;
+                if (full) {
 #pragma unroll
-                for (int c = 0; c < 128; c++)
-                    if (c < nvis) bm = fmaxf(bm, __uint_as_float(s[c]) * C);
+                    for (int i = 0; i < 64; i++) bm = fmaxf(bm, fmaxf(tt[i].x, tt[i].y));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; i++) {
+                        if (2 * i < nvis) bm = fmaxf(bm, tt[i].x);
+                        if (2 * i + 1 < nvis) bm = fmaxf(bm, tt[i].y);
+                    }
+                }
                 if (bm > m2) {  // also true on the first visible tile
                     if (m2 != -INFINITY) factor = ex2(m2 - bm);
                     m2 = bm;
                 }
-                shift = m2 == -INFINITY ? 0.0f : m2;
+                const float shift = m2 == -INFINITY ? 0.0f : m2;
+#pragma unroll
+                for (int i = 0; i < 64; i++) tt[i] = __fadd2_rn(tt[i], make_float2(-shift, -shift));
                 l *= factor;
             }
-            // The probabilities first, packed to BF16 pairs in registers, so
-            // this overlaps PV_t(j-1), which still reads the P tile.
-            // Whole tile visible for every row of the warp: no per-key mask.
-            const bool full = __all_sync(0xffffffffu, nvis >= 128);
-            float lsum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            // The probabilities, packed to BF16 pairs in registers, so this
+            // overlaps PV_t(j-1), which still reads the P tile.  The static
+            // shift sums the rounded probabilities PV multiplies; the online
+            // softmax sums the unrounded ones.
+            float2 ls[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
             uint32_t pk[64];
-#pragma unroll
-            for (int i = 0; i < 64; i++) {
-                const int c = 2 * i;
-                float x0, x1;
-                const float t0 = STATIC ? __uint_as_float(s[c]) * C : __uint_as_float(s[c]) * C - shift;
-                const float t1 = STATIC ? __uint_as_float(s[c + 1]) * C : __uint_as_float(s[c + 1]) * C - shift;
-                x0 = ex2(t0);
-                x1 = ex2(t1);
-                if (!full) {
-                    x0 = c < nvis ? x0 : 0.0f;
-                    x1 = c + 1 < nvis ? x1 : 0.0f;
-                }
+            auto pair = [&](int i, float x0, float x1) {
                 pk[i] = pack_bf16(x0, x1);
-                if constexpr (STATIC) {  // the static shift sums the rounded probabilities PV multiplies
-                    lsum[i & 3] += __uint_as_float(pk[i] << 16);
-                    lsum[i & 3] += __uint_as_float(pk[i] & 0xFFFF0000u);
-                } else {  // the online softmax sums the unrounded probabilities
-                    lsum[i & 3] += x0;
-                    lsum[i & 3] += x1;
-                }
+                if constexpr (STATIC)
+                    ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(__uint_as_float(pk[i] << 16),
+                                                                  __uint_as_float(pk[i] & 0xFFFF0000u)));
+                else
+                    ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(x0, x1));
+            };
+            if (full) {
+#pragma unroll
+                for (int i = 0; i < 64; i++) pair(i, ex2(tt[i].x), ex2(tt[i].y));
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; i++)
+                    pair(i, 2 * i < nvis ? ex2(tt[i].x) : 0.0f, 2 * i + 1 < nvis ? ex2(tt[i].y) : 0.0f);
             }
-            l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+            l += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
             // P_t is free once PV_t(j-1) has completed.
             if (j > 0) {
                 ok = __all_sync(0xffffffffu, mbar_wait(p_empty + t, (j - 1) & 1, abort_flag, a.err));
