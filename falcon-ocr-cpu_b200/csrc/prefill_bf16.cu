@@ -212,8 +212,17 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                     ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(x0, x1));
             };
             if (full) {
+                // 3 of every 16 exponentials run on the FMA pipes (ex2_poly),
+                // the rest on the SFU, which would otherwise bound the loop.
 #pragma unroll
-                for (int i = 0; i < 64; i++) pair(i, ex2(tt[i].x), ex2(tt[i].y));
+                for (int i = 0; i < 64; i++) {
+                    if ((i & 7) == 3 || (i & 7) == 6)
+                        pair(i, ex2(tt[i].x), ex2_poly(tt[i].y));
+                    else if ((i & 7) == 7)
+                        pair(i, ex2_poly(tt[i].x), ex2_poly(tt[i].y));
+                    else
+                        pair(i, ex2(tt[i].x), ex2(tt[i].y));
+                }
             } else {
 #pragma unroll
                 for (int i = 0; i < 64; i++)

@@ -207,6 +207,23 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^t on the FMA and integer pipes (no SFU): the reference's own degree-3
+// polynomial for 2^f on [-0.5, 0.5] with n = round(t) (its static-shift exp2,
+// src/kernels/attention/prefill64/bf16/static_shift.rs:36-38, 322-336;
+// relative error at most 7.5e-5), the same FMA order, n taken with the
+// 1.5 * 2^23 rounding constant and added to the exponent field.  Valid for t <= 127 (t below -127 is
+// clamped there and gives a value below 2^-126); the prefill's static shift
+// requires |scores| < 80, so t < 116.
+__device__ __forceinline__ float ex2_poly(float t) {
+    t = fmaxf(t, -127.0f);
+    const float j = __fadd_rn(t, 12582912.0f);
+    const float f = __fsub_rn(t, __fsub_rn(j, 12582912.0f));
+    float p = __fmaf_rn(0.05517167f, f, 0.24261113f);
+    p = __fmaf_rn(p, f, 0.69326097f);
+    p = __fmaf_rn(p, f, 0.99992806f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
 // Two floats to packed BF16 (round to nearest even): hi in the upper half.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     uint32_t r;
