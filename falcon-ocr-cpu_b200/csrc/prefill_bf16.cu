@@ -354,27 +354,58 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                 issue_s(1, 0);
                 commit(k_empty + 0);
             }
-            for (int j = 0; j < nkv && ok; j++) {
-                if (j + 1 < nkv) {
-                    const int st1 = (j + 1) % BT_STAGES, u1 = (j + 1) / BT_STAGES;
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(k_full + st1, u1 & 1, abort_flag, a.err)))) break;
-                    for (int t = 0; t < 2 && ok; t++) {
-                        if (!(ok = __all_sync(0xffffffffu, mbar_wait(s_empty + t, j & 1, abort_flag, a.err)))) break;
-                        tc_fence_after();
-                        issue_s(t, st1);
+            // Issue order: S_t(j) and PV_t(j) in increasing j for each tile t,
+            // but the two tiles do not wait for each other: the warp polls
+            // every pending operation's barriers and issues whichever is
+            // ready (S_t(j + 1) needs K(j + 1) and the softmax's load of
+            // S_t(j); PV_t(j) needs V(j) and P_t(j)).  A K (V) stage is
+            // released once both tiles' S (PV) have been issued from it.
+            int ns[2] = {1, 1}, np[2] = {0, 0};  // next S and PV index per tile
+            uint64_t t_last = globaltimer();
+            while (ok && (np[0] < nkv || np[1] < nkv)) {
+                bool progress = false;
+#pragma unroll
+                for (int t = 0; t < 2; t++) {
+                    const int js = ns[t];
+                    if (js < nkv) {
+                        const int st = js % BT_STAGES;
+                        bool ready = mbar_try_wait(k_full + st, (js / BT_STAGES) & 1) &&
+                                     mbar_try_wait(s_empty + t, (js - 1) & 1);
+                        ready = __shfl_sync(0xffffffffu, ready, 0);
+                        if (ready) {
+                            tc_fence_after();
+                            issue_s(t, st);
+                            ns[t] = js + 1;
+                            if (ns[t ^ 1] > js) commit(k_empty + st);  // both tiles are done with K(js)
+                            progress = true;
+                        }
                     }
-                    if (!ok) break;
-                    commit(k_empty + st1);
+                    const int jp = np[t];
+                    if (jp < nkv && jp < ns[t]) {
+                        const int st = jp % BT_STAGES;
+                        bool ready = mbar_try_wait(v_full + st, (jp / BT_STAGES) & 1) &&
+                                     mbar_try_wait(p_full + t, jp & 1);
+                        ready = __shfl_sync(0xffffffffu, ready, 0);
+                        if (ready) {
+                            tc_fence_after();
+                            issue_pv(t, st, jp);
+                            np[t] = jp + 1;
+                            if (np[t ^ 1] > jp) commit(v_empty + st);  // both tiles are done with V(jp)
+                            progress = true;
+                        }
+                    }
                 }
-                const int st = j % BT_STAGES, u = j / BT_STAGES;
-                if (!(ok = __all_sync(0xffffffffu, mbar_wait(v_full + st, u & 1, abort_flag, a.err)))) break;
-                for (int t = 0; t < 2 && ok; t++) {
-                    if (!(ok = __all_sync(0xffffffffu, mbar_wait(p_full + t, j & 1, abort_flag, a.err)))) break;
-                    tc_fence_after();
-                    issue_pv(t, st, j);
+                if (progress) {
+                    t_last = globaltimer();
+                } else if (globaltimer() - t_last > FO_WAIT_NS || *abort_flag) {
+                    // Nothing became ready within the bound: unwind.
+                    if (lane == 0 && !*abort_flag) {
+                        *abort_flag = 1;
+                        if (a.err) atomicOr(a.err, FO_DEVERR_WAIT_TIMEOUT);
+                    }
+                    ok = false;
                 }
-                if (!ok) break;
-                commit(v_empty + st);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
             }
             // Every issued MMA completes before TMEM is released.
             commit(mma_done);
