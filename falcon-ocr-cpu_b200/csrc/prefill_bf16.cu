@@ -84,8 +84,10 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t T = a.total, H = a.n_heads;
-    const int64_t pair = a.pair_end - 1 - blockIdx.x;  // heaviest (latest) tiles first
-    const int64_t head = blockIdx.y;
+    // Blocks start in index order, x fastest: every head of the heaviest
+    // (latest) query pair first, so the longest CTAs start earliest.
+    const int64_t pair = a.pair_end - 1 - blockIdx.y;
+    const int64_t head = blockIdx.x;
     const int64_t kv_head = head / (H / a.n_kv_heads);
     const int64_t q0 = pair * 256;
     // Tile span over both Q tiles (src/kernels/attention/prefill64/span.rs:9-20).
@@ -212,16 +214,16 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                     ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(x0, x1));
             };
             if (full) {
-                // 3 of every 16 exponentials run on the FMA pipes (ex2_poly),
+                // 4 of every 16 exponentials run on the FMA pipes (ex2_poly2),
                 // the rest on the SFU, which would otherwise bound the loop.
 #pragma unroll
                 for (int i = 0; i < 64; i++) {
-                    if ((i & 7) == 3 || (i & 7) == 6)
-                        pair(i, ex2(tt[i].x), ex2_poly(tt[i].y));
-                    else if ((i & 7) == 7)
-                        pair(i, ex2_poly(tt[i].x), ex2_poly(tt[i].y));
-                    else
+                    if ((i & 3) == 3) {
+                        const float2 e = ex2_poly2(tt[i]);
+                        pair(i, e.x, e.y);
+                    } else {
                         pair(i, ex2(tt[i].x), ex2(tt[i].y));
+                    }
                 }
             } else {
 #pragma unroll
@@ -460,7 +462,8 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
         return cudaErrorInvalidValue;
     const int64_t pb = query_begin / 256, pe = (query_end + 255) / 256;
     fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe};
-    dim3 grid((unsigned)(pe - pb), (unsigned)n_heads);
+    if (pe - pb > 65535) return cudaErrorInvalidValue;  // grid y limit: 16.7M query rows per launch
+    dim3 grid((unsigned)n_heads, (unsigned)(pe - pb));
     auto launch = [&](auto kernel) -> cudaError_t {
         cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fo::SMEM_BYTES);

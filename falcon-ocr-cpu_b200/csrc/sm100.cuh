@@ -207,21 +207,26 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// 2^t on the FMA and integer pipes (no SFU): the reference's own degree-3
-// polynomial for 2^f on [-0.5, 0.5] with n = round(t) (its static-shift exp2,
-// src/kernels/attention/prefill64/bf16/static_shift.rs:36-38, 322-336;
+// 2^t for two values on the FMA and integer pipes (no SFU): the reference's own
+// degree-3 polynomial for 2^f on [-0.5, 0.5] with n = round(t) (its static-shift
+// exp2, src/kernels/attention/prefill64/bf16/static_shift.rs:36-38, 322-336;
 // relative error at most 7.5e-5), the same FMA order, n taken with the
-// 1.5 * 2^23 rounding constant and added to the exponent field.  Valid for t <= 127 (t below -127 is
-// clamped there and gives a value below 2^-126); the prefill's static shift
-// requires |scores| < 80, so t < 116.
-__device__ __forceinline__ float ex2_poly(float t) {
-    t = fmaxf(t, -127.0f);
-    const float j = __fadd_rn(t, 12582912.0f);
-    const float f = __fsub_rn(t, __fsub_rn(j, 12582912.0f));
-    float p = __fmaf_rn(0.05517167f, f, 0.24261113f);
-    p = __fmaf_rn(p, f, 0.69326097f);
-    p = __fmaf_rn(p, f, 0.99992806f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+// 1.5 * 2^23 rounding constant and added to the exponent field.  Packed FP32
+// (two lanes per instruction); f = t - (j - 1.5 * 2^23) is formed as
+// t + (1.5 * 2^23 - j), the same single rounding of an exact difference.  Valid
+// for t <= 127 (t below -127 is clamped there and gives a value below 2^-126);
+// the prefill's static shift requires |scores| < 80, so t < 116.
+__device__ __forceinline__ float2 ex2_poly2(float2 t) {
+    constexpr float R = 12582912.0f;
+    t.x = fmaxf(t.x, -127.0f);
+    t.y = fmaxf(t.y, -127.0f);
+    const float2 j = __fadd2_rn(t, make_float2(R, R));
+    const float2 f = __fadd2_rn(t, __ffma2_rn(j, make_float2(-1.0f, -1.0f), make_float2(R, R)));
+    float2 p = __ffma2_rn(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261113f, 0.24261113f));
+    p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+    p = __ffma2_rn(p, f, make_float2(0.99992806f, 0.99992806f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(j.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(j.y) << 23)));
 }
 
 // Two floats to packed BF16 (round to nearest even): hi in the upper half.
