@@ -201,15 +201,16 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             }
             // The probabilities, packed to BF16 pairs in registers, so this
             // overlaps PV_t(j-1), which still reads the P tile.  The static
-            // shift sums the rounded probabilities PV multiplies; the online
-            // softmax sums the unrounded ones.
+            // shift sums the rounded probabilities PV multiplies (four
+            // running sums, even key first within a pair); the online softmax
+            // sums the unrounded ones.
             float2 ls[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+            float la[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             uint32_t pk[64];
             auto pair = [&](int i, float x0, float x1) {
                 pk[i] = pack_bf16(x0, x1);
                 if constexpr (STATIC)
-                    ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(__uint_as_float(pk[i] << 16),
-                                                                  __uint_as_float(pk[i] & 0xFFFF0000u)));
+                    la[i & 3] = add_bf16x2_f32(la[i & 3], pk[i]);
                 else
                     ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(x0, x1));
             };
@@ -230,7 +231,10 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                 for (int i = 0; i < 64; i++)
                     pair(i, 2 * i < nvis ? ex2(tt[i].x) : 0.0f, 2 * i + 1 < nvis ? ex2(tt[i].y) : 0.0f);
             }
-            l += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
+            if constexpr (STATIC)
+                l += (la[0] + la[1]) + (la[2] + la[3]);
+            else
+                l += (ls[0].x + ls[0].y) + (ls[1].x + ls[1].y);
             // P_t is free once PV_t(j-1) has completed.
             if (j > 0) {
                 ok = __all_sync(0xffffffffu, mbar_wait(p_empty + t, (j - 1) & 1, abort_flag, a.err));

@@ -229,6 +229,19 @@ __device__ __forceinline__ float2 ex2_poly2(float2 t) {
                        __int_as_float(__float_as_int(p.y) + (__float_as_int(j.y) << 23)));
 }
 
+// acc + lo + hi for a packed BF16 pair (lo = the even key, added first), each
+// BF16 widened exactly inside the add (sm_100 mixed-precision add.f32.bf16).
+__device__ __forceinline__ float add_bf16x2_f32(float acc, uint32_t pk) {
+    float r;
+    asm("{\n\t.reg .b16 lo, hi;\n\t.reg .f32 t;\n\t"
+        "mov.b32 {lo, hi}, %1;\n\t"
+        "add.rn.f32.bf16 t, lo, %2;\n\t"
+        "add.rn.f32.bf16 %0, hi, t;\n\t}"
+        : "=f"(r)
+        : "r"(pk), "f"(acc));
+    return r;
+}
+
 // Two floats to packed BF16 (round to nearest even): hi in the upper half.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     uint32_t r;
