@@ -12,7 +12,7 @@
 // FO_STATIC_POSITIONS cached positions (prefix + tail), the shapes of the
 // reference model (8 verification rows, 16 heads, a 16,384-token context);
 // larger calls are refused.  Every GPU that loads this library holds the
-// array (about 2.1 MiB) until the process exits.
+// array (about 4.1 MiB) until the process exits.
 //
 // The first call on each device looks the array's device address up
 // (cudaGetSymbolAddress, with that device current); make that first call

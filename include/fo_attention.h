@@ -213,7 +213,7 @@ int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const fl
  * device.  The caller passes the sealed records (as fo_kv_records describes
  * them), device q [rows][n_heads][64], sinks and output, and a stream (NULL
  * is the default stream); results equal fo_kv_attention_decode_rows'.  The
- * split partials live in one static device array of about 2.1 MiB that every
+ * split partials live in one static device array of about 4.1 MiB that every
  * GPU loading the library holds until exit, which limits a call to 8 rows,
  * 16 heads and 16,384 positions (FO_ERR_CAPACITY beyond).  The first call on
  * a device looks the array up and should come before any stream capture;
