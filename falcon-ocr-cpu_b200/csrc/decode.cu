@@ -6,23 +6,26 @@
 // Work items are (page, split, group): FO_SPLIT positions of one KV group,
 // for both heads of the group and every verification row, as the reference's
 // pair_rows serves them (each record is read once and every row runs over
-// it).  Persistent CTAs walk the items.  A split is cut into chunks of 64
-// keys (32 for FP32 records); one warp bulk-copies (cp.async.bulk, one
-// mbarrier per chunk) a chunk's records into shared memory, one padded slot
-// per key laid out [T 32 | S0 32 | S1 32 | V 64] (a tail record's key fills
-// both spatial halves), and two warps compute on it, one per head of the
-// pair: logits with lane = key, the reference's online softmax per row over
-// the chunk (chunk max, rescale, exp(s - max)), and O += P V with lane = two
-// output dimensions, dequantizing exactly as the reference (fl(code * scale),
-// decode.rs:151-187).  Products are accumulated with the packed FP32 FMA
-// (each half an ordinary fmaf).  Once both warps are done with a chunk, the
-// copies for the CTA's next item are issued into its slots, overlapping the
-// combine and merges.  The chunks combine, in chunk order, into the split's
-// unnormalized partial; a merge kernel, launched as a programmatic dependent,
-// combines the splits in order and applies the sink.  Rows only see their own
-// positions (row r: prefix + tail - rows + 1 + r, kv.rs:851-855) and every
-// boundary and order is absolute, so each verification row equals its
-// single-row decode bit for bit.
+// it).  Persistent CTAs of four warp pairs walk the items; a pair owns whole
+// items and streams each through two buffers of 32-key chunks.  A chunk of
+// prefix records arrives by one TMA tile copy through the cache's record
+// tensor map, whose box is wider than a record so that the out-of-bounds fill
+// pads every key's slot (consecutive keys start on different banks); a chunk
+// that reaches the tail is copied record by record (cp.async.bulk).  Slots
+// hold [T 32 | S0 32 | S1 32 | V 64] (a tail record's key fills both spatial
+// halves).  The two warps of a pair compute on a chunk, one per head: logits
+// with lane = key, the reference's online softmax per row over the chunk
+// (chunk max, rescale, exp(s - max)), and O += P V with lane = two output
+// dimensions, dequantizing exactly as the reference (fl(code * scale),
+// decode.rs:151-187) with packed FP32 FMA (each half an ordinary fmaf).  Once
+// both warps are done with a chunk, the copies two chunks ahead are issued
+// into its buffer, and the next item's records are prefetched into L2.  The
+// chunks combine, in chunk order, into the split's unnormalized partial; a
+// merge kernel, launched as a programmatic dependent, combines the splits in
+// order and applies the sink.  Rows only see their own positions (row r:
+// prefix + tail - rows + 1 + r, kv.rs:851-855) and every boundary and order
+// is absolute, so each verification row equals its single-row decode bit for
+// bit.
 #include "fo_common.cuh"
 #include "fo_kernels.h"
 #include "sm100.cuh"
