@@ -597,17 +597,34 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
     float *lk = msm + splits;                            // [splits] denominators
     float4 *part = reinterpret_cast<float4 *>(lk + splits + 4 - (2 * splits) % 4);  // [SLICES][16]
     const float *ml = pp->part_ml + row_head * splits * 2;
-    const int t = threadIdx.x;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    __shared__ float wred[2][MERGE_THREADS / 32];
+    // Row maximum over the splits: per thread, then per warp, then over the
+    // warps (a maximum does not depend on the order).
+    float m = -INFINITY;
     for (int k = t; k < n; k += MERGE_THREADS) {
         const float2 x = __ldcg(reinterpret_cast<const float2 *>(ml) + k);
         fk[k] = x.x;
         lk[k] = x.y;
+        m = rmax(m, x.x);
     }
+    m = warp_max(m);
+    if (lane == 0) wred[0][warp] = m;
     __syncthreads();
-    float m = -INFINITY;
-    for (int k = 0; k < n; k++) m = rmax(m, fk[k]);
-    __syncthreads();
-    for (int k = t; k < n; k += MERGE_THREADS) fk[k] = fk[k] == -INFINITY ? -1.0f : expf(fk[k] - m);
+#pragma unroll
+    for (int w = 0; w < MERGE_THREADS / 32; w++) m = rmax(m, wred[0][w]);
+    // Split factors exp(m_k - M) (-1 marks an empty split) and the
+    // denominator: per thread over its splits, a butterfly per warp, then
+    // the warps in order, so every call sums in the same order.
+    float den = 0.0f;
+    for (int k = t; k < n; k += MERGE_THREADS) {
+        const float f = fk[k] == -INFINITY ? -1.0f : expf(fk[k] - m);
+        fk[k] = f;
+        if (f >= 0.0f) den = fmaf(lk[k], f, den);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
+    if (lane == 0) wred[1][warp] = den;
     __syncthreads();
     const int dq = t % (FO_HD / 4), sl = t / (FO_HD / 4);
     const float4 *po = reinterpret_cast<const float4 *>(pp->part_o + row_head * splits * FO_HD) + dq;
@@ -633,9 +650,9 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
     part[sl * (FO_HD / 4) + dq] = acc;
     __syncthreads();
     if (t < FO_HD) {
-        float den = 0.0f;
-        for (int j = 0; j < n; j++)
-            if (fk[j] >= 0.0f) den = fmaf(lk[j], fk[j], den);
+        den = 0.0f;
+#pragma unroll
+        for (int w = 0; w < MERGE_THREADS / 32; w++) den = __fadd_rn(den, wred[1][w]);
         const float *pf = reinterpret_cast<const float *>(part);
         float o = 0.0f;
 #pragma unroll
@@ -687,17 +704,21 @@ bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t
 }
 
 // The merge kernel, as a programmatic dependent of the decode kernel just
-// launched on `stream`.
+// launched on `stream`.  Its dynamic shared memory (2 floats per split plus
+// the slice sums) stays below 200 KB up to 25,000 splits (3.2M positions).
+constexpr int MERGE_DSMEM_MAX = 200 * 1024;
 static cudaError_t launch_merge(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
                                 int64_t groups, int max_splits, int rows, cudaStream_t stream) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(fo::merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        // The kernel's own static array sits beside the dynamic allowance.
+        cudaError_t e =
+            cudaFuncSetAttribute(fo::merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_DSMEM_MAX);
         if (e != cudaSuccess) return e;
         configured = true;
     }
     const size_t smem = (size_t)(2 * max_splits + 4 + fo::MERGE_SLICES * FO_HD) * sizeof(float);
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    if (smem > MERGE_DSMEM_MAX) return cudaErrorInvalidValue;
     const int64_t H = 2 * groups;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(rows * H), (unsigned)n_pages);

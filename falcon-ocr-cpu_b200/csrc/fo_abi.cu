@@ -491,6 +491,8 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
     if (!(head_dim == 64 && n_heads == 2 * n_kv_heads && n_kv_heads >= 1 && n_kv_heads <= 8))
         return fail(FO_ERR_INVALID, "split cache requires Falcon 64-wide paired GQA heads");
     if (!(prefix_len > 0 && capacity >= prefix_len)) return fail(FO_ERR_CAPACITY, "invalid split-prefix capacity");
+    // The split merge keeps two floats per split in shared memory.
+    if (capacity > (int64_t)3000000) return fail(FO_ERR_CAPACITY, "split-prefix capacity above 3,000,000 positions");
     if (format < FO_KV_F32 || format > FO_KV_BF16) return fail(FO_ERR_INVALID, "unknown split-cache format %d", format);
     if (!k || !v) return fail(FO_ERR_INVALID, "split prefix key/value pointer is null");
     if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");

@@ -51,7 +51,7 @@ typedef enum {
     FO_ERR_PAIR = 2,        /* temporal keys differ inside a GQA pair (kv.rs:266-278) */
     FO_ERR_NONFINITE = 3,   /* non-finite value in a sealed prefix (kv.rs:288) */
     FO_ERR_OVERFLOW = 4,    /* Q8/Q16 code * scale overflowed (kv.rs:328, 355) */
-    FO_ERR_CAPACITY = 5,    /* prefix_len == 0, capacity < prefix_len, or tail full */
+    FO_ERR_CAPACITY = 5,    /* prefix_len == 0, capacity < prefix_len or above 3,000,000, or tail full */
     FO_ERR_CUDA = 6,        /* a CUDA runtime call failed; see fo_last_error() */
     FO_ERR_DECLINED = 7     /* shape outside a kernel's scope; nothing written */
 } fo_status;
