@@ -393,7 +393,7 @@ def time_sharded(run, args):
     kd = torch.from_numpy(k.reshape(T, HEADS, 64)).to(run.dev)
     vd = torch.from_numpy(v.reshape(T, KV_HEADS, 64)).to(run.dev)
     sd = torch.from_numpy(sinks).to(run.dev)
-    sp = S.ShardedPrefill(qd, kd, vd, sd, geo, HEADS, KV_HEADS, run.rank, run.world, n_bands=4)
+    sp = S.ShardedPrefill(qd, kd, vd, sd, geo, HEADS, KV_HEADS, run.rank, run.world, n_bands=args.bands)
     for _ in range(max(args.warmup, 3)):
         sp.run()
     steps = max(3, min(args.steps, 20))
@@ -538,6 +538,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--bands", type=int, default=1,
+                    help="query-row bands of the sharded prefill (C5b); one band measured fastest at 2 ranks")
     ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded"], default="full",
                     help="full: the contract line; prefill/decode: only that part (profiling runs)")
     args = ap.parse_args()

@@ -7,7 +7,10 @@ traffic while it computes; each rank reads only its own heads' Q, K and V)
 and the outputs meet in one all-gather.  The output is produced in bands of
 query rows so that the gather of a finished band overlaps the computation of
 the next: each band's kernel runs on the compute stream, and its all-gather is
-issued on a separate stream that waits for that band's event.  Each band
+issued on a separate stream that waits for that band's event.  Bands run
+latest rows first: under a causal or prefix-LM mask later rows see more keys,
+so the heavy band computes while nothing waits on it and the light band last
+leaves the shortest gather exposed.  Each band
 gathers into its own rank-major buffer ``[world][rows][heads_per_rank][64]``
 (every rank's block contiguous, so the gather needs neither packing nor a
 copy afterwards); ``token_major`` assembles ``[T][H][64]`` for a consumer
@@ -125,7 +128,8 @@ class ShardedPrefill:
         current stream on return)."""
         kwargs = {"ctx": self.ctx} if self.compute is cuda_band else {}
         if not self.cuda:
-            for i, (b, e) in enumerate(self.bands):
+            for i in reversed(range(len(self.bands))):
+                b, e = self.bands[i]
                 self.compute(self.q, self.kb, self.vb, self.sinks, self.geometry, self.heads, self.groups, b, e,
                              self.out, **kwargs)
                 self.out_lp[b:e].copy_(self.out[b:e])
@@ -133,7 +137,8 @@ class ShardedPrefill:
             return self.gathered
         caller = torch.cuda.current_stream(self.q.device)
         self.compute_stream.wait_stream(caller)
-        for i, (b, e) in enumerate(self.bands):
+        for i in reversed(range(len(self.bands))):
+            b, e = self.bands[i]
             with torch.cuda.stream(self.compute_stream):
                 self.compute(self.q, self.kb, self.vb, self.sinks, self.geometry, self.heads, self.groups, b, e,
                              self.out, **kwargs)
