@@ -144,6 +144,9 @@ struct fo_ctx {
     HostDesc host_i8_pages;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
+    // Host-buffer prefill pipeline: copy streams and per-band events.
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    std::vector<cudaEvent_t> band_ev;
 };
 
 struct fo_kv_cache {
@@ -276,6 +279,99 @@ int timed_end(fo_ctx *ctx, bool on) {
     return FO_OK;
 }
 
+// Host-buffer BF16 prefill, pipelined over bands of query rows: the image rows
+// (which need every image key) form the first band and the rest splits into at
+// most four bands of at least 1,024 rows, all on 256-row boundaries.  Band b's
+// keys, values and queries go up on the h2d stream; its BF16 conversion and
+// prefill kernel run on the context's stream once they have landed; its output
+// comes down on the d2h stream while later bands go up.  A band's kernel reads
+// keys and values only below the end of its own rows (or of the image), which
+// earlier bands have converted.  Returns after the last copy.
+int prefill_bf16_host_pipelined(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, const fo_geometry &geometry,
+                                const float *sinks, float *output, const fo_prefill_options &options) {
+    const int64_t T = kv->total_len, H = kv->n_heads, G = kv->n_kv_heads;
+    std::vector<std::pair<int64_t, int64_t>> bands;
+    int64_t first = std::min<int64_t>(T, (geometry.image_end + 255) / 256 * 256);
+    if (first > 0) bands.push_back({0, first});
+    const int64_t rest = T - first;
+    if (rest > 0) {
+        const int64_t nb = std::max<int64_t>(1, std::min<int64_t>(4, rest / 1024));
+        const int64_t step = (rest + nb - 1) / nb;
+        for (int64_t r = first; r < T;) {
+            const int64_t e = std::min<int64_t>(T, (r + step + 255) / 256 * 256);
+            bands.push_back({r, e});
+            r = e;
+        }
+    }
+    const size_t nb = bands.size();
+    if (!ctx->h2d) FO_CUDA(cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (!ctx->d2h) FO_CUDA(cudaStreamCreateWithFlags(&ctx->d2h, cudaStreamNonBlocking), "cudaStreamCreate");
+    while (ctx->band_ev.size() < 2 * nb + 1) {
+        cudaEvent_t e;
+        FO_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        ctx->band_ev.push_back(e);
+    }
+    cudaEvent_t start = ctx->band_ev[0];
+    const int64_t qn = T * H * 64, kn = T * H * 64, vn = T * G * 64;
+    FO_CUDA(ctx->stage[0].ensure((size_t)qn * 4), "cudaMalloc(staging)");
+    FO_CUDA(ctx->stage[1].ensure((size_t)kn * 4), "cudaMalloc(staging)");
+    FO_CUDA(ctx->stage[3].ensure((size_t)vn * 4), "cudaMalloc(staging)");
+    FO_CUDA(ctx->stage[4].ensure((size_t)H * 4), "cudaMalloc(staging)");
+    FO_CUDA(ctx->stage[5].ensure((size_t)qn * 4), "cudaMalloc(staging)");
+    FO_CUDA(ctx->bf16_k.ensure((size_t)kn * 2), "cudaMalloc(bf16 keys)");
+    FO_CUDA(ctx->bf16_v.ensure((size_t)vn * 2), "cudaMalloc(bf16 values)");
+    float *dq = (float *)ctx->stage[0].ptr, *dk = (float *)ctx->stage[1].ptr, *dv = (float *)ctx->stage[3].ptr;
+    float *ds = (float *)ctx->stage[4].ptr, *dout = (float *)ctx->stage[5].ptr;
+    uint16_t *kb = (uint16_t *)ctx->bf16_k.ptr, *vb = (uint16_t *)ctx->bf16_v.ptr;
+    if (!aligned16(kb) || !aligned16(vb) || !aligned16(dq) || !aligned16(dout))
+        return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
+    // Earlier work on the context's stream (which may still read the staging
+    // buffers) comes first.
+    FO_CUDA(cudaEventRecord(start, ctx->stream), "cudaEventRecord");
+    FO_CUDA(cudaStreamWaitEvent(ctx->h2d, start, 0), "cudaStreamWaitEvent");
+    FO_CUDA(cudaMemcpyAsync(ds, sinks, (size_t)H * 4, cudaMemcpyHostToDevice, ctx->h2d), "cudaMemcpyAsync(H2D)");
+    const bool prof = options.profile != 0;
+    for (size_t b = 0; b < nb; b++) {
+        const int64_t r0 = bands[b].first, r1 = bands[b].second;
+        cudaEvent_t up = ctx->band_ev[1 + 2 * b], done = ctx->band_ev[2 + 2 * b];
+        FO_CUDA(cudaMemcpyAsync(dk + r0 * H * 64, kv->prefix_k + r0 * H * 64, (size_t)(r1 - r0) * H * 64 * 4,
+                                cudaMemcpyHostToDevice, ctx->h2d),
+                "cudaMemcpyAsync(H2D)");
+        FO_CUDA(cudaMemcpyAsync(dv + r0 * G * 64, kv->v + r0 * G * 64, (size_t)(r1 - r0) * G * 64 * 4,
+                                cudaMemcpyHostToDevice, ctx->h2d),
+                "cudaMemcpyAsync(H2D)");
+        FO_CUDA(cudaMemcpyAsync(dq + r0 * H * 64, q + r0 * H * 64, (size_t)(r1 - r0) * H * 64 * 4,
+                                cudaMemcpyHostToDevice, ctx->h2d),
+                "cudaMemcpyAsync(H2D)");
+        FO_CUDA(cudaEventRecord(up, ctx->h2d), "cudaEventRecord");
+        FO_CUDA(cudaStreamWaitEvent(ctx->stream, up, 0), "cudaStreamWaitEvent");
+        if (b == 0 && prof) FO_CUDA(cudaEventRecord(ctx->ev0, ctx->stream), "cudaEventRecord");
+        cudaError_t e = fo_launch_convert_bf16(dk + r0 * H * 64, kb + r0 * H * 64, (r1 - r0) * H * 64, ctx->stream);
+        if (e == cudaSuccess)
+            e = fo_launch_convert_bf16(dv + r0 * G * 64, vb + r0 * G * 64, (r1 - r0) * G * 64, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "convert kernel launch");
+        e = fo_launch_prefill_bf16(dq, kb, vb, ds, dout, T, H, G, geometry.image_start, geometry.image_end, r0, r1,
+                                   options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err,
+                                   ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
+        FO_CUDA(cudaEventRecord(done, ctx->stream), "cudaEventRecord");
+    }
+    if (prof) FO_CUDA(cudaEventRecord(ctx->ev1, ctx->stream), "cudaEventRecord");
+    // The outputs come down band by band (issued after every upload, so a
+    // pageable destination cannot hold up the uploads).
+    for (size_t b = 0; b < nb; b++) {
+        const int64_t r0 = bands[b].first, r1 = bands[b].second;
+        FO_CUDA(cudaStreamWaitEvent(ctx->d2h, ctx->band_ev[2 + 2 * b], 0), "cudaStreamWaitEvent");
+        FO_CUDA(cudaMemcpyAsync(output + r0 * H * 64, dout + r0 * H * 64, (size_t)(r1 - r0) * H * 64 * 4,
+                                cudaMemcpyDeviceToHost, ctx->d2h),
+                "cudaMemcpyAsync(D2H)");
+    }
+    FO_CUDA(cudaStreamSynchronize(ctx->d2h), "cudaStreamSynchronize");
+    FO_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (prof) FO_CUDA(cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1), "cudaEventElapsedTime");
+    return check_device_errors(ctx);
+}
+
 }  // namespace
 
 extern "C" {
@@ -330,6 +426,11 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->ev0) cudaEventDestroy(ctx->ev0);
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
+    if (ctx->h2d) cudaStreamSynchronize(ctx->h2d);
+    if (ctx->d2h) cudaStreamSynchronize(ctx->d2h);
+    for (cudaEvent_t e : ctx->band_ev) cudaEventDestroy(e);
+    if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
+    if (ctx->d2h) cudaStreamDestroy(ctx->d2h);
     if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return FO_OK;
@@ -413,6 +514,7 @@ int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *
     if (keys_bf16 && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "BF16 copies must be device pointers");
     if (!ctx) return fail(FO_ERR_INVALID, "null context");
     DeviceGuard guard(ctx->device);
+    if (mem == FO_MEM_HOST) return prefill_bf16_host_pipelined(ctx, q, kv, geometry, sinks, output, options);
     const int64_t T = kv->total_len, H = kv->n_heads, G = kv->n_kv_heads;
     Staged s;
     // The FP32 keys and values are only read when converting.

@@ -140,3 +140,23 @@ def test_sharded_prefill_on_one_rank_matches_the_whole_page(ctx):
     F.attention_prefill_bf16(q, k, v, (0, 0, 300), s, whole, 16, 8, ctx=ctx)
     torch.cuda.synchronize()
     assert torch.equal(got, whole.view(T, 16, 64).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("T,image", [(6544, (0, 4096)), (5000, (0, 0)), (1000, (5, 262)), (300, (0, 300)), (4, (0, 0))])
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_buffers_pipeline_equals_device_call(ctx, T, image, pinned):
+    """FO_MEM_HOST runs the page in bands (uploads, kernels and downloads
+    overlapped); every row equals the device-pointer call bit for bit, with
+    pinned and with pageable host memory."""
+    q, k, v, s = G.bf16_operands(T)
+    geo = (0, image[0], image[1])
+    whole = torch.zeros(q.size, device="cuda")
+    F.attention_prefill_bf16(dev(q), dev(k), dev(v), geo, dev(s), whole, 16, 8, ctx=ctx)
+    host = [torch.from_numpy(x.reshape(-1)) for x in (q, k, v)]
+    out = torch.full((q.size,), float("nan"))
+    if pinned:
+        host = [x.pin_memory() for x in host]
+        out = out.pin_memory()
+    F.attention_prefill_bf16(host[0], host[1], host[2], geo, torch.from_numpy(s), out, 16, 8, ctx=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(out, whole.cpu())
