@@ -422,20 +422,23 @@ def time_sharded(run, args):
     return out
 
 
-def time_decode(run, args):
-    """5-row verify decode at 16,384 positions over BF16 and FP32 records,
-    rotating distinct caches (more than 4x L2).  The K calls are captured once
-    in a CUDA graph on the caches' own stream and replayed, so the device time
-    is not bounded by the Python launch path (a serving loop replays a graph
-    the same way)."""
+def time_decode(run, args, lengths=(DECODE_L,)):
+    """5-row verify decode over BF16 and FP32 records at each cache length,
+    rotating distinct caches (together more than 4x L2).  The K calls are
+    captured once in a CUDA graph on the caches' own stream and replayed, so
+    the device time is not bounded by the Python launch path (a serving loop
+    replays a graph the same way).  Returns {length: {format: line}}."""
     torch, F = run.torch, run.F
     rng = np.random.default_rng(2 + run.rank)
     sd = torch.from_numpy(rng.standard_normal(HEADS).astype(np.float32)).to(run.dev)
     stream = torch.cuda.Stream(device=run.dev)
     dctx = F.Context(run.local, stream=stream.cuda_stream)
-    out = {}
-    for fmt, n_caches in (("bf16", 12), ("f32", 6)):
-        p = DECODE_L - DECODE_ROWS
+    l2 = getattr(torch.cuda.get_device_properties(run.dev), "L2_cache_size", 126 << 20) or (126 << 20)
+    res = {}
+    for length, fmt in [(n, f) for n in lengths for f in ("bf16", "f32")]:
+        out = res.setdefault(length, {})
+        p = length - DECODE_ROWS
+        n_caches = max(2, -(-4 * l2 // (p * RECORD_BYTES[fmt])))
         kp = rng.standard_normal((p, HEADS, 64)).astype(np.float32)
         kp[:, 1::2, :32] = kp[:, 0::2, :32]
         vp = rng.standard_normal((p, KV_HEADS, 64)).astype(np.float32)
@@ -447,7 +450,7 @@ def time_decode(run, args):
         for i in range(n_caches):
             kk = kd if i == 0 else kd * (1 + 1e-3 * i)
             torch.cuda.synchronize()
-            c = F.SplitPrefix.from_compact(kk, vd, p, DECODE_L, fmt=fmt, ctx=dctx)
+            c = F.SplitPrefix.from_compact(kk, vd, p, length, fmt=fmt, ctx=dctx)
             c.append(td, td)
             caches.append(c)
         torch.cuda.synchronize()
@@ -478,18 +481,69 @@ def time_decode(run, args):
         us = run.max_over_ranks(start.elapsed_time(end)) * 1e3 / steps
         bytes_step = p * RECORD_BYTES[fmt] + DECODE_ROWS * KV_HEADS * 128 * (2 if fmt == "bf16" else 4)
         gbs = bytes_step / (us * 1e-6) / 1e9
-        out[fmt] = {"us_per_step": round(us, 2), "rows": DECODE_ROWS, "kv_len": DECODE_L,
+        out[fmt] = {"us_per_step": round(us, 2), "rows": DECODE_ROWS, "kv_len": length,
                     "bytes_per_step": int(bytes_step),
                     "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"],
                                  "unit": "GB/s", "frac": round(gbs / run.peaks["hbm_gbs"], 4),
-                                 "traffic": run.traffic.get(f"decode_{fmt}")},
+                                 "traffic": run.traffic.get(f"decode_{fmt}") if length == DECODE_L else None},
                     "caches_rotated": n_caches, "gpu_launches_per_step": 1, "timing": "CUDA graph of the steps"}
         del graph
         for c in caches:
             c.close()
         torch.cuda.empty_cache()
     dctx.close()
-    return out
+    return res
+
+
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 148 SMs x 128 FP32 FMA/clk x 1.965 GHz
+
+
+def time_prefill_rows(run, args, inputs):
+    """Secondary prefill rows of the C2 page: the FP32 exact tiles
+    (fo_attention, platform-exact exp; bound by FP32 CUDA cores) and the
+    reference probe's geometry (image_end 6,534: every row but the last ten
+    bidirectional) on the BF16 static-shift tiles."""
+    torch, F = run.torch, run.F
+    q, k, v, sinks, geo = inputs
+    qd, kd, vd = (torch.from_numpy(x).to(run.dev) for x in (q, k, v))
+    kb, vb = kd.to(torch.bfloat16), vd.to(torch.bfloat16)
+    sd = torch.from_numpy(sinks).to(run.dev)
+    out = torch.empty(SEQ * HEADS * 64, device=run.dev)
+    res = {}
+    steps = max(3, min(args.steps, 10))
+
+    def fp32(_):
+        F.attention_with(qd, kd, vd, SEQ, geo, sd, out, HEADS, KV_HEADS, 64, ctx=run.ctx)
+
+    for i in range(2):
+        fp32(i)
+    ms, _ = run.timed(fp32, steps)
+    ms /= steps
+    tf = FLOP_PER_CALL / (ms / 1e3) / 1e12
+    res["fp32_exact"] = {"ms_per_step": round(ms, 4), "tok_per_s": round(SEQ / (ms / 1e3), 1),
+                         "roofline": {"bound": "fp32", "achieved": round(tf, 1), "peak": round(FP32_NOMINAL_TFLOPS, 1),
+                                      "unit": "TFLOP/s", "frac": round(tf / FP32_NOMINAL_TFLOPS, 4),
+                                      "note": "peak = nominal FP32 FMA rate (no measured FP32 figure)"}}
+    probe = (0, 0, 6534)
+    pairs = 6534 * 6534 + sum(t + 1 for t in range(6534, SEQ))  # rows < 6534 see 6,534 keys, the rest t + 1
+    flop = 4.0 * 64 * pairs * HEADS
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
+
+    def bf16_probe(_):
+        F.attention_prefill_bf16(qd, kd, vd, probe, sd, out, HEADS, KV_HEADS, keys_bf16=kb, values_bf16=vb,
+                                 options=opts, ctx=run.ctx)
+
+    for i in range(3):
+        bf16_probe(i)
+    ms, _ = run.timed(bf16_probe, max(args.steps, 10))
+    ms /= max(args.steps, 10)
+    tf = flop / (ms / 1e3) / 1e12
+    res["bf16_probe_geometry"] = {"image_end": 6534, "ms_per_step": round(ms, 4),
+                                  "tok_per_s": round(SEQ / (ms / 1e3), 1), "gflop": round(flop / 1e9, 2),
+                                  "roofline": {"bound": "tensor", "achieved": round(tf, 1),
+                                               "peak": run.peaks["bf16_tflops"], "unit": "TFLOP/s",
+                                               "frac": round(tf / run.peaks["bf16_tflops"], 4)}}
+    return res
 
 
 def run_ours(args, world, rank, local):
@@ -509,11 +563,17 @@ def run_ours(args, world, rank, local):
     if args.mode == "full":
         line["e2e"] = time_e2e(run, args, inputs)
     if args.mode in ("full", "decode"):
-        line["decode"] = time_decode(run, args)
+        lengths = (DECODE_L, 6544, 12000) if args.mode == "full" else (DECODE_L,)
+        dec = time_decode(run, args, lengths)
+        line["decode"] = dec[DECODE_L]
+        if len(lengths) > 1:
+            line["decode_lengths"] = {str(n): dec[n] for n in lengths[1:]}
     if args.mode in ("full", "c4"):
         line["decode_c4"] = time_c4(run, args)
     if args.mode in ("full", "sharded"):
         line["sharded_prefill"] = time_sharded(run, args)
+    if args.mode == "full":
+        line["prefill_rows"] = time_prefill_rows(run, args, inputs)
     if args.mode == "full" and rank == 0 and world == 1:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
