@@ -68,8 +68,9 @@ __global__ void __launch_bounds__(256) quantize_i8_kernel(const float *x, int64_
 
 // ------------------------------------------------------------------ decode
 template <bool FAST>
-__global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page *pages, int64_t heads) {
+__global__ void __launch_bounds__(I8_THREADS, 3) decode_i8_kernel(const fo_i8_page *pages, int64_t heads) {
     __shared__ float ow[I8_WARPS][64];
+    __shared__ __align__(16) float qs[64];  // the head's query row
     __shared__ float mw[I8_WARPS], lw[I8_WARPS];
     // Per warp, two buffers of 32 key rows and 32 value rows (dynamic: 64 KB).
     extern __shared__ __align__(128) int8_t i8_rows[];
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page 
     const float *ks = pg.k_scales + h * groups, *vs = pg.v_scales + h * groups;
     if (t < 2 * I8_WARPS) sm100::mbar_init(&bars[t / 2][t % 2], 1);
     if (t == 0) abort_flag = 0;
+    if (t < 16) reinterpret_cast<float4 *>(qs)[t] = __ldg(reinterpret_cast<const float4 *>(pg.q + h * 64) + t);
     __syncthreads();
     const int64_t w0 = (int64_t)s * FO_I8_SPLIT + (int64_t)warp * I8_KEYS_PER_WARP;
     const int64_t w1 = min64(w0 + I8_KEYS_PER_WARP, min64((int64_t)(s + 1) * FO_I8_SPLIT, len));
@@ -105,20 +107,11 @@ __global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page 
     };
     if (lane == 0)
         for (int c = 0; c < min(2, n_chunks); c++) stage(c);
-    // The query row of this head, in every lane.
-    float q[64];
-    {
-        const float4 *qp = reinterpret_cast<const float4 *>(pg.q + h * 64);
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const float4 x = __ldg(qp + i);
-            q[4 * i] = x.x;
-            q[4 * i + 1] = x.y;
-            q[4 * i + 2] = x.z;
-            q[4 * i + 3] = x.w;
-        }
-    }
-    float m_st = -INFINITY, l_st = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    // P V runs in half warps: lanes 16 h + i take the keys of parity h and
+    // output dimensions 4 i .. 4 i + 3, as (d, d + 1), (d + 2, d + 3) pairs.
+    const int half = lane >> 4, dq = 4 * (lane & 15);
+    float m_st = -INFINITY, l_st = 0.0f;
+    float2 oa = make_float2(0.0f, 0.0f), ob = make_float2(0.0f, 0.0f);
     bool ok = true;
     int c = 0;
     for (; c < n_chunks; c++) {
@@ -133,7 +126,9 @@ __global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page 
         {
             const uint4 *kp = reinterpret_cast<const uint4 *>(kb + min(lane, nk - 1) * 64);
             const float sc = __ldg(ks + (k0 + min(lane, nk - 1)) / I8_GROUP);
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            // Dimensions d % 4 = 0, 1 (a01) and 2, 3 (a23) in packed FMA,
+            // each half an ordinary fmaf.
+            float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const uint4 wv = kp[i];
@@ -142,14 +137,13 @@ __global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page 
                 for (int j = 0; j < 4; j++) {
                     float cf[4];
                     s8x4_f32(ww[j], cf);
-                    const int d = 16 * i + 4 * j;
-                    a0 = fmaf(q[d], cf[0], a0);
-                    a1 = fmaf(q[d + 1], cf[1], a1);
-                    a2 = fmaf(q[d + 2], cf[2], a2);
-                    a3 = fmaf(q[d + 3], cf[3], a3);
+                    const float4 qv = reinterpret_cast<const float4 *>(qs)[4 * i + j];
+                    a01 = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(cf[0], cf[1]), a01);
+                    a23 = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(cf[2], cf[3]), a23);
                 }
             }
-            x = lane < nk ? __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3)), sc), 0.125f)
+            x = lane < nk ? __fmul_rn(__fmul_rn(__fadd_rn(__fadd_rn(a01.x, a01.y), __fadd_rn(a23.x, a23.y)), sc),
+                                      0.125f)
                           : -INFINITY;
         }
         // Online softmax of the chunk (chunk max, rescale, exp(s - max)).
@@ -159,18 +153,25 @@ __global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page 
         const float p = lane < nk ? softmax_exp<FAST>(__fsub_rn(x, m_new)) : 0.0f;
         l_st = __fadd_rn(__fmul_rn(l_st, alpha), warp_sum(p));
         m_st = m_new;
-        o0 = __fmul_rn(o0, alpha);
-        o1 = __fmul_rn(o1, alpha);
-        // O += P V: this lane's dimensions 2 lane, 2 lane + 1 of every key,
-        // the value scale folded into p (a chunk never straddles a group).
+        oa = __fmul2_rn(oa, make_float2(alpha, alpha));
+        ob = __fmul2_rn(ob, make_float2(alpha, alpha));
+        // O += P V over the keys of this half's parity, the value scale
+        // folded into p (a chunk never straddles a group).
         const float ps = __fmul_rn(p, __ldg(vs + k0 / I8_GROUP));
-#pragma unroll 8
-        for (int j = 0; j < nk; j++) {
-            const float pj = __shfl_sync(0xffffffffu, ps, j);
-            float v0, v1;
-            s8x2_f32(reinterpret_cast<const unsigned short *>(vb + j * 64)[lane], v0, v1);
-            o0 = fmaf(pj, v0, o0);
-            o1 = fmaf(pj, v1, o1);
+        auto pv = [&](int j) {
+            const float pj = __shfl_sync(0xffffffffu, ps, min(j, 31));
+            if (j < nk) {
+                float v[4];
+                s8x4_f32(*reinterpret_cast<const uint32_t *>(vb + j * 64 + dq), v);
+                oa = __ffma2_rn(make_float2(pj, pj), make_float2(v[0], v[1]), oa);
+                ob = __ffma2_rn(make_float2(pj, pj), make_float2(v[2], v[3]), ob);
+            }
+        };
+        if (nk == 32) {
+#pragma unroll
+            for (int j2 = 0; j2 < 16; j2++) pv(2 * j2 + half);
+        } else {
+            for (int j2 = 0; j2 < (nk + 1) / 2; j2++) pv(2 * j2 + half);
         }
         __syncwarp();
         if (lane == 0 && c + 2 < n_chunks) {
@@ -187,15 +188,19 @@ __global__ void __launch_bounds__(I8_THREADS) decode_i8_kernel(const fo_i8_page 
         }
         m_st = -INFINITY;
         l_st = 0.0f;
-        o0 = o1 = 0.0f;
+        oa = ob = make_float2(0.0f, 0.0f);
     }
+    // The even-key and odd-key halves of this lane's dimensions.
+    oa.x = __fadd_rn(oa.x, __shfl_xor_sync(0xffffffffu, oa.x, 16));
+    oa.y = __fadd_rn(oa.y, __shfl_xor_sync(0xffffffffu, oa.y, 16));
+    ob.x = __fadd_rn(ob.x, __shfl_xor_sync(0xffffffffu, ob.x, 16));
+    ob.y = __fadd_rn(ob.y, __shfl_xor_sync(0xffffffffu, ob.y, 16));
     // Combine the warps in order into the split's partial.
     if (lane == 0) {
         mw[warp] = m_st;
         lw[warp] = l_st;
     }
-    ow[warp][2 * lane] = o0;
-    ow[warp][2 * lane + 1] = o1;
+    if (half == 0) *reinterpret_cast<float4 *>(&ow[warp][dq]) = make_float4(oa.x, oa.y, ob.x, ob.y);
     __syncthreads();
     if (t < 64) {
         float m = -INFINITY;

@@ -85,21 +85,35 @@ __device__ __forceinline__ float softmax_exp(float x) {
 // The four signed bytes of w.
 __device__ __forceinline__ void s8x4_f32(uint32_t w, float *out) {
     const uint32_t u = w ^ 0x80808080u;
-#pragma unroll
-    for (int j = 0; j < 4; j++)
-        out[j] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u + j)), 8388736.0f);
+    // (2^23 + 128 + c) - (2^23 + 128) is exact; two codes per packed subtract.
+    const float2 lo = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
+                                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))),
+                                 make_float2(-8388736.0f, -8388736.0f));
+    const float2 hi = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542u)),
+                                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543u))),
+                                 make_float2(-8388736.0f, -8388736.0f));
+    out[0] = lo.x;
+    out[1] = lo.y;
+    out[2] = hi.x;
+    out[3] = hi.y;
 }
 // The two signed bytes in the low half of w (as a 16-bit load returns them).
 __device__ __forceinline__ void s8x2_f32(uint32_t w, float &lo, float &hi) {
     const uint32_t u = w ^ 0x8080u;
-    lo = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)), 8388736.0f);
-    hi = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u)), 8388736.0f);
+    const float2 x = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))),
+                                make_float2(-8388736.0f, -8388736.0f));
+    lo = x.x;
+    hi = x.y;
 }
 // The two signed 16-bit halves of w.
 __device__ __forceinline__ void s16x2_f32(uint32_t w, float &lo, float &hi) {
     const uint32_t u = w ^ 0x80008000u;
-    lo = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7510u)), 8421376.0f);
-    hi = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7532u)), 8421376.0f);
+    const float2 x = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7510u)),
+                                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7532u))),
+                                make_float2(-8421376.0f, -8421376.0f));
+    lo = x.x;
+    hi = x.y;
 }
 
 // Rust f32::max: the non-NaN operand when one is NaN (fmaxf semantics).
