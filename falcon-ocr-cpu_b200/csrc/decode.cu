@@ -7,7 +7,7 @@
 // for both heads of the group and every verification row, as the reference's
 // pair_rows serves them (each record is read once and every row runs over
 // it).  Persistent CTAs of four warp pairs walk the items; a pair owns whole
-// items and streams each through two buffers of 32-key chunks.  A chunk of
+// items and streams each through NBUF buffers of 32-key chunks.  A chunk of
 // prefix records arrives by one TMA tile copy through the cache's record
 // tensor map, whose box is wider than a record so that the out-of-bounds fill
 // pads every key's slot (consecutive keys start on different banks); a chunk
@@ -18,7 +18,7 @@
 // (chunk max, rescale, exp(s - max)), and O += P V with lane = two output
 // dimensions, dequantizing exactly as the reference (fl(code * scale),
 // decode.rs:151-187) with packed FP32 FMA (each half an ordinary fmaf).  Once
-// both warps are done with a chunk, the copies two chunks ahead are issued
+// both warps are done with a chunk, the copies NBUF chunks ahead are issued
 // into its buffer, and the next item's records are prefetched into L2.  The
 // chunks combine, in chunk order, into the split's unnormalized partial; a
 // merge kernel, launched as a programmatic dependent, combines the splits in
@@ -40,7 +40,7 @@ namespace fo {
 enum { DF32 = 0, DQ16 = 1, DQ8 = 2, DBF16 = 3 };
 
 // Per-format shape of a CTA: NPAIR pairs of warps; a pair owns whole items
-// and streams their 32-key chunks through two slot buffers; warp 2p + h of
+// and streams their 32-key chunks through NBUF slot buffers; warp 2p + h of
 // pair p computes head h of the item's KV group.
 template <int F>
 struct Shape {
@@ -50,14 +50,16 @@ struct Shape {
     static constexpr int KPL = 1;                // keys per lane
     static constexpr int NCH = FO_SPLIT / CK;    // chunks per item
     static constexpr int NPAIR = 4;
-    static constexpr int NBUF = 2;               // slot buffers per pair
+    // Slot buffers per pair: Q8 records are small enough for a third, which
+    // keeps one more chunk in flight (single-row decode waits on its copies).
+    static constexpr int NBUF = F == DQ8 ? 3 : 2;
     static constexpr int NW = 2 * NPAIR;
     static constexpr int THREADS = 32 * NW;
     static constexpr int MIN_CTAS = F == DF32 ? 1 : 2;
     // Padded slot: 16 bytes past the record, so consecutive keys start on
     // different banks (slot stride 4, 20 or 12 mod 32 words).
     static constexpr int SLOT = FO_RECORD * E + 16;
-    static_assert(NCH >= NBUF, "an item spans both buffers");
+    static_assert(NCH >= NBUF, "an item spans every buffer");
 };
 
 // Shared-memory layout of one instantiation (bytes).
@@ -98,8 +100,9 @@ __device__ __forceinline__ float2 slot_pair(const unsigned char *slot, int e, fl
 }
 
 // 16 consecutive decoded values of a staged slot at element `e` (a multiple
-// of 16, inside one 32-element scale block).
-template <int F>
+// of 16, inside one 32-element scale block); with SCALED false, the codes of a
+// coded format before their block scale.
+template <int F, bool SCALED = true>
 __device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, float scale, float *out) {
     if constexpr (F == DF32) {
         const float4 *p = reinterpret_cast<const float4 *>(slot + 4 * e);
@@ -125,8 +128,8 @@ __device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, fl
                 } else {
                     float lo, hi;
                     s16x2_f32(w[c], lo, hi);
-                    out[8 * i + 2 * c] = __fmul_rn(lo, scale);
-                    out[8 * i + 2 * c + 1] = __fmul_rn(hi, scale);
+                    out[8 * i + 2 * c] = SCALED ? __fmul_rn(lo, scale) : lo;
+                    out[8 * i + 2 * c + 1] = SCALED ? __fmul_rn(hi, scale) : hi;
                 }
             }
         }
@@ -138,7 +141,7 @@ __device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, fl
             float f[4];
             s8x4_f32(w[c], f);
 #pragma unroll
-            for (int b = 0; b < 4; b++) out[4 * c + b] = __fmul_rn(f[b], scale);
+            for (int b = 0; b < 4; b++) out[4 * c + b] = SCALED ? __fmul_rn(f[b], scale) : f[b];
         }
     }
 }
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
         load_q(cur, qv);  // ahead of the bulk copies in the memory queues
         if (stager) {
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
+            for (int c = 0; c < S::NBUF; c++) {
                 stage_chunk<F>(*cur.pp, cur.g, cur.s, c, lane, brec(c), &pbar[c]);
                 if constexpr (S::CODED) {
                     float sc[5];
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
             }
         }
     }
-    pair_sync_and(pair, true);  // chunks 0 and 1's scales are visible
+    pair_sync_and(pair, true);  // the first chunks' scales are visible
     uint32_t u = 0;             // chunks consumed by this pair
     bool ok = true;
     while (have && ok) {
@@ -384,10 +387,10 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
             ob[r] = make_float2(0.0f, 0.0f);
         }
         for (int c = 0; c < NCH && ok; c++, u++) {
-            const int b = u & 1;
-            // The stager asks for chunk u + 2's scales now; they land while
+            const int b = (int)(u % S::NBUF);
+            // The stager asks for chunk u + NBUF's scales now; they land while
             // this chunk computes and are published with its copies below.
-            const int c2 = c + 2;
+            const int c2 = c + S::NBUF;
             const bool in_item = c2 < NCH;
             const Item &x2 = in_item ? cur : nxt;
             const bool has2 = in_item || have_n;
@@ -398,7 +401,7 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
             const int64_t k0 = p0 + (int64_t)c * CK;
             const int64_t w1 = min64(k0 + CK, p_end);
             const int nk = (int)max64(0, w1 - k0);  // the chunk's keys (warp-uniform)
-            const bool staged = sm100::mbar_wait(&pbar[b], (u >> 1) & 1, abort_flag, pg.err);
+            const bool staged = sm100::mbar_wait(&pbar[b], (u / S::NBUF) & 1, abort_flag, pg.err);
             if (c == 0 && have_n && stager && lane == 0) {
                 // The pair's next item streams into L2 while this one
                 // computes (one item ahead: a whole batch of pages would
@@ -417,28 +420,35 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
                 const float *kscl = cscl + key * 5;
                 float lg[R];
                 {
-                    float2 acc[R];
+                    // Coded formats: the temporal (acc) and spatial (acs) blocks
+                    // accumulate codes apart and take their scales once.
+                    float2 acc[R], acs[R];
 #pragma unroll
-                    for (int r = 0; r < R; r++) acc[r] = make_float2(0.0f, 0.0f);
+                    for (int r = 0; r < R; r++) acc[r] = acs[r] = make_float2(0.0f, 0.0f);
 #pragma unroll
                     for (int part = 0; part < 4; part++) {  // T[0:16], T[16:32], S_h[0:16], S_h[16:32]
                         const int e = part < 2 ? 16 * part : 32 + 32 * hd + 16 * (part - 2);
-                        const int blk = part < 2 ? 0 : 1 + hd;
                         float kv[16];
-                        slot_span16<F>(ks, e, S::CODED ? kscl[blk] : 1.0f, kv);
+                        slot_span16<F, !S::CODED>(ks, e, 1.0f, kv);
 #pragma unroll
                         for (int d = 0; d < 16; d += 4) {
 #pragma unroll
                             for (int r = 0; r < R; r++) {
                                 const float4 x = *reinterpret_cast<const float4 *>(&qw[r][16 * part + d]);
-                                acc[r] = __ffma2_rn(make_float2(x.x, x.y), make_float2(kv[d], kv[d + 1]), acc[r]);
-                                acc[r] =
-                                    __ffma2_rn(make_float2(x.z, x.w), make_float2(kv[d + 2], kv[d + 3]), acc[r]);
+                                float2 &a = (S::CODED && part >= 2) ? acs[r] : acc[r];
+                                a = __ffma2_rn(make_float2(x.x, x.y), make_float2(kv[d], kv[d + 1]), a);
+                                a = __ffma2_rn(make_float2(x.z, x.w), make_float2(kv[d + 2], kv[d + 3]), a);
                             }
                         }
                     }
 #pragma unroll
-                    for (int r = 0; r < R; r++) lg[r] = __fadd_rn(acc[r].x, acc[r].y);
+                    for (int r = 0; r < R; r++) {
+                        if constexpr (S::CODED)
+                            lg[r] = __fadd_rn(__fmul_rn(kscl[0], __fadd_rn(acc[r].x, acc[r].y)),
+                                              __fmul_rn(kscl[1 + hd], __fadd_rn(acs[r].x, acs[r].y)));
+                        else
+                            lg[r] = __fadd_rn(acc[r].x, acc[r].y);
+                    }
                 }
                 // Online softmax of the chunk per row (the reference's tile
                 // step: chunk max, rescale, exp(s - max)), the rows interleaved
@@ -524,8 +534,8 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
                 __syncwarp();
             }
             // Both warps are done with buffer b (and agree whether their
-            // waits succeeded); the stager refills it with chunk u + 2 and
-            // its scales (read by both warps two chunks later, after the
+            // waits succeeded); the stager refills it with chunk u + NBUF and
+            // its scales (read by both warps NBUF chunks later, after the
             // next pair barrier).
             ok = pair_sync_and(pair, staged);
             if (ok && stager && has2) {
@@ -563,10 +573,14 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
     }
     if (!ok && stager) {
         // A wait that gave up (error word raised) at chunk u - 1: let the
-        // pair's copies in flight (chunks u - 1 and u) land before the CTA
-        // can exit; a phase that was never issued gives up after the bound.
-        sm100::mbar_wait_drain(&pbar[(u - 1) & 1], ((u - 1) >> 1) & 1);
-        sm100::mbar_wait_drain(&pbar[u & 1], (u >> 1) & 1);
+        // pair's copies in flight (chunks u - 1 .. u + NBUF - 2) land before
+        // the CTA can exit; a phase that was never issued gives up after the
+        // bound.
+#pragma unroll
+        for (int i = 0; i < S::NBUF; i++) {
+            const uint32_t w = u - 1 + i;
+            sm100::mbar_wait_drain(&pbar[w % S::NBUF], (w / S::NBUF) & 1);
+        }
     }
 }
 
