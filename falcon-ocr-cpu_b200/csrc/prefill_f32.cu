@@ -60,16 +60,18 @@ __global__ void __launch_bounds__(F32_THREADS) prefill_f32_kernel(F32Args a) {
         Qt[(4 * c + 3) * F32_LD + r] = x.w;
     }
     // Per-row state: rows ty*8 + i.
+    // Outputs as (dims 4 tx, 4 tx + 1) and (4 tx + 2, 4 tx + 3) pairs of the
+    // packed FMA (each half an ordinary fmaf).
     int64_t vend[8];
-    float m[8], l[8], acc[8][4];
+    float m[8], l[8];
+    float2 acc[8][2];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const int64_t abs_row = first_abs + ty * 8 + i;
         vend[i] = visible_end(abs_row, a.image_start, a.image_end);
         m[i] = -INFINITY;
         l[i] = 0.0f;
-#pragma unroll
-        for (int c = 0; c < 4; c++) acc[i][c] = 0.0f;
+        acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
     }
     const float scale = 0.125f;  // (64 as f32).sqrt().recip()
 
@@ -93,23 +95,29 @@ __global__ void __launch_bounds__(F32_THREADS) prefill_f32_kernel(F32Args a) {
         }
         __syncthreads();
 
-        // S = Q K^T: rows ty*8..+8, keys tx*4..+4.
-        float s[8][4];
+        // S = Q K^T: rows ty*8..+8, keys tx*4..+4 (key pairs in packed FMA).
+        float2 s2[8][2];
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-#pragma unroll
-            for (int c = 0; c < 4; c++) s[i][c] = 0.0f;
+        for (int i = 0; i < 8; i++) s2[i][0] = s2[i][1] = make_float2(0.0f, 0.0f);
 #pragma unroll 8
         for (int d = 0; d < FO_HD; d++) {
             const float4 qa = *reinterpret_cast<const float4 *>(Qt + d * F32_LD + ty * 8);
             const float4 qb = *reinterpret_cast<const float4 *>(Qt + d * F32_LD + ty * 8 + 4);
             const float4 kb = *reinterpret_cast<const float4 *>(Kt + d * F32_LD + tx * 4);
             const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            const float kv[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-            for (int i = 0; i < 8; i++)
+            for (int i = 0; i < 8; i++) {
+                s2[i][0] = __ffma2_rn(make_float2(qv[i], qv[i]), make_float2(kb.x, kb.y), s2[i][0]);
+                s2[i][1] = __ffma2_rn(make_float2(qv[i], qv[i]), make_float2(kb.z, kb.w), s2[i][1]);
+            }
+        }
+        float s[8][4];
 #pragma unroll
-                for (int c = 0; c < 4; c++) s[i][c] = fmaf(qv[i], kv[c], s[i][c]);
+        for (int i = 0; i < 8; i++) {
+            s[i][0] = s2[i][0].x;
+            s[i][1] = s2[i][0].y;
+            s[i][2] = s2[i][1].x;
+            s[i][3] = s2[i][1].y;
         }
         // Mask, softmax, P to shared memory.
 #pragma unroll
@@ -153,8 +161,8 @@ __global__ void __launch_bounds__(F32_THREADS) prefill_f32_kernel(F32Args a) {
 #pragma unroll
                 for (int o = 8; o > 0; o >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, o);
                 l[i] = l[i] * rescale + rsum;
-#pragma unroll
-                for (int c = 0; c < 4; c++) acc[i][c] *= rescale;
+                acc[i][0] = __fmul2_rn(acc[i][0], make_float2(rescale, rescale));
+                acc[i][1] = __fmul2_rn(acc[i][1], make_float2(rescale, rescale));
             }
             *reinterpret_cast<float4 *>(Ps + (ty * 8 + i) * F32_LD + tx * 4) = make_float4(p[0], p[1], p[2], p[3]);
         }
@@ -172,10 +180,8 @@ __global__ void __launch_bounds__(F32_THREADS) prefill_f32_kernel(F32Args a) {
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const float p = jj == 0 ? pv[i].x : jj == 1 ? pv[i].y : jj == 2 ? pv[i].z : pv[i].w;
-                    acc[i][0] = fmaf(p, vb.x, acc[i][0]);
-                    acc[i][1] = fmaf(p, vb.y, acc[i][1]);
-                    acc[i][2] = fmaf(p, vb.z, acc[i][2]);
-                    acc[i][3] = fmaf(p, vb.w, acc[i][3]);
+                    acc[i][0] = __ffma2_rn(make_float2(p, p), make_float2(vb.x, vb.y), acc[i][0]);
+                    acc[i][1] = __ffma2_rn(make_float2(p, p), make_float2(vb.z, vb.w), acc[i][1]);
                 }
             }
         }
@@ -189,10 +195,10 @@ __global__ void __launch_bounds__(F32_THREADS) prefill_f32_kernel(F32Args a) {
         const float lse = STATIC ? logf(l[i]) : m[i] + logf(l[i]);
         const float ss = sink_scale(sink, lse);
         float4 o;
-        o.x = (acc[i][0] / l[i]) * ss;
-        o.y = (acc[i][1] / l[i]) * ss;
-        o.z = (acc[i][2] / l[i]) * ss;
-        o.w = (acc[i][3] / l[i]) * ss;
+        o.x = (acc[i][0].x / l[i]) * ss;
+        o.y = (acc[i][0].y / l[i]) * ss;
+        o.z = (acc[i][1].x / l[i]) * ss;
+        o.w = (acc[i][1].y / l[i]) * ss;
         *reinterpret_cast<float4 *>(a.out + (q0 + r) * qw + head * FO_HD + tx * 4) = o;
     }
 }
