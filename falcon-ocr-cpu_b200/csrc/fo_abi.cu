@@ -23,7 +23,8 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
                                               const float *sinks, float *out, int64_t total, int64_t n_heads,
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
                                               int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
-                                              unsigned *err, cudaStream_t stream);
+                                              unsigned *err, int n_split, float *part_o, float *part_ml,
+                                              cudaStream_t stream);
 
 #define FO_WAIT_LIMIT_MAX_NS 10000000000ull
 #define FO_BATCH_PAGES 1024  // pages per batched launch
@@ -138,6 +139,7 @@ struct fo_ctx {
     unsigned *dev_err = nullptr;               // kernel error bits (bounded waits that gave up)
     DevBuf stage[6];                           // prefill host staging: q, prefix_k, generated_k, v, sinks, out
     DevBuf bf16_k, bf16_v;                     // Bf16Kv::Convert scratch
+    DevBuf split_o, split_ml;                  // key-range split partials of the row-band prefill
     DevBuf pages;                              // decode batch descriptors (device)
     HostDesc host_pages;                       // and their pinned staging
     DevBuf i8_pages;                           // INT8-format decode descriptors (device)
@@ -351,8 +353,8 @@ int prefill_bf16_host_pipelined(fo_ctx *ctx, const float *q, const fo_compact_kv
             e = fo_launch_convert_bf16(dv + r0 * G * 64, vb + r0 * G * 64, (r1 - r0) * G * 64, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "convert kernel launch");
         e = fo_launch_prefill_bf16(dq, kb, vb, ds, dout, T, H, G, geometry.image_start, geometry.image_end, r0, r1,
-                                   options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err,
-                                   ctx->stream);
+                                   options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err, 1,
+                                   nullptr, nullptr, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
         FO_CUDA(cudaEventRecord(done, ctx->stream), "cudaEventRecord");
     }
@@ -418,6 +420,8 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     for (auto &b : ctx->stage) b.release();
     ctx->bf16_k.release();
     ctx->bf16_v.release();
+    ctx->split_o.release();
+    ctx->split_ml.release();
     ctx->pages.release();
     ctx->host_pages.release();
     ctx->i8_pages.release();
@@ -541,8 +545,8 @@ int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *
     if (!aligned16(kb) || !aligned16(vb) || !aligned16(s.q) || !aligned16(s.out))
         return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
     e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, T, H, G, geometry.image_start, geometry.image_end, 0, T,
-                               options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err,
-                               ctx->stream);
+                               options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err, 1,
+                               nullptr, nullptr, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
     if ((st = timed_end(ctx, options.profile)) != FO_OK) return st;
     return finish_host(ctx, output, s.out, query_len * H * 64, mem);
@@ -552,7 +556,17 @@ int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *
                                    const uint16_t *values_bf16, int64_t total_len, int64_t n_heads, int64_t n_kv_heads,
                                    fo_geometry geometry, const float *sinks, float *output, int64_t query_begin,
                                    int64_t query_end, fo_prefill_options options) {
+    return fo_attention_prefill_bf16_rows_split(ctx, q, keys_bf16, values_bf16, total_len, n_heads, n_kv_heads,
+                                                geometry, sinks, output, query_begin, query_end, options, 1);
+}
+
+int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint16_t *keys_bf16,
+                                         const uint16_t *values_bf16, int64_t total_len, int64_t n_heads,
+                                         int64_t n_kv_heads, fo_geometry geometry, const float *sinks, float *output,
+                                         int64_t query_begin, int64_t query_end, fo_prefill_options options,
+                                         int32_t kv_splits) {
     if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    if (kv_splits < 1 || kv_splits > 64) return fail(FO_ERR_INVALID, "kv_splits must be 1..64");
     if (!q || !keys_bf16 || !values_bf16 || !sinks || !output) return fail(FO_ERR_INVALID, "null argument");
     if (!(total_len >= 4 && n_kv_heads >= 1 && n_heads >= n_kv_heads && n_heads % n_kv_heads == 0))
         return fail(FO_ERR_INVALID, "bad shape");
@@ -565,10 +579,17 @@ int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *
     if (!aligned16(keys_bf16) || !aligned16(values_bf16) || !aligned16(q) || !aligned16(output))
         return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
     DeviceGuard guard(ctx->device);
+    float *po = nullptr, *pml = nullptr;
+    if (kv_splits > 1) {
+        FO_CUDA(ctx->split_o.ensure((size_t)kv_splits * total_len * n_heads * 64 * 4), "cudaMalloc(split partials)");
+        FO_CUDA(ctx->split_ml.ensure((size_t)kv_splits * total_len * n_heads * 2 * 4), "cudaMalloc(split partials)");
+        po = (float *)ctx->split_o.ptr;
+        pml = (float *)ctx->split_ml.ptr;
+    }
     cudaError_t e = fo_launch_prefill_bf16(q, keys_bf16, values_bf16, sinks, output, total_len, n_heads, n_kv_heads,
                                            geometry.image_start, geometry.image_end, query_begin, query_end,
                                            options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST,
-                                           ctx->dev_err, ctx->stream);
+                                           ctx->dev_err, kv_splits, po, pml, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
     return FO_OK;
 }

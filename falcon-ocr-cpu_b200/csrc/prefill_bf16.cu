@@ -57,6 +57,11 @@ struct Bf16Args {
     unsigned *err;
     int64_t total, n_heads, n_kv_heads, image_start, image_end;
     int64_t pair_begin, pair_end;  // the 256-query pairs [begin, end) this launch computes
+    // Key-range split (SPLIT kernels): each pair's key tiles in n_split
+    // consecutive ranges, one CTA per range, writing unnormalized partials
+    // [n_split][T][H][64] and (max in log2 units, denominator) [n_split][T][H].
+    int n_split;
+    float *part_o, *part_ml;
 };
 
 // Bounded wait that ignores the abort flag (for copies/MMAs that complete on
@@ -67,7 +72,7 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t phase) {
         if (globaltimer() - t0 > FO_WAIT_NS) break;
 }
 
-template <bool STATIC>
+template <bool STATIC, bool SPLIT>
 __global__ void __launch_bounds__(BT_THREADS, 1)
     prefill_bf16_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, Bf16Args a) {
     extern __shared__ uint8_t smem_raw[];
@@ -86,7 +91,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     const int64_t T = a.total, H = a.n_heads;
     // Blocks start in index order, x fastest: every head of the heaviest
     // (latest) query pair first, so the longest CTAs start earliest.
-    const int64_t pair = a.pair_end - 1 - blockIdx.y;
+    const int64_t pair = a.pair_end - 1 - (SPLIT ? blockIdx.y / a.n_split : blockIdx.y);
     const int64_t head = blockIdx.x;
     const int64_t kv_head = head / (H / a.n_kv_heads);
     const int64_t q0 = pair * 256;
@@ -94,7 +99,29 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     const int64_t last_abs = min64(q0 + 255, T - 1);
     int64_t tile_end = last_abs + 1;
     if (q0 < a.image_end && last_abs >= a.image_start) tile_end = max64(tile_end, a.image_end);
-    const int nkv = (int)((tile_end + 127) / 128);
+    // This CTA's key tiles: [jbase, jbase + nkv) (all of them unless split).
+    int jbase = 0, nkv = (int)((tile_end + 127) / 128);
+    const int part = SPLIT ? (int)(blockIdx.y % a.n_split) : 0;
+    if constexpr (SPLIT) {
+        const int all = nkv;
+        jbase = (int)((int64_t)part * all / a.n_split);
+        nkv = (int)((int64_t)(part + 1) * all / a.n_split) - jbase;
+        if (nkv == 0) {
+            // An empty range (a pair with fewer tiles than ranges): an empty
+            // partial, before any barrier or tensor memory is set up.
+            if (threadIdx.x < 256) {
+                const int64_t row = q0 + threadIdx.x;
+                if (row < T) {
+                    const int64_t idx = ((int64_t)part * T + row) * H + head;
+                    float4 *dst = reinterpret_cast<float4 *>(a.part_o + idx * FO_HD);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float2 *>(a.part_ml + idx * 2) = make_float2(-INFINITY, 0.0f);
+                }
+            }
+            return;
+        }
+    }
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 256);
@@ -167,7 +194,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(s_empty + t);
-            const int nvis = (int)max64(0, min64(128, vend - 128 * (int64_t)j));
+            const int nvis = (int)max64(0, min64(128, vend - 128 * (int64_t)(jbase + j)));
             // Whole tile visible for every row of the warp: the common case
             // runs without any per-key mask (a separate copy of the loop).
             const bool full = __all_sync(0xffffffffu, nvis >= 128);
@@ -270,7 +297,16 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             FO_TMEM_LD32(o_tm, (o + 0));
             FO_TMEM_LD32(o_tm + 32, (o + 32));
             tmem_wait_ld();
-            if (row < T) {
+            if (SPLIT && row < T) {
+                // The range's unnormalized output, its max and denominator.
+                const int64_t idx = ((int64_t)part * T + row) * H + head;
+                float4 *dst = reinterpret_cast<float4 *>(a.part_o + idx * FO_HD);
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                         __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+                *reinterpret_cast<float2 *>(a.part_ml + idx * 2) = make_float2(STATIC ? 0.0f : m2, l);
+            } else if (row < T) {
                 const float lse = STATIC ? logf(l) : m2 * 0.69314718055994530942f + logf(l);
                 const float ss = sink_scale(a.sinks[head], lse);
                 float4 *dst = reinterpret_cast<float4 *>(a.out + (row * H + head) * FO_HD);
@@ -296,13 +332,13 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                 const int st = j % BT_STAGES, u = j / BT_STAGES;
                 if (u > 0 && !(ok = mbar_wait(k_empty + st, (u - 1) & 1, abort_flag, a.err))) break;
                 mbar_expect_tx(k_full + st, BT_TILE);
-                tma_load_3d(smem + OFF_K + st * BT_TILE, &tmk, k_full + st, 0, (int)head, 128 * j);
+                tma_load_3d(smem + OFF_K + st * BT_TILE, &tmk, k_full + st, 0, (int)head, 128 * (jbase + j));
                 if (u > 0 && !(ok = mbar_wait(v_empty + st, (u - 1) & 1, abort_flag, a.err))) {
                     issued = 2 * j + 1;
                     break;
                 }
                 mbar_expect_tx(v_full + st, BT_TILE);
-                tma_load_3d(smem + OFF_V + st * BT_TILE, &tmv, v_full + st, 0, (int)kv_head, 128 * j);
+                tma_load_3d(smem + OFF_V + st * BT_TILE, &tmv, v_full + st, 0, (int)kv_head, 128 * (jbase + j));
                 issued = 2 * j + 2;
             }
             if (!ok) {
@@ -427,6 +463,43 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
     }
 }
 
+// Combines the key ranges of a split launch in range order and applies the
+// sink: a warp per (row, head), two output dimensions per lane.  Static shift:
+// the ranges' outputs and denominators add (one fixed shift); online: each is
+// scaled by 2^(m_r - M) first.
+template <bool STATIC>
+__global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *part_o, const float *part_ml,
+                                                                  const float *sinks, float *out, int64_t T,
+                                                                  int64_t H, int64_t row0, int64_t rows,
+                                                                  int n_split) {
+    const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (w >= rows * H) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = row0 + w / H, head = w % H;
+    float M = 0.0f;
+    if constexpr (!STATIC) {
+        M = -INFINITY;
+        for (int r = 0; r < n_split; r++) M = rmax(M, part_ml[(((int64_t)r * T + row) * H + head) * 2]);
+    }
+    float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    for (int r = 0; r < n_split; r++) {
+        const int64_t idx = ((int64_t)r * T + row) * H + head;
+        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
+        float f = 1.0f;
+        if constexpr (!STATIC) {
+            if (ml.x == -INFINITY) continue;
+            f = exp2f(__fsub_rn(ml.x, M));
+        }
+        const float2 o = *reinterpret_cast<const float2 *>(part_o + idx * FO_HD + 2 * lane);
+        o0 = fmaf(o.x, f, o0);
+        o1 = fmaf(o.y, f, o1);
+        l = fmaf(ml.y, f, l);
+    }
+    const float lse = STATIC ? logf(l) : M * 0.69314718055994530942f + logf(l);
+    const float ss = sink_scale(sinks[head], lse);
+    *reinterpret_cast<float2 *>(out + (row * H + head) * FO_HD + 2 * lane) = make_float2((o0 / l) * ss, (o1 / l) * ss);
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (!fn) {
@@ -458,16 +531,19 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
                                               const float *sinks, float *out, int64_t total, int64_t n_heads,
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
                                               int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
-                                              unsigned *err, cudaStream_t stream) {
+                                              unsigned *err, int n_split, float *part_o, float *part_ml,
+                                              cudaStream_t stream) {
     (void)exp_fast;  // the tensor-core softmax always takes the hardware exp2
     if (total == 0 || query_end <= query_begin) return cudaSuccess;
+    if (n_split < 1 || (n_split > 1 && (!part_o || !part_ml))) return cudaErrorInvalidValue;
     CUtensorMap mk, mv;
     if (!fo::make_map(&mk, keys_bf16, total, n_heads) || !fo::make_map(&mv, values_bf16, total, n_kv_heads))
         return cudaErrorInvalidValue;
     const int64_t pb = query_begin / 256, pe = (query_end + 255) / 256;
-    fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe};
-    if (pe - pb > 65535) return cudaErrorInvalidValue;  // grid y limit: 16.7M query rows per launch
-    dim3 grid((unsigned)n_heads, (unsigned)(pe - pb));
+    fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe,
+                      n_split, part_o, part_ml};
+    if ((pe - pb) * n_split > 65535) return cudaErrorInvalidValue;  // grid y limit
+    dim3 grid((unsigned)n_heads, (unsigned)((pe - pb) * n_split));
     auto launch = [&](auto kernel) -> cudaError_t {
         cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fo::SMEM_BYTES);
@@ -475,5 +551,19 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
         kernel<<<grid, fo::BT_THREADS, fo::SMEM_BYTES, stream>>>(mk, mv, args);
         return cudaGetLastError();
     };
-    return softmax_static ? launch(fo::prefill_bf16_kernel<true>) : launch(fo::prefill_bf16_kernel<false>);
+    if (n_split == 1)
+        return softmax_static ? launch(fo::prefill_bf16_kernel<true, false>)
+                              : launch(fo::prefill_bf16_kernel<false, false>);
+    cudaError_t e = softmax_static ? launch(fo::prefill_bf16_kernel<true, true>)
+                                   : launch(fo::prefill_bf16_kernel<false, true>);
+    if (e != cudaSuccess) return e;
+    const int64_t rows = query_end - query_begin;
+    const unsigned blocks = (unsigned)((rows * n_heads + 7) / 8);
+    if (softmax_static)
+        fo::prefill_split_merge_kernel<true><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, total, n_heads,
+                                                                         query_begin, rows, n_split);
+    else
+        fo::prefill_split_merge_kernel<false><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, total,
+                                                                          n_heads, query_begin, rows, n_split);
+    return cudaGetLastError();
 }

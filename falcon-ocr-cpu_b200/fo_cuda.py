@@ -93,7 +93,7 @@ EXPORTS = [
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
     "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch", "fo_selftest_bounded_wait",
-    "fo_attention_prefill_bf16_rows", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
+    "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
     "fo_i8_decode_batch",
 ]
 
@@ -136,6 +136,8 @@ def lib() -> ctypes.CDLL:
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
         "fo_attention_prefill_bf16_rows": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64, PrefillOptions]),
+        "fo_attention_prefill_bf16_rows_split": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64,
+                                                     PrefillOptions, I]),
         "fo_i8_seal": (I, [P, P, P, I64, I64, I, ctypes.POINTER(P)]),
         "fo_i8_destroy": (I, [P]),
         "fo_i8_bytes": (I64, [P]),
@@ -272,10 +274,12 @@ def attention_prefill_bf16(q, k, v, geometry, sinks, output, n_heads, n_kv_heads
 
 
 def attention_prefill_bf16_rows(q, keys_bf16, values_bf16, geometry, sinks, output, n_heads, n_kv_heads, query_begin,
-                                query_end, options=None, ctx=None):
+                                query_end, options=None, ctx=None, kv_splits=1):
     """fo_attention_prefill_bf16_rows: the BF16 prefill of query rows
     [query_begin, query_end) of a pure prefix (CUDA tensors; BF16 keys and
-    values already converted).  Rows outside the range are left as they are."""
+    values already converted).  Rows outside the range are left as they are.
+    kv_splits > 1 cuts each query pair's keys into that many ranges
+    (fo_attention_prefill_bf16_rows_split)."""
     ctx = ctx or default_context()
     for a in (q, keys_bf16, values_bf16, sinks, output):
         if not _on_device(a) or not a.is_contiguous():
@@ -283,9 +287,16 @@ def attention_prefill_bf16_rows(q, keys_bf16, values_bf16, geometry, sinks, outp
     total = q.numel() // (n_heads * 64)
     if options is None:
         options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
-    check(lib().fo_attention_prefill_bf16_rows(ctx.handle, q.data_ptr(), keys_bf16.data_ptr(), values_bf16.data_ptr(),
-                                               total, n_heads, n_kv_heads, Geometry(*geometry), sinks.data_ptr(),
-                                               output.data_ptr(), query_begin, query_end, options))
+    if kv_splits == 1:
+        check(lib().fo_attention_prefill_bf16_rows(ctx.handle, q.data_ptr(), keys_bf16.data_ptr(),
+                                                   values_bf16.data_ptr(), total, n_heads, n_kv_heads,
+                                                   Geometry(*geometry), sinks.data_ptr(), output.data_ptr(),
+                                                   query_begin, query_end, options))
+    else:
+        check(lib().fo_attention_prefill_bf16_rows_split(ctx.handle, q.data_ptr(), keys_bf16.data_ptr(),
+                                                         values_bf16.data_ptr(), total, n_heads, n_kv_heads,
+                                                         Geometry(*geometry), sinks.data_ptr(), output.data_ptr(),
+                                                         query_begin, query_end, options, kv_splits))
     return output
 
 

@@ -61,11 +61,22 @@ def token_major(band_buffers: Sequence[torch.Tensor]) -> torch.Tensor:
     return torch.cat(parts, 0)
 
 
-def cuda_band(q, kb, vb, sinks, geometry, heads, groups, begin, end, out, ctx=None, options=None):
+def kv_splits_for(pairs: int, heads: int, sms: int) -> int:
+    """Key ranges per query pair so that a launch of `pairs` x `heads` CTAs
+    has at least two per SM (a rank holding few heads would otherwise wait on
+    its longest pairs): the smallest power of two up to 8."""
+    k = 1
+    while k < 8 and pairs * heads * k < 2 * sms:
+        k *= 2
+    return k
+
+
+def cuda_band(q, kb, vb, sinks, geometry, heads, groups, begin, end, out, ctx=None, options=None, kv_splits=1):
     """The CUDA computation of one band on one rank (fo_attention_prefill_bf16_rows)."""
     import fo_cuda as F
 
-    F.attention_prefill_bf16_rows(q, kb, vb, geometry, sinks, out, heads, groups, begin, end, options=options, ctx=ctx)
+    F.attention_prefill_bf16_rows(q, kb, vb, geometry, sinks, out, heads, groups, begin, end, options=options, ctx=ctx,
+                                  kv_splits=kv_splits)
 
 
 class ShardedPrefill:
@@ -80,7 +91,7 @@ class ShardedPrefill:
                  geometry: Sequence[int], n_heads: int, n_kv_heads: int, rank: int, world: int,
                  group: Optional[dist.ProcessGroup] = None, n_bands: int = 4,
                  compute: Optional[Callable] = None, out_dtype: torch.dtype = torch.bfloat16, ctx=None,
-                 stream: Optional["torch.cuda.Stream"] = None):
+                 stream: Optional["torch.cuda.Stream"] = None, kv_splits: Optional[int] = None):
         """q [T][H][64], k [T][H][64], v [T][G][64] hold either the whole page
         (this rank slices its heads) or only this rank's heads.  On GPUs,
         `ctx` must be bound to `stream` (both are created when not given)."""
@@ -103,10 +114,17 @@ class ShardedPrefill:
                          for b, e in self.bands]
         self.compute = compute or cuda_band
         self.cuda = q.is_cuda
+        self.kv_splits = 1
         if self.cuda:
             # The kernels run on the context's stream; the gathers on their own.
             import fo_cuda as F
 
+            if kv_splits is None:
+                sms = torch.cuda.get_device_properties(q.device).multi_processor_count
+                pairs = min((e - b + 255) // 256 for b, e in self.bands)
+                kv_splits = kv_splits_for(pairs, self.heads, sms)
+
+            self.kv_splits = kv_splits
             self.compute_stream = stream or torch.cuda.Stream(device=q.device)
             self.ctx = ctx or F.Context(q.device.index, stream=self.compute_stream.cuda_stream)
             self.comm_stream = torch.cuda.Stream(device=q.device)
@@ -126,7 +144,7 @@ class ShardedPrefill:
         """Computes this rank's heads band by band and gathers every band;
         returns the bands' rank-major buffers (complete for the caller's
         current stream on return)."""
-        kwargs = {"ctx": self.ctx} if self.compute is cuda_band else {}
+        kwargs = {"ctx": self.ctx, "kv_splits": self.kv_splits} if self.compute is cuda_band else {}
         if not self.cuda:
             for i in reversed(range(len(self.bands))):
                 b, e = self.bands[i]

@@ -159,6 +159,20 @@ int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *
                                    fo_geometry geometry, const float *sinks, float *output, int64_t query_begin,
                                    int64_t query_end, fo_prefill_options options);
 
+/* fo_attention_prefill_bf16_rows with each query pair's key tiles cut into
+ * kv_splits consecutive ranges (1..64), one CTA per range, combined in range
+ * order with the sink by a second kernel.  For launches with fewer query
+ * pairs x heads than the GPU has SMs (a band of a head-sharded page on many
+ * GPUs), where the longest pairs would otherwise bound the launch.  Results
+ * equal the unsplit call within rounding (the ranges' partial sums add in a
+ * different order); the partials live in context scratch
+ * (kv_splits x total_len x n_heads x 65 floats). */
+int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint16_t *keys_bf16,
+                                         const uint16_t *values_bf16, int64_t total_len, int64_t n_heads,
+                                         int64_t n_kv_heads, fo_geometry geometry, const float *sinks, float *output,
+                                         int64_t query_begin, int64_t query_end, fo_prefill_options options,
+                                         int32_t kv_splits);
+
 /* FP32 -> BF16 (round to nearest even) of n device values, the conversion
  * fo_attention_prefill_bf16 applies to Bf16Kv::Convert inputs. */
 int fo_convert_bf16(fo_ctx *ctx, const float *src, uint16_t *dst, int64_t n);

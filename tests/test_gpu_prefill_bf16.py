@@ -134,7 +134,7 @@ def test_sharded_prefill_on_one_rank_matches_the_whole_page(ctx):
     T = 1100
     q, k, v, s = (torch.from_numpy(x).cuda() for x in G.bf16_operands(T))
     sp = S.ShardedPrefill(q.view(T, 16, 64), k.view(T, 16, 64), v.view(T, 8, 64), s, (0, 0, 300), 16, 8, 0, 1,
-                          n_bands=3)
+                          n_bands=3, kv_splits=1)
     got = S.token_major(sp.run())
     whole = torch.zeros(T * 16 * 64, device="cuda")
     F.attention_prefill_bf16(q, k, v, (0, 0, 300), s, whole, 16, 8, ctx=ctx)
@@ -160,3 +160,53 @@ def test_host_buffers_pipeline_equals_device_call(ctx, T, image, pinned):
     F.attention_prefill_bf16(host[0], host[1], host[2], geo, torch.from_numpy(s), out, 16, 8, ctx=ctx)
     torch.cuda.synchronize()
     assert torch.equal(out, whole.cpu())
+
+
+@pytest.mark.parametrize("static", [True, False])
+@pytest.mark.parametrize("T,image,splits", [(1100, (0, 300), 2), (2000, (0, 0), 3), (6544, (0, 4096), 4),
+                                            (700, (5, 262), 8), (300, (0, 0), 5)])
+def test_key_range_split_equals_the_unsplit_rows(ctx, static, T, image, splits):
+    """fo_attention_prefill_bf16_rows_split: each pair's key tiles in ranges
+    (empty ones too, when a pair has fewer tiles than ranges), merged in range
+    order with the sink.  Static shift: equal to the unsplit rows up to the
+    rounding of the FP32 accumulations.  Online: each range rounds its probabilities to
+    BF16 against its own running maximum, so the split rows are held to the
+    online bound against float64 (and twice it against the unsplit rows)."""
+    q, k, v, s = (torch.from_numpy(x).cuda() for x in G.bf16_operands(T))
+    kb, vb = k.to(torch.bfloat16), v.to(torch.bfloat16)
+    geo = (0, image[0], image[1])
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC if static else F.SOFTMAX_ONLINE, F.SOFTMAX_ONLINE)
+    whole = torch.zeros(T * 16 * 64, device="cuda")
+    F.attention_prefill_bf16_rows(q, kb, vb, geo, s, whole, 16, 8, 0, T, options=opts, ctx=ctx)
+    split = torch.full((T * 16 * 64,), float("nan"), device="cuda")
+    b = 256 if T > 512 else 0
+    F.attention_prefill_bf16_rows(q, kb, vb, geo, s, split, 16, 8, 0, b, options=opts, ctx=ctx, kv_splits=splits)
+    F.attention_prefill_bf16_rows(q, kb, vb, geo, s, split, 16, 8, b, T, options=opts, ctx=ctx, kv_splits=splits)
+    torch.cuda.synchronize()
+    assert not torch.isnan(split).any()
+    if static:
+        # The tensor cores accumulate a range's outputs in FP32 over up to
+        # ~4,000 keys: a few hundred roundings of 2^-23 either way.
+        assert torch.allclose(split, whole, rtol=2e-4, atol=2e-5), float((split - whole).abs().max())
+        return
+    assert float((split - whole).abs().max()) <= 2 * ONLINE_BOUND
+    if T <= 1100:
+        ref = G.attention_f64(*(x.cpu().numpy() for x in (q, k, v)), 16, 8, 64, geo, s.cpu().numpy())
+        assert worst(split.cpu().numpy(), ref) <= ONLINE_BOUND
+
+
+def test_sharded_prefill_with_key_ranges_on_one_rank(ctx):
+    """The sharded driver's automatic key-range split (few pairs x heads per
+    band) against the whole page, within BF16 output rounding."""
+    import sharded as S
+    T = 1100
+    q, k, v, s = (torch.from_numpy(x).cuda() for x in G.bf16_operands(T))
+    sp = S.ShardedPrefill(q.view(T, 16, 64), k.view(T, 16, 64), v.view(T, 8, 64), s, (0, 0, 300), 16, 8, 0, 1,
+                          n_bands=3)
+    assert sp.kv_splits > 1
+    got = S.token_major(sp.run()).float()
+    whole = torch.zeros(T * 16 * 64, device="cuda")
+    F.attention_prefill_bf16(q, k, v, (0, 0, 300), s, whole, 16, 8, ctx=ctx)
+    torch.cuda.synchronize()
+    ref = whole.view(T, 16, 64)
+    assert torch.allclose(got, ref.to(torch.bfloat16).float(), rtol=2 ** -7, atol=1e-6)

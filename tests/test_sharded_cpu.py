@@ -26,6 +26,16 @@ def test_group_ranges_and_bands():
     assert S.bands(1000, 1) == [(0, 1000)]
 
 
+def test_key_range_splits_fill_the_gpu():
+    """Two CTAs per SM at least, in powers of two up to 8: C5b's 64 query
+    pairs on 148 SMs split at 4 ranks (4 heads) and 8 ranks (2 heads)."""
+    assert S.kv_splits_for(64, 16, 148) == 1
+    assert S.kv_splits_for(64, 8, 148) == 1
+    assert S.kv_splits_for(64, 4, 148) == 2
+    assert S.kv_splits_for(64, 2, 148) == 4
+    assert S.kv_splits_for(1, 2, 148) == 8
+
+
 def oracle_band(q, kb, vb, sinks, geometry, heads, groups, begin, end, out):
     """Rows [begin, end) of the BF16 static-shift tiles on this rank's heads."""
     full = O.prefill_bf16(q.numpy().reshape(-1), kb.float().numpy().reshape(-1), vb.float().numpy().reshape(-1),
