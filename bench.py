@@ -393,7 +393,8 @@ def time_sharded(run, args):
     kd = torch.from_numpy(k.reshape(T, HEADS, 64)).to(run.dev)
     vd = torch.from_numpy(v.reshape(T, KV_HEADS, 64)).to(run.dev)
     sd = torch.from_numpy(sinks).to(run.dev)
-    sp = S.ShardedPrefill(qd, kd, vd, sd, geo, HEADS, KV_HEADS, run.rank, run.world, n_bands=args.bands)
+    sp = S.ShardedPrefill(qd, kd, vd, sd, geo, HEADS, KV_HEADS, run.rank, run.world, n_bands=args.bands,
+                          kv_splits=args.kv_splits or None)
     for _ in range(max(args.warmup, 3)):
         sp.run()
     steps = max(3, min(args.steps, 20))
@@ -413,7 +414,8 @@ def time_sharded(run, args):
     gathered_bytes = T * HEADS * 64 * 2
     achieved = flop / (ms / 1e3) / 1e12
     out = {"workload": "C5b: 16,384-token causal prefill, heads sharded by KV group, BF16 output all-gathered",
-           "tokens": T, "ranks": run.world, "bands": len(sp.bands), "ms_per_step": round(ms, 4),
+           "tokens": T, "ranks": run.world, "bands": len(sp.bands), "kv_splits": sp.kv_splits,
+           "ms_per_step": round(ms, 4),
            "tok_per_s": round(T / (ms / 1e3), 1), "gflop": round(flop / 1e9, 1), "tflops": round(achieved, 1),
            "frac_of_world_peak": round(achieved / (run.world * run.peaks["bf16_tflops"]), 4),
            "gather_bytes": gathered_bytes, "max_abs_diff_vs_one_gpu": check}
@@ -598,6 +600,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--kv-splits", type=int, default=0,
+                    help="key ranges per query pair in the sharded prefill (0: chosen from the CTA count)")
     ap.add_argument("--bands", type=int, default=1,
                     help="query-row bands of the sharded prefill (C5b); one band measured fastest at 2 ranks")
     ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded"], default="full",
