@@ -27,12 +27,12 @@ def test_group_ranges_and_bands():
 
 
 def test_key_range_splits_fill_the_gpu():
-    """Two CTAs per SM at least, in powers of two up to 8: C5b's 64 query
-    pairs on 148 SMs split at 4 ranks (4 heads) and 8 ranks (2 heads)."""
+    """One CTA per SM at least, in powers of two up to 8: C5b's 64 query
+    pairs on 148 SMs split only at 8 ranks (2 heads each)."""
     assert S.kv_splits_for(64, 16, 148) == 1
     assert S.kv_splits_for(64, 8, 148) == 1
-    assert S.kv_splits_for(64, 4, 148) == 2
-    assert S.kv_splits_for(64, 2, 148) == 4
+    assert S.kv_splits_for(64, 4, 148) == 1
+    assert S.kv_splits_for(64, 2, 148) == 2
     assert S.kv_splits_for(1, 2, 148) == 8
 
 
