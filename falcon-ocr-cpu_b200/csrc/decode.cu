@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 namespace fo {
@@ -723,13 +724,17 @@ bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t
 constexpr int MERGE_DSMEM_MAX = 200 * 1024;
 static cudaError_t launch_merge(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
                                 int64_t groups, int max_splits, int rows, cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
+    // The attribute belongs to each device's context: set once per device.
+    static std::atomic<unsigned long long> configured{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
         // The kernel's own static array sits beside the dynamic allowance.
         cudaError_t e =
             cudaFuncSetAttribute(fo::merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MERGE_DSMEM_MAX);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured.fetch_or(bit);
     }
     const size_t smem = (size_t)(2 * max_splits + 4 + fo::MERGE_SLICES * FO_HD) * sizeof(float);
     if (smem > MERGE_DSMEM_MAX) return cudaErrorInvalidValue;
@@ -755,22 +760,27 @@ static cudaError_t launch_one(const fo_decode_page &page0, const fo_decode_page 
                               int64_t groups, int max_splits, cudaStream_t stream) {
     constexpr int smem = fo::Smem<F, R>::BYTES;
     constexpr int threads = fo::Shape<F>::THREADS;
-    static int resident = 0;  // CTAs of this instantiation the device holds at once
-    if (!resident) {
-        cudaError_t e =
-            cudaFuncSetAttribute(fo::decode_kernel<F, FAST, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    // CTAs of this instantiation each device holds at once (the attribute and
+    // the occupancy belong to each device's context: set up once per device).
+    static std::atomic<int> resident[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int res = resident[dev & 63].load();
+    if (!res) {
+        e = cudaFuncSetAttribute(fo::decode_kernel<F, FAST, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        int dev = 0, sms = 0, per_sm = 0;
-        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+        int sms = 0, per_sm = 0;
         if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fo::decode_kernel<F, FAST, R>, threads, smem);
         if (e != cudaSuccess) return e;
-        resident = std::max(1, sms * per_sm);
+        res = std::max(1, sms * per_sm);
+        resident[dev & 63].store(res);
     }
     const int64_t items = n_pages * (int64_t)max_splits * groups;
-    const unsigned grid = (unsigned)std::min<int64_t>(items, resident);
+    const unsigned grid = (unsigned)std::min<int64_t>(items, res);
     fo::decode_kernel<F, FAST, R><<<grid, threads, smem, stream>>>(page0, dev_pages, n_pages, groups, max_splits);
-    cudaError_t e = cudaGetLastError();
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_merge(page0, dev_pages, n_pages, groups, max_splits, R, stream);
 }

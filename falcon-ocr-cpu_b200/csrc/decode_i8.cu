@@ -22,6 +22,7 @@
 #include "sm100.cuh"
 
 #include <algorithm>
+#include <atomic>
 
 namespace fo {
 
@@ -260,15 +261,19 @@ extern "C" cudaError_t fo_launch_decode_i8(const fo_i8_page *dev_pages, int64_t 
                                            int32_t max_splits, int fast_exp, cudaStream_t stream) {
     if (n_pages <= 0 || max_splits <= 0) return cudaSuccess;
     dim3 grid((unsigned)max_splits, (unsigned)heads, (unsigned)n_pages);
-    static bool configured = false;
-    if (!configured) {
+    // The attribute belongs to each device's context: set once per device.
+    static std::atomic<unsigned long long> configured{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(configured.load() & bit)) {
         cudaError_t e = cudaFuncSetAttribute(fo::decode_i8_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              fo::I8_DSMEM);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(fo::decode_i8_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      fo::I8_DSMEM);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured.fetch_or(bit);
     }
     if (fast_exp)
         fo::decode_i8_kernel<true><<<grid, fo::I8_THREADS, fo::I8_DSMEM, stream>>>(dev_pages, heads);

@@ -105,3 +105,31 @@ def test_a_cache_twice_in_one_batch_is_refused(ctx):
     with pytest.raises(F.FoError):
         F.int8_decode_batch([c, c], [qd, qd], [sd, sd], [od, od])
     c.close()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_one_process_decodes_on_a_second_device():
+    """Launch attributes (the INT8 kernel's 64 KB of shared memory, the split
+    merge's allowance) belong to each device: a process that decodes on
+    device 0 and then on device 1 gets the same results on both."""
+    k, v, q, sinks = page(3000, 7)
+    outs = []
+    for d in (0, 1):
+        c = F.Context(d)
+        with torch.cuda.device(d):
+            cache = F.Int8Cache(torch.from_numpy(k).to(d), torch.from_numpy(v).to(d), ctx=c)
+            out = torch.zeros(16 * 64, device=d)
+            F.int8_decode_batch([cache], [torch.from_numpy(q).to(d)], [torch.from_numpy(sinks).to(d)], [out])
+            kk = k.copy()  # a split cache needs each pair's temporal halves equal
+            kk[:, 1::2, :32] = kk[:, 0::2, :32]
+            vv = np.ascontiguousarray(v[:, :8])
+            split = F.SplitPrefix.from_compact(torch.from_numpy(kk).to(d), torch.from_numpy(vv).to(d), 3000, 3001,
+                                               fmt="q8", ctx=c)
+            o2 = torch.zeros(16 * 64, device=d)
+            split.attention_decode(torch.from_numpy(q.reshape(-1)).to(d), 3000, torch.from_numpy(sinks).to(d), o2)
+            torch.cuda.synchronize(d)
+            outs.append((out.cpu(), o2.cpu()))
+            split.close()
+            cache.close()
+        c.close()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
