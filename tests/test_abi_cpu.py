@@ -129,3 +129,16 @@ def test_null_handles_are_rejected():
     assert L.fo_i8_bytes(None) == -1 and L.fo_i8_destroy(None) == F.OK
     h = ctypes.c_void_p()
     assert L.fo_ctx_create(-1, None, ctypes.byref(h)) != F.OK
+
+
+def test_row_band_entries_reject_a_null_context():
+    """The row-band prefill entries (whole and split) refuse a null context
+    before touching a device, whatever the number of key ranges."""
+    L = F.lib()
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
+    g = F.Geometry(0, 0, 0)
+    assert L.fo_attention_prefill_bf16_rows(None, None, None, None, 256, 16, 8, g, None, None, 0, 256,
+                                            opts) == F.ERR_INVALID
+    for splits in (1, 0, 65):
+        assert L.fo_attention_prefill_bf16_rows_split(None, None, None, None, 256, 16, 8, g, None, None, 0, 256,
+                                                      opts, splits) == F.ERR_INVALID
