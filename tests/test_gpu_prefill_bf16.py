@@ -210,3 +210,13 @@ def test_sharded_prefill_with_key_ranges_on_one_rank(ctx):
     torch.cuda.synchronize()
     ref = whole.view(T, 16, 64)
     assert torch.allclose(got, ref.to(torch.bfloat16).float(), rtol=2 ** -7, atol=1e-6)
+
+
+def test_key_range_split_rejects_out_of_range_counts(ctx):
+    T = 300
+    q, k, v, s = (torch.from_numpy(x).cuda() for x in G.bf16_operands(T))
+    kb, vb = k.to(torch.bfloat16), v.to(torch.bfloat16)
+    out = torch.zeros(T * 16 * 64, device="cuda")
+    for splits in (0, 65):
+        with pytest.raises(F.FoError):
+            F.attention_prefill_bf16_rows(q, kb, vb, (0, 0, 0), s, out, 16, 8, 0, T, ctx=ctx, kv_splits=splits)
