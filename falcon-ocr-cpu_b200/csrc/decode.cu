@@ -605,6 +605,12 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
     const int64_t row_head = blockIdx.x;
     const int64_t r = row_head / H, h = row_head % H;
     if (r >= pp->rows) return;
+    if (pp->err && *reinterpret_cast<volatile unsigned *>(pp->err)) {
+        // A bounded wait of the decode gave up: its partials are stale, so the
+        // row is NaN rather than a plausible wrong answer.
+        if (threadIdx.x < FO_HD) pp->out[row_head * FO_HD + threadIdx.x] = __int_as_float(0x7fc00000);
+        return;
+    }
     const int splits = pp->splits;
     const int64_t row_len = pp->last - pp->rows + 1 + r;
     const int n = (int)((row_len + FO_SPLIT - 1) / FO_SPLIT);

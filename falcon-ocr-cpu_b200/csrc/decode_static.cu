@@ -16,11 +16,17 @@
 //
 // The first call on each device looks the array's device address up
 // (cudaGetSymbolAddress, with that device current); make that first call
-// before any stream capture.  All calls share the one array: calls whose
-// kernels overlap on the GPU (other streams, other threads) race on it and
-// must be serialized by the caller.  The decode kernel writes every partial
-// that the merge kernel after it reads, so nothing in the array needs
-// initializing or clearing between calls.
+// before any stream capture.  A lookup that fails is not remembered: the next
+// call tries again.  All calls share the one array: calls whose kernels
+// overlap on the GPU (other streams, other threads) race on it and must be
+// serialized by the caller.  The decode kernel writes every partial that the
+// merge kernel after it reads, so nothing in the array needs initializing or
+// clearing between calls.
+//
+// Errors the kernels find on the device (a bounded wait that gave up) land in
+// a second static word: the merge kernel then writes NaN outputs instead of
+// stale partials, and fo_decode_static_scratch_status reports the word (and
+// clears it) once the caller's stream has drained.
 #include <cstdio>
 #include <mutex>
 
@@ -39,15 +45,39 @@
 // The decode partials: split outputs [rows][heads][splits][64], then their
 // (max, denominator) [rows][heads][splits][2].
 static __device__ __align__(256) float g_decode_scratch[FO_STATIC_FLOATS];
+// Error bits of the kernels these calls launch (FO_DEVERR_*; 0 when none).
+static __device__ unsigned g_decode_static_err;
 
 namespace {
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
+std::mutex g_setup_mutex;
 float *g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices];
+unsigned *g_err_ptr[kMaxDevices];
 
 thread_local char g_msg[256];
+
+// The device addresses of the static array and error word on the current
+// device `dev`, looked up once; a failed lookup is retried on the next call.
+cudaError_t device_symbols(int dev, float **scratch, unsigned **err) {
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    if (!g_scratch_ptr[dev] || !g_err_ptr[dev]) {
+        void *p = nullptr, *w = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&w, g_decode_static_err);
+        if (e != cudaSuccess || !p || !w) {
+            cudaGetLastError();  // the failed lookup is not left pending for the caller
+            return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+        }
+        g_scratch_ptr[dev] = static_cast<float *>(p);
+        g_err_ptr[dev] = static_cast<unsigned *>(w);
+    }
+    *scratch = g_scratch_ptr[dev];
+    *err = g_err_ptr[dev];
+    return cudaSuccess;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 }  // namespace
 
@@ -65,6 +95,13 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
         return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: coded records need their scales");
     if (format < FO_KV_F32 || format > FO_KV_BF16)
         return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: unknown record format");
+    // The records are staged with bulk copies (16-byte aligned sources); the
+    // queries are read two floats at a time, the scales as 16-bit words.
+    if (!aligned(codes, 16) || (tail_len > 0 && !aligned(tail_codes, 16)) || !aligned(q, 8) ||
+        !aligned(output, 4) || !aligned(sinks, 4) || (scales && !aligned(scales, 2)) ||
+        (tail_scales && !aligned(tail_scales, 2)))
+        return fo_internal_fail(FO_ERR_INVALID,
+                                "static-scratch decode: codes and tail_codes must be 16-byte aligned, q 8-byte aligned");
     if (!(n_kv_heads >= 1 && n_heads == 2 * n_kv_heads))
         return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: heads must be paired GQA heads");
     if (!(prefix_len >= 1 && tail_len >= 0 && prefix_stride >= prefix_len && tail_stride >= tail_len))
@@ -84,14 +121,11 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
     if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return fo_internal_fail(FO_ERR_CUDA, "static-scratch decode: no usable current device");
     // Once per device, with that device current: the array's device address.
-    std::call_once(g_once[dev], [dev] {
-        void *p = nullptr;
-        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_decode_scratch);
-        g_scratch_ptr[dev] = static_cast<float *>(p);
-    });
-    if (g_scratch_err[dev] != cudaSuccess || !g_scratch_ptr[dev]) {
-        snprintf(g_msg, sizeof g_msg, "static-scratch decode: cudaGetSymbolAddress failed: %s",
-                 cudaGetErrorString(g_scratch_err[dev]));
+    float *base = nullptr;
+    unsigned *err_word = nullptr;
+    e = device_symbols(dev, &base, &err_word);
+    if (e != cudaSuccess) {
+        snprintf(g_msg, sizeof g_msg, "static-scratch decode: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
         return fo_internal_fail(FO_ERR_CUDA, g_msg);
     }
     fo_decode_page p{};
@@ -102,7 +136,7 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
     p.q = q;
     p.sinks = sinks;
     p.out = output;
-    float *base = g_scratch_ptr[dev];
+    p.err = err_word;
     p.part_o = base;
     p.part_ml = base + FO_STATIC_O_FLOATS;
     p.has_map = fo_make_record_map(&p.rec_map, codes, format, prefix_len, prefix_stride, n_kv_heads) ? 1 : 0;
@@ -115,6 +149,37 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
     e = fo_launch_decode_one(&p, format, n_kv_heads, fast_exp != 0, (cudaStream_t)stream);
     if (e != cudaSuccess) {
         snprintf(g_msg, sizeof g_msg, "static-scratch decode launch: %s", cudaGetErrorString(e));
+        return fo_internal_fail(FO_ERR_CUDA, g_msg);
+    }
+    return FO_OK;
+}
+
+extern "C" int fo_decode_static_scratch_status(void *stream) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return fo_internal_fail(FO_ERR_CUDA, "static-scratch status: no usable current device");
+    float *base = nullptr;
+    unsigned *err_word = nullptr;
+    if ((e = device_symbols(dev, &base, &err_word)) != cudaSuccess) {
+        snprintf(g_msg, sizeof g_msg, "static-scratch status: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        return fo_internal_fail(FO_ERR_CUDA, g_msg);
+    }
+    const cudaStream_t st = (cudaStream_t)stream;
+    unsigned bits = 0;
+    e = cudaMemcpyAsync(&bits, err_word, sizeof bits, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && bits) e = cudaMemsetAsync(err_word, 0, sizeof bits, st);
+    if (e == cudaSuccess && bits) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        snprintf(g_msg, sizeof g_msg, "static-scratch status: %s", cudaGetErrorString(e));
+        return fo_internal_fail(FO_ERR_CUDA, g_msg);
+    }
+    if (bits) {
+        snprintf(g_msg, sizeof g_msg,
+                 "static-scratch decode: a kernel wait exceeded its time limit (bits 0x%x); the outputs of the "
+                 "calls since the last status check are NaN",
+                 bits);
         return fo_internal_fail(FO_ERR_CUDA, g_msg);
     }
     return FO_OK;

@@ -92,7 +92,8 @@ EXPORTS = [
     "fo_attention", "fo_attention_prefill_bf16", "fo_convert_bf16", "fo_kv_seal", "fo_kv_destroy",
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
-    "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch", "fo_selftest_bounded_wait",
+    "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
+    "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
     "fo_i8_decode_batch",
 ]
@@ -134,6 +135,7 @@ def lib() -> ctypes.CDLL:
         "fo_kv_attention_decode_rows": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_batch": (I, [PP, I64, PP, PP, PP]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
+        "fo_decode_static_scratch_status": (I, [P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
         "fo_attention_prefill_bf16_rows": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64, PrefillOptions]),
         "fo_attention_prefill_bf16_rows_split": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64,
@@ -438,3 +440,25 @@ def decode_rows_static_scratch(cache: SplitPrefix, fmt, q, rows, sinks, output, 
                                               cache.tail_len, ts, cache.heads, cache.heads // 2, q.data_ptr(), rows,
                                               sinks.data_ptr(), int(bool(fast_exp)), output.data_ptr(), stream))
     return output
+
+
+def static_scratch_status(stream=None):
+    """fo_decode_static_scratch_status: raises CudaError if a bounded device
+    wait of a static-scratch decode gave up since the last check."""
+    check(lib().fo_decode_static_scratch_status(stream))
+
+
+class _DeviceArray:
+    """A raw device pointer as a CUDA array (__cuda_array_interface__)."""
+
+    def __init__(self, ptr, n, dtype):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": np.dtype(dtype).str, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_to_host(ptr, n, dtype):
+    """n elements of device memory at `ptr` (e.g. from SplitPrefix.records)
+    copied to a numpy array through torch (tests and tooling)."""
+    import torch
+    torch.cuda.synchronize()
+    return torch.as_tensor(_DeviceArray(ptr, n, dtype), device="cuda").cpu().numpy().copy()

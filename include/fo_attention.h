@@ -20,6 +20,15 @@
  *   fo_kv_attention_decode_batch one decode row per page, as Model::decode_batch_next
  *                                  calls LayerCache::attention per page (src/model/mod.rs:827-852)
  *
+ * Entry points with no single reference counterpart (each says why below):
+ *   fo_attention_prefill_bf16_rows[_split]  query-row bands of the BF16 prefill
+ *                                  (the head-sharded multi-GPU prefill's unit)
+ *   fo_convert_bf16                the Bf16Kv::Convert rounding on its own
+ *   fo_decode_rows_static_scratch  verify decode with no device allocation,
+ *   fo_decode_static_scratch_status  and its device error report
+ *   fo_i8_*                        BASELINE config 4's INT8 KV format
+ *   fo_selftest_bounded_wait       the kernels' bounded-wait failure path
+ *
  * Conventions (mirroring the reference's, src/kernels/attention/mod.rs:159-195
  * and src/quant/kv.rs:248-295):
  *   - Every call returns an fo_status; FO_OK is 0.  Shape violations that the
@@ -140,7 +149,10 @@ int fo_attention(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t q
  * (Bf16Kv::Converted); when NULL the call converts kv's FP32 keys and
  * values into context scratch (Bf16Kv::Convert).  options.softmax selects
  * online or static shift; the static shift requires every score
- * |q.k| / 8 to stay below 80 (per-head RMS norms keep it below 8). */
+ * |q.k| / 8 to stay below 80 (per-head RMS norms keep it below 8).  As in the
+ * reference, which selects the static shift without checking scores, the
+ * bound is not checked: outside it the static shift's results are undefined
+ * (denominators overflow to inf or underflow to 0). */
 int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *kv, int64_t query_len,
                               fo_geometry geometry, const float *sinks, float *output, const uint16_t *keys_bf16,
                               const uint16_t *values_bf16, fo_prefill_options options, int mem);
@@ -229,14 +241,24 @@ int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const fl
  * is the default stream); results equal fo_kv_attention_decode_rows'.  The
  * split partials live in one static device array of about 4.1 MiB that every
  * GPU loading the library holds until exit, which limits a call to 8 rows,
- * 16 heads and 16,384 positions (FO_ERR_CAPACITY beyond).  The first call on
- * a device looks the array up and should come before any stream capture;
- * calls that overlap on the GPU share the array and race. */
+ * 16 heads and 16,384 positions (FO_ERR_CAPACITY beyond).  codes and
+ * tail_codes must be 16-byte aligned and q 8-byte aligned (FO_ERR_INVALID
+ * otherwise).  The first call on a device looks the array up and should come
+ * before any stream capture (a failed lookup is retried by the next call);
+ * calls that overlap on the GPU share the array and race.  If a bounded
+ * device wait of a call gives up, that call's outputs are NaN and the next
+ * fo_decode_static_scratch_status reports it. */
 int fo_decode_rows_static_scratch(const void *codes, const uint16_t *scales, const void *tail_codes,
                                   const uint16_t *tail_scales, int32_t format, int64_t prefix_len,
                                   int64_t prefix_stride, int64_t tail_len, int64_t tail_stride, int64_t n_heads,
                                   int64_t n_kv_heads, const float *q, int64_t rows, const float *sinks,
                                   int32_t fast_exp, float *output, void *stream);
+/* Device status of fo_decode_rows_static_scratch on the current device (no
+ * counterpart in the reference): synchronizes `stream`, then returns
+ * FO_ERR_CUDA if a bounded wait of any call since the last check gave up
+ * (those calls wrote NaN outputs) and clears the report; FO_OK otherwise.
+ * Allocates nothing. */
+int fo_decode_static_scratch_status(void *stream);
 
 /* BASELINE config 4's INT8 KV format (no counterpart in the reference,
  * whose INT8 KV is the Q8 record format above): keys and values of every head

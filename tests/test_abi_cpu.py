@@ -142,3 +142,17 @@ def test_row_band_entries_reject_a_null_context():
     for splits in (1, 0, 65):
         assert L.fo_attention_prefill_bf16_rows_split(None, None, None, None, 256, 16, 8, g, None, None, 0, 256,
                                                       opts, splits) == F.ERR_INVALID
+
+
+def test_static_scratch_decode_refuses_misaligned_pointers_before_any_device_call():
+    """fo_decode_rows_static_scratch stages records with bulk copies from
+    16-byte aligned addresses and reads q two floats at a time: misaligned
+    pointers are refused on the host (this runs without a GPU)."""
+    buf = np.zeros(4096, np.float32)
+    base = (buf.ctypes.data + 15) & ~15
+    L = F.lib()
+    for codes, tail, q in ((base + 8, base, base), (base, base + 4, base), (base, base, base + 4)):
+        st = L.fo_decode_rows_static_scratch(codes, base, tail, base, F.KV_Q8, 10, 10, 2, 2, 16, 8, q, 2, base, 0,
+                                             base, None)
+        assert st == F.ERR_INVALID
+        assert "aligned" in last_error()
