@@ -5,8 +5,6 @@ of the float64 attention over the dequantized cache, and within BASELINE's
 INT8 tolerance (2e-2 * (1 + |b|)) of attention over the unquantized keys and
 values."""
 
-import ctypes
-
 import numpy as np
 import pytest
 
@@ -16,18 +14,10 @@ import fo_cuda as F
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-_CUDART = None
-
 
 def d2h(ptr, n, dtype):
-    global _CUDART
-    if _CUDART is None:
-        _CUDART = ctypes.CDLL("/usr/local/cuda/lib64/libcudart.so.12")
-    out = np.empty(n, dtype)
-    torch.cuda.synchronize()
-    assert _CUDART.cudaMemcpy(ctypes.c_void_p(out.ctypes.data), ctypes.c_void_p(ptr), ctypes.c_size_t(out.nbytes),
-                              2) == 0
-    return out
+    """Copy n elements of device memory at `ptr` to a numpy array."""
+    return F.device_to_host(ptr, n, dtype)
 
 
 @pytest.fixture(scope="module")

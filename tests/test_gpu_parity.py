@@ -159,20 +159,9 @@ def sealed_pair(fmt, p, generated, seed, capacity=None):
     return ref, gpu, q
 
 
-_CUDART = None
-
-
 def d2h(ptr, n, dtype):
     """Copy n elements of device memory at `ptr` to a numpy array."""
-    global _CUDART
-    import ctypes
-    if _CUDART is None:
-        _CUDART = ctypes.CDLL("/usr/local/cuda/lib64/libcudart.so.12")
-    out = np.empty(n, dtype)
-    torch.cuda.synchronize()
-    assert _CUDART.cudaMemcpy(ctypes.c_void_p(out.ctypes.data), ctypes.c_void_p(ptr), ctypes.c_size_t(out.nbytes),
-                              2) == 0  # cudaMemcpyDeviceToHost
-    return out
+    return F.device_to_host(ptr, n, dtype)
 
 
 def device_records(gpu, fmt, groups):
