@@ -17,8 +17,11 @@ on the data path (weak scaling); timing is the max over ranks of CUDA-event
 time, bracketed by barriers and synchronizes.
 
 --impl reference times the reference's algorithm on the host cores instead:
-the C restatement of its CPU prefill tiles (oracle/, OpenMP over all
-threads), since the Rust reference cannot be built here.
+the reference's production CPU kernels restated in C with the same x86
+vector instructions (oracle/fo_cpu_simd.c: AVX-512 BF16 static-shift prefill
+tiles on all logical cores, AVX2 verify decode over F32 records on the
+physical cores), since the Rust reference cannot be built here.  Prefill
+pages and decode steps interleave; each reports the median.
 """
 
 from __future__ import annotations
@@ -136,45 +139,123 @@ def host_cores():
 
 
 # ------------------------------------------------------------------ CPU arm
-def cpu_prefill_page(q, k, v, sinks, image_end):
-    """Seconds for one full page (all 16 heads) of the oracle's BF16 static
-    tiles: the reference's fast-mode prefill restated in C, OpenMP over all
-    host threads."""
-    import oracle as O
-    t0 = time.perf_counter()
-    O.prefill_bf16(q, k, v, HEADS, KV_HEADS, (0, image_end), sinks, softmax_static=True)
-    return time.perf_counter() - t0
+CPU_SAMPLE_S = 10.0  # the cpu_baseline leg repeats whole pages for at least this long
 
 
-CPU_SAMPLE_S = 10.0  # the CPU baseline repeats whole pages for at least this long
+def bench_config(world):
+    """The workload both arms time (identical config keys and values)."""
+    return {"workload": "C2 full-page prefill attention, 6,544 tokens (4,096 image + 2,448 text), 16 heads x 64, "
+                        "8 KV heads, BF16 static-shift softmax, one page per step",
+            "global_batch": world, "seq_len": SEQ, "parallelism": f"pages x{world}",
+            "l2": "inputs rotate over more than 3x L2"}
+
+
+class CpuReference:
+    """The reference's CPU path on the host cores: oracle/fo_cpu_simd.c (its
+    production SIMD kernels restated with the same instructions; bitwise
+    equal to the scalar restatement, tests/test_cpu_baseline.py).  Prefill:
+    BF16 static-shift tiles (AVX-512 BF16) over all logical cores, or the
+    scalar restatement when the host lacks AVX512-BF16.  Decode: 5-row verify
+    over F32 split records at 16,384 positions (AVX2) on the physical cores,
+    as the reference's thread policy has it."""
+
+    def __init__(self):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import cpu_simd as C
+        import generators as G
+        import oracle as O
+        self.C, self.O = C, O
+        self.host = C.host_description()
+        self.logical = C.max_threads()
+        self.physical = self.host.get("physical") or self.logical
+        self.q, self.k, self.v, self.sinks, _ = G.c2_inputs(seed=1)
+        self.out = np.empty(self.q.size, np.float32)
+        self.simd = C.has_bf16()
+        rng = np.random.default_rng(2)
+        p = DECODE_L - DECODE_ROWS
+        kp = rng.standard_normal((p, HEADS, 64)).astype(np.float32)
+        kp[:, 1::2, :32] = kp[:, 0::2, :32]
+        vp = rng.standard_normal((p, KV_HEADS, 64)).astype(np.float32)
+        self.cache = O.SplitCache(kp, vp, p, DECODE_L, fmt=O.F32)
+        tail = rng.standard_normal((DECODE_ROWS, KV_HEADS, 64)).astype(np.float32)
+        for t in range(DECODE_ROWS):
+            self.cache.push(tail[t], tail[t])
+        self.dq = rng.standard_normal(DECODE_ROWS * HEADS * 64).astype(np.float32)
+        self.ds = rng.standard_normal(HEADS).astype(np.float32)
+        self.dout = np.empty(DECODE_ROWS * HEADS * 64, np.float32)
+        self.decode_ok = C.has_avx2()
+
+    def prefill_page(self):
+        C = self.C
+        C.set_threads(self.logical)
+        t0 = time.perf_counter()
+        if self.simd:
+            C.prefill_bf16_static(self.q, self.k, self.v, HEADS, KV_HEADS, (0, IMAGE_END), self.sinks, self.out)
+        else:
+            self.O.prefill_bf16(self.q, self.k, self.v, HEADS, KV_HEADS, (0, IMAGE_END), self.sinks,
+                                softmax_static=True)
+        return time.perf_counter() - t0
+
+    def decode_step(self):
+        if not self.decode_ok:
+            return None
+        C = self.C
+        C.set_threads(self.physical)
+        t0 = time.perf_counter()
+        C.decode_rows_f32(self.cache, self.dq, DECODE_ROWS, self.ds, self.dout)
+        dt = time.perf_counter() - t0
+        C.set_threads(self.logical)
+        return dt
+
+    def run(self, steps, warmup, min_seconds=0.0):
+        """Interleaved prefill pages and decode steps: warmup of each, then
+        at least `steps` of each (and at least min_seconds of prefill)."""
+        for _ in range(warmup):
+            self.prefill_page()
+            self.decode_step()
+        pre, dec = [], []
+        while len(pre) < steps or sum(pre) < min_seconds:
+            pre.append(self.prefill_page())
+            d = self.decode_step()
+            if d is not None:
+                dec.append(d)
+        return pre, dec
+
+    def describe(self, pre, dec):
+        med = statistics.median(pre)
+        kind = "AVX-512 BF16 static-shift tiles" if self.simd else "scalar restatement (host lacks AVX512-BF16)"
+        out = {"value": round(SEQ / med, 1), "unit": "tok/s", "cores": self.logical, "kind": "port",
+               "sample": f"median of {len(pre)} interleaved full C2 pages ({med:.3f} s each, {sum(pre):.1f} s in "
+                         f"all), {kind}, {self.logical} threads; C restatement of the reference's prefill64/bf16 "
+                         f"kernels (oracle/fo_cpu_simd.c)",
+               "host": {"model": self.host.get("model"), "logical": self.logical, "physical": self.physical,
+                        "flags": self.host.get("flags")}}
+        if dec:
+            out["decode_us_per_step"] = round(statistics.median(dec) * 1e6, 1)
+            out["decode_sample"] = (f"median of {len(dec)} interleaved C3 steps: 5 verify rows over F32 records at "
+                                    f"{DECODE_L:,} positions, AVX2 pair_rows on {self.physical} threads")
+        return out
 
 
 def run_reference(args, world, rank):
     """--impl reference: the reference algorithm on the host cores (rank 0)."""
     if rank != 0:
         return
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import generators as G
-    import oracle as O
-    q, k, v, sinks, geo = G.c2_inputs(seed=1)
-    cores = O.max_threads()
-    for _ in range(args.warmup):
-        cpu_prefill_page(q, k, v, sinks, IMAGE_END)
-    times = [cpu_prefill_page(q, k, v, sinks, IMAGE_END) for _ in range(args.steps)]
-    per_page = sum(times) / len(times)
-    value = SEQ / per_page
+    ref = CpuReference()
+    pre, dec = ref.run(args.steps, args.warmup)
+    cpu = ref.describe(pre, dec)
+    med = statistics.median(pre)
+    value = SEQ / med
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_page * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C2 full-page prefill attention, 6,544 tokens (4,096 image + 2,448 text), "
-                               "16 heads x 64, 8 KV heads, BF16 static-shift tiles", "global_batch": 1,
-                   "seq_len": SEQ, "parallelism": "host threads"},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"one full page (16 heads) per step, {per_page:.2f} s each; "
-                                   "C restatement of prefill64/bf16 static-shift tiles (oracle/fo_oracle.c)"},
-        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": bench_config(world),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(value, 1), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if dec:
+        line["decode"] = {"f32": {"us_per_step": cpu["decode_us_per_step"]}, "kv_len": DECODE_L,
+                          "rows": DECODE_ROWS}
     print(json.dumps(line), flush=True)
 
 
@@ -548,16 +629,28 @@ def time_prefill_rows(run, args, inputs):
     return res
 
 
+def compact_decode(d):
+    """One length's decode lines, short enough that the whole JSON line's
+    tail (where the decode headline sits) survives truncated logs."""
+    out = {}
+    for fmt, x in d.items():
+        r = x["roofline"]
+        out[fmt] = {"us_per_step": x["us_per_step"], "gbs": r["achieved"], "frac": r["frac"],
+                    "bytes_per_step": x["bytes_per_step"]}
+        if r.get("traffic"):
+            out[fmt]["traffic"] = r["traffic"]
+    any_line = next(iter(d.values()))
+    out.update(rows=any_line["rows"], caches_rotated=any_line["caches_rotated"], timing=any_line["timing"])
+    return out
+
+
 def run_ours(args, world, rank, local):
     run = Runner(world, rank, local)
     inputs = prefill_inputs(rank)
     line = {"metric": METRIC, "value": None, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "C2 full-page prefill attention, 6,544 tokens (4,096 image + 2,448 text), "
-                                   "16 heads x 64, 8 KV heads, BF16 static-shift softmax, one page per GPU",
-                       "global_batch": world, "seq_len": SEQ, "parallelism": f"pages x{world}",
-                       "l2": "6 distinct input sets rotate (>3x L2)"}}
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": bench_config(world)}
+    extra, dec = {}, None
     if args.mode in ("full", "prefill"):
         value, ms_per_step, roof, clocks = time_prefill(run, args, inputs, 6 if args.mode == "full" else 1)
         line.update(value=round(value, 1), ms_per_step=round(ms_per_step, 4), roofline=roof, clocks=clocks,
@@ -567,28 +660,26 @@ def run_ours(args, world, rank, local):
     if args.mode in ("full", "decode"):
         lengths = (DECODE_L, 6544, 12000) if args.mode == "full" else (DECODE_L,)
         dec = time_decode(run, args, lengths)
-        line["decode"] = dec[DECODE_L]
-        if len(lengths) > 1:
-            line["decode_lengths"] = {str(n): dec[n] for n in lengths[1:]}
     if args.mode in ("full", "c4"):
-        line["decode_c4"] = time_c4(run, args)
+        extra["decode_c4"] = time_c4(run, args)
     if args.mode in ("full", "sharded"):
-        line["sharded_prefill"] = time_sharded(run, args)
+        extra["sharded_prefill"] = time_sharded(run, args)
     if args.mode == "full":
-        line["prefill_rows"] = time_prefill_rows(run, args, inputs)
+        extra["prefill_rows"] = time_prefill_rows(run, args, inputs)
+    cpu_decode_us = None
     if args.mode == "full" and rank == 0 and world == 1:
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-        q, k, v, sinks, _ = inputs
-        cpu_prefill_page(q, k, v, sinks, IMAGE_END)  # warm the pages and threads
-        times = []
-        while sum(times) < CPU_SAMPLE_S or len(times) < 2:
-            times.append(cpu_prefill_page(q, k, v, sinks, IMAGE_END))
-        per_page = sum(times) / len(times)
-        line["cpu_baseline"] = {
-            "value": round(SEQ / per_page, 1), "unit": "tok/s", "cores": O.max_threads(), "kind": "port",
-            "sample": f"{len(times)} full pages (16 heads each), {sum(times):.1f} s in all, mean {per_page:.3f} s; "
-                      "C restatement of the reference's prefill64/bf16 static-shift tiles"}
+        ref = CpuReference()
+        pre, cdec = ref.run(steps=8, warmup=1, min_seconds=CPU_SAMPLE_S)
+        line["cpu_baseline"] = ref.describe(pre, cdec)
+        cpu_decode_us = line["cpu_baseline"].get("decode_us_per_step")
+    line.update(extra)
+    if dec is not None:
+        # The decode headline (BASELINE config 3 at 16,384 positions) goes last.
+        if len(dec) > 1:
+            line["decode_lengths"] = {str(n): compact_decode(dec[n]) for n in dec if n != DECODE_L}
+        line["decode"] = dict(kv_len=DECODE_L, peak_gbs=run.peaks["hbm_gbs"], **compact_decode(dec[DECODE_L]))
+        if cpu_decode_us is not None:
+            line["decode"]["cpu_f32_us_per_step"] = cpu_decode_us
     if rank == 0:
         print(json.dumps(line), flush=True)
     run.close()
