@@ -241,13 +241,32 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                 else
                     ls[i & 1] = __fadd2_rn(ls[i & 1], make_float2(x0, x1));
             };
-            if (full) {
-                // 4 of every 16 exponentials run on the FMA pipes (ex2_poly2),
-                // the rest on the SFU, which would otherwise bound the loop.
+            if constexpr (STATIC) {
+                // The reference's own 2^t (degree-3 polynomial in f = t - n,
+                // times 2^n) for every probability: its 7.5e-5 relative error
+                // decides some BF16 roundings of P, so the SFU's (nearly exact)
+                // exp2 would move them away from the reference's.
+                if (full) {
+#pragma unroll
+                    for (int i = 0; i < 64; i++) {
+                        const float2 e = ex2_poly2_inrange(tt[i]);
+                        pair(i, e.x, e.y);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 64; i++) {
+                        const float2 e = ex2_poly2(tt[i]);
+                        pair(i, 2 * i < nvis ? e.x : 0.0f, 2 * i + 1 < nvis ? e.y : 0.0f);
+                    }
+                }
+            } else if (full) {
+                // 4 of every 16 exponentials run on the FMA pipes (ex2_fit5, as
+                // accurate as the SFU's), the rest on the SFU, which would
+                // otherwise bound the loop.
 #pragma unroll
                 for (int i = 0; i < 64; i++) {
                     if ((i & 3) == 3) {
-                        const float2 e = ex2_poly2(tt[i]);
+                        const float2 e = ex2_fit5(tt[i]);
                         pair(i, e.x, e.y);
                     } else {
                         pair(i, ex2(tt[i].x), ex2(tt[i].y));

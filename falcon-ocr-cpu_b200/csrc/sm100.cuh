@@ -213,13 +213,52 @@ __device__ __forceinline__ float ex2(float x) {
 // relative error at most 7.5e-5), the same FMA order, n taken with the
 // 1.5 * 2^23 rounding constant and added to the exponent field.  Packed FP32
 // (two lanes per instruction); f = t - (j - 1.5 * 2^23) is formed as
-// t + (1.5 * 2^23 - j), the same single rounding of an exact difference.  Valid
-// for t <= 127 (t below -127 is clamped there and gives a value below 2^-126);
-// the prefill's static shift requires |scores| < 80, so t < 116.
+// t + (1.5 * 2^23 - j), the same single rounding of an exact difference.  t is
+// clamped below at -126, so the exponent field never wraps: values of t below
+// -126 give a value of at most about 2^-126 instead of the reference's
+// subnormal or zero (the prefill's static shift requires |scores| < 80, so
+// there t > -116).
 __device__ __forceinline__ float2 ex2_poly2(float2 t) {
     constexpr float R = 12582912.0f;
-    t.x = fmaxf(t.x, -127.0f);
-    t.y = fmaxf(t.y, -127.0f);
+    t.x = fmaxf(t.x, -126.0f);
+    t.y = fmaxf(t.y, -126.0f);
+    const float2 j = __fadd2_rn(t, make_float2(R, R));
+    const float2 f = __fadd2_rn(t, __ffma2_rn(j, make_float2(-1.0f, -1.0f), make_float2(R, R)));
+    float2 p = __ffma2_rn(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261113f, 0.24261113f));
+    p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+    p = __ffma2_rn(p, f, make_float2(0.99992806f, 0.99992806f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(j.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(j.y) << 23)));
+}
+
+// 2^t for two values (t <= 0, as the online softmax's shifted scores), accurate
+// to about 3 ulp (relative error 1.7e-7, comparable to the SFU's ex2.approx) on
+// the FMA and integer pipes: a degree-5 polynomial for 2^f on [-0.5, 0.5] with
+// constant term 1, fitted for this library (iteratively reweighted least
+// squares on Chebyshev nodes to near-minimax relative error), times 2^n as in
+// ex2_poly2.  t is clamped below at -126 (results below about 2^-126 are not
+// exact; they vanish next to the row maximum's 1).
+__device__ __forceinline__ float2 ex2_fit5(float2 t) {
+    constexpr float R = 12582912.0f;
+    t.x = fmaxf(t.x, -126.0f);
+    t.y = fmaxf(t.y, -126.0f);
+    const float2 j = __fadd2_rn(t, make_float2(R, R));
+    const float2 f = __fadd2_rn(t, __ffma2_rn(j, make_float2(-1.0f, -1.0f), make_float2(R, R)));
+    float2 p = __ffma2_rn(make_float2(0.001326472731307149f, 0.001326472731307149f), f,
+                          make_float2(0.009671512991189957f, 0.009671512991189957f));
+    p = __ffma2_rn(p, f, make_float2(0.05550733581185341f, 0.05550733581185341f));
+    p = __ffma2_rn(p, f, make_float2(0.24022242426872253f, 0.24022242426872253f));
+    p = __ffma2_rn(p, f, make_float2(0.6931470036506653f, 0.6931470036506653f));
+    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(j.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(j.y) << 23)));
+}
+
+// ex2_poly2 without the clamp, for exponents known to lie in [-126, 127]
+// (the static shift's precondition |score| < 80 keeps t within 116): the
+// same operations and bits as ex2_poly2 there.
+__device__ __forceinline__ float2 ex2_poly2_inrange(float2 t) {
+    constexpr float R = 12582912.0f;
     const float2 j = __fadd2_rn(t, make_float2(R, R));
     const float2 f = __fadd2_rn(t, __ffma2_rn(j, make_float2(-1.0f, -1.0f), make_float2(R, R)));
     float2 p = __ffma2_rn(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261113f, 0.24261113f));
