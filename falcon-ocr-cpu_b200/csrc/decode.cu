@@ -613,7 +613,13 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
     }
     const int splits = pp->splits;
     const int64_t row_len = pp->last - pp->rows + 1 + r;
-    const int n = (int)((row_len + FO_SPLIT - 1) / FO_SPLIT);
+    // The row's partials: one per FO_SPLIT positions from 0, or (prefix_splits
+    // set) one per `chunk` splits of the prefix and then of its tail.
+    int n = (int)((row_len + FO_SPLIT - 1) / FO_SPLIT);
+    if (pp->prefix_splits) {
+        const int tail_splits = (int)((row_len - pp->prefix_len + FO_SPLIT - 1) / FO_SPLIT);
+        n = (pp->prefix_splits + pp->chunk - 1) / pp->chunk + (tail_splits + pp->chunk - 1) / pp->chunk;
+    }
     float *fk = msm;                                     // [splits] factors exp(m_k - M); -1 skips
     float *lk = msm + splits;                            // [splits] denominators
     float4 *part = reinterpret_cast<float4 *>(lk + splits + 4 - (2 * splits) % 4);  // [SLICES][16]
@@ -828,7 +834,12 @@ static cudaError_t launch_decode(const fo_decode_page &page0, const fo_decode_pa
 
 extern "C" cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t groups, int fast_exp,
                                             cudaStream_t stream) {
+    if (page->prefix_splits) return fo_launch_decode_tc(page, groups, fast_exp, stream);
     return launch_decode(*page, nullptr, 1, format, groups, fast_exp, page->splits, page->rows, stream);
+}
+
+extern "C" cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream) {
+    return launch_merge(*page, nullptr, 1, groups, page->splits, page->rows, stream);
 }
 
 extern "C" cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format,

@@ -37,7 +37,9 @@
 #define FO_STATIC_ROWS 8
 #define FO_STATIC_HEADS 16
 #define FO_STATIC_POSITIONS 16384
-#define FO_STATIC_SPLITS (FO_STATIC_POSITIONS / FO_SPLIT)
+// One split more than the positions need: BF16 records split the prefix and
+// the tail apart (decode_tc.cu).
+#define FO_STATIC_SPLITS (FO_STATIC_POSITIONS / FO_SPLIT + 1)
 #define FO_STATIC_O_FLOATS (FO_STATIC_ROWS * FO_STATIC_HEADS * FO_STATIC_SPLITS * FO_HD)
 #define FO_STATIC_ML_FLOATS (FO_STATIC_ROWS * FO_STATIC_HEADS * FO_STATIC_SPLITS * 2)
 #define FO_STATIC_FLOATS (FO_STATIC_O_FLOATS + FO_STATIC_ML_FLOATS)
@@ -146,6 +148,12 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
     p.last = last;
     p.rows = (int32_t)rows;
     p.splits = (int32_t)((last + FO_SPLIT - 1) / FO_SPLIT);
+    if (format == FO_KV_BF16 && fo_make_tc_maps(&p, n_kv_heads, tail_len)) {
+        // The tensor-core decode's split layout (prefix and tail apart), as
+        // fo_kv_attention_decode_rows uses for BF16 records; the tail map ends
+        // at tail_len, so records past it are never read.
+        fo_tc_layout(&p, n_kv_heads, tail_len);
+    }
     e = fo_launch_decode_one(&p, format, n_kv_heads, fast_exp != 0, (cudaStream_t)stream);
     if (e != cudaSuccess) {
         snprintf(g_msg, sizeof g_msg, "static-scratch decode launch: %s", cudaGetErrorString(e));

@@ -169,6 +169,9 @@ struct fo_kv_cache {
     size_t bytes = 0;                                // record bytes
     alignas(64) CUtensorMap rec_map;                 // prefix records for the decode kernel's TMA loads
     int has_map = 0;
+    // BF16 records: the tensor-core decode's maps (decode_tc.cu), built at seal.
+    alignas(64) CUtensorMap tc_map, tail_map;
+    int has_tc = 0, has_tail_map = 0;
 };
 
 struct fo_i8_cache {
@@ -647,8 +650,10 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
     alloc(&c->tail_codes, tail_bytes);
     alloc((void **)&c->scales, scale_bytes);
     alloc((void **)&c->tail_scales, tscale_bytes);
-    alloc((void **)&c->part_o, (size_t)FO_MAX_ROWS_ABI * H * c->max_splits * 64 * 4);
-    alloc((void **)&c->part_ml, (size_t)FO_MAX_ROWS_ABI * H * c->max_splits * 2 * 4);
+    // Partials for max_splits + 1 splits: the tensor-core decode splits the
+    // prefix and the tail apart (at most one split more).
+    alloc((void **)&c->part_o, (size_t)FO_MAX_ROWS_ABI * H * (c->max_splits + 1) * 64 * 4);
+    alloc((void **)&c->part_ml, (size_t)FO_MAX_ROWS_ABI * H * (c->max_splits + 1) * 2 * 4);
     alloc((void **)&c->q_stage, (size_t)FO_MAX_ROWS_ABI * H * 64 * 4);
     alloc((void **)&c->out_stage, (size_t)FO_MAX_ROWS_ABI * H * 64 * 4);
     alloc((void **)&c->sinks_stage, (size_t)H * 4);
@@ -660,6 +665,20 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
     c->bytes = code_bytes + tail_bytes + (coded(format) ? scale_bytes + tscale_bytes : 0);
     // Without a tensor map the decode kernel copies record by record.
     c->has_map = fo_make_record_map(&c->rec_map, c->codes, format, prefix_len, c->prefix_stride, G) ? 1 : 0;
+    if (format == FO_KV_BF16) {
+        fo_decode_page tp{};
+        tp.codes = c->codes;
+        tp.tail_codes = c->tail_codes;
+        tp.prefix_len = prefix_len;
+        tp.prefix_stride = c->prefix_stride;
+        tp.tail_stride = c->tail_stride;
+        if (fo_make_tc_maps(&tp, G, c->tail_capacity)) {
+            c->tc_map = tp.tc_map;
+            c->tail_map = tp.tail_map;
+            c->has_tail_map = tp.has_tail_map;
+            c->has_tc = 1;
+        }
+    }
     if (e == cudaSuccess) e = cudaMemsetAsync(c->tail_codes, 0, tail_bytes, ctx->stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(c->tail_scales, 0, tscale_bytes, ctx->stream);
     const float *dk = k, *dv = v;
@@ -735,6 +754,22 @@ int fo_kv_append(fo_kv_cache *c, const float *k, const float *v, int64_t rows, i
 int fo_kv_truncate_tail(fo_kv_cache *c, int64_t tail_len) {
     if (!c) return fail(FO_ERR_INVALID, "null cache");
     if (tail_len < 0 || tail_len > c->tail_len) return fail(FO_ERR_INVALID, "cannot grow the tail by truncation");
+    if (tail_len < c->tail_len) {
+        // The dropped records go back to zero, as seal leaves the tail: the
+        // tensor-core decode reads whole 128-position tiles of tail records,
+        // and past the cache's end they must add nothing (zero keys, values).
+        DeviceGuard guard(c->ctx->device);
+        const size_t es = elem_size(c->format);
+        const size_t pitch = (size_t)c->tail_stride * FO_TAIL_ELEMS * es;
+        FO_CUDA(cudaMemset2DAsync(static_cast<char *>(c->tail_codes) + (size_t)tail_len * FO_TAIL_ELEMS * es, pitch, 0,
+                                  (size_t)(c->tail_len - tail_len) * FO_TAIL_ELEMS * es, (size_t)c->groups,
+                                  c->ctx->stream),
+                "cudaMemset2DAsync(tail records)");
+        if (coded(c->format))
+            FO_CUDA(cudaMemset2DAsync(c->tail_scales + (size_t)tail_len * 4, (size_t)c->tail_stride * 4 * 2, 0,
+                                      (size_t)(c->tail_len - tail_len) * 4 * 2, (size_t)c->groups, c->ctx->stream),
+                    "cudaMemset2DAsync(tail scales)");
+    }
     c->tail_len = tail_len;
     return FO_OK;
 }
@@ -753,6 +788,16 @@ int fo_kv_records(const fo_kv_cache *c, void **codes, void **scales, void **tail
     if (prefix_stride) *prefix_stride = c->prefix_stride;
     if (tail_stride) *tail_stride = c->tail_stride;
     return FO_OK;
+}
+
+// A single-page decode of BF16 records runs on the tensor cores
+// (decode_tc.cu) with its own split layout; others, and batches, on decode.cu.
+static void use_tc_layout(const fo_kv_cache *c, fo_decode_page *p) {
+    if (!c->has_tc || (c->tail_len > 0 && !c->has_tail_map)) return;
+    p->tc_map = c->tc_map;
+    p->tail_map = c->tail_map;
+    p->has_tail_map = c->has_tail_map;
+    fo_tc_layout(p, c->groups, c->tail_len);
 }
 
 static fo_decode_page make_page(const fo_kv_cache *c, const float *q, const float *sinks, float *out, int rows) {
@@ -798,6 +843,7 @@ int fo_kv_attention_decode_rows(fo_kv_cache *c, const float *q, int64_t rows, co
         dout = c->out_stage;
     }
     fo_decode_page p = make_page(c, dq, ds, dout, (int)rows);
+    use_tc_layout(c, &p);
     cudaError_t e = fo_launch_decode_one(&p, c->format, c->groups, c->fast_exp, st);
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     return finish_host(c->ctx, output, dout, n, mem);
@@ -825,6 +871,7 @@ int fo_kv_attention_decode(fo_kv_cache *c, const float *q, int64_t total_len, co
         dout = c->out_stage;
     }
     fo_decode_page p = make_page(c, dq, ds, dout, 1);
+    use_tc_layout(c, &p);
     cudaError_t e = fo_launch_decode_one(&p, c->format, c->groups, c->fast_exp, st);
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     return finish_host(c->ctx, output, dout, n, mem);

@@ -35,7 +35,9 @@ cudaError_t fo_launch_append(const float *k, const float *v, int64_t rows, int64
 
 // One decode page: a cache's records and the query rows against it.
 struct alignas(64) fo_decode_page {
-    CUtensorMap rec_map;  // prefix records as padded slots (fo_make_record_map); valid when has_map
+    CUtensorMap rec_map;   // prefix records as padded slots (fo_make_record_map); valid when has_map
+    CUtensorMap tc_map;    // BF16 prefix records in 64-element swizzled boxes (fo_make_tc_maps)
+    CUtensorMap tail_map;  // BF16 tail records likewise; valid when has_tail_map
     const void *codes;
     const uint16_t *scales;
     const void *tail_codes;
@@ -47,9 +49,26 @@ struct alignas(64) fo_decode_page {
     float *part_ml;      // [rows][H][splits][2] (max, denominator)
     unsigned *err;       // error word for bounded waits that gave up (may be null)
     int64_t prefix_len, prefix_stride, tail_stride, last;  // last = prefix_len + tail_len
-    int32_t rows, splits;                                   // splits = ceil(last / FO_SPLIT)
-    int32_t has_map;
+    int32_t rows, splits;                                   // splits = ceil(last / FO_SPLIT), or see prefix_splits
+    int32_t has_map, has_tail_map;
+    // 0: splits are FO_SPLIT positions from position 0 (decode.cu).  Otherwise
+    // the prefix splits into this many FO_SPLIT-position splits and the tail
+    // into its own, starting at prefix_len (decode_tc.cu): splits =
+    // prefix_splits + ceil(tail_len / FO_SPLIT).
+    int32_t prefix_splits;
+    // With prefix_splits set: splits per partial ("unit"), and `splits` counts
+    // units per row and head (fo_tc_layout).
+    int32_t chunk;
 };
+
+// The tensor-core decode's maps of BF16 records (decode_tc.cu) for page p
+// (codes, tail_codes, prefix_len and strides set); false if the encoder is
+// unavailable or refuses (the caller then uses the CUDA-core decode).
+bool fo_make_tc_maps(fo_decode_page *p, int64_t groups, int64_t tail_rows);
+// Sets the tensor-core decode's split layout of page p (prefix_len set) with
+// tail_len tail positions: prefix_splits, chunk and splits (units per row).
+void fo_tc_layout(fo_decode_page *p, int64_t groups, int64_t tail_len);
+
 
 // The tensor map the decode kernel loads prefix records through: records
 // [groups][stride][160] of `format`, rows past prefix_len out of bounds, a
@@ -66,6 +85,12 @@ bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t
 // One page (descriptor read on the host, passed by value).
 cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t groups, int fast_exp,
                                  cudaStream_t stream);
+// One page of BF16 records on the tensor cores (decode_tc.cu); the page has
+// prefix_splits set and its tc maps built.
+cudaError_t fo_launch_decode_tc(const fo_decode_page *page, int64_t groups, int fast_exp, cudaStream_t stream);
+// The split merge of one page (a programmatic dependent of the decode just
+// launched on `stream`).
+cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream);
 // n_pages pages whose descriptors are a device array.
 cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format, int64_t groups,
                                    int fast_exp, int64_t max_splits, int max_rows, cudaStream_t stream);

@@ -55,11 +55,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, volatile int *abort_flag, unsigned *err,
                                           uint64_t limit_ns = FO_WAIT_NS) {
     if (mbar_try_wait(bar, phase)) return true;
-    const uint64_t t0 = globaltimer();
+    // The clock is read only once a wait has lasted 64 polls, so short waits
+    // never pay for it; the bound then runs from that first reading.
+    uint64_t t0 = 0;
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, phase)) return true;
         if ((it & 63) == 0) {
             if (*abort_flag) return false;
+            if (t0 == 0) t0 = globaltimer();
             if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
                 if (err) atomicOr(err, FO_DEVERR_WAIT_TIMEOUT);
@@ -196,6 +199,25 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr, uint32_t lbo
         "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),   \
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                                                              \
         : "memory")
+
+// One 32-bit column of this warp's 32 TMEM lanes.
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return r;
+}
+
+// Shared-memory matrix descriptor without swizzle (layout 0), version 1:
+// 8-row x 16-byte core matrices, lbo_bytes apart along K, sbo_bytes apart
+// along M/N.
+__device__ __forceinline__ uint64_t sdesc_none(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // version
+    return d;
+}
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
