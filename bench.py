@@ -569,7 +569,10 @@ def time_decode(run, args, lengths=(DECODE_L,)):
                     "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"],
                                  "unit": "GB/s", "frac": round(gbs / run.peaks["hbm_gbs"], 4),
                                  "traffic": run.traffic.get(f"decode_{fmt}") if length == DECODE_L else None},
-                    "caches_rotated": n_caches, "gpu_launches_per_step": 1, "timing": "CUDA graph of the steps"}
+                    "caches_rotated": n_caches,
+                    # the decode kernel (tensor-core for BF16 records, CUDA-core
+                    # for F32) and its split-merge kernel
+                    "gpu_launches_per_step": 2, "timing": "CUDA graph of the steps"}
         del graph
         for c in caches:
             c.close()

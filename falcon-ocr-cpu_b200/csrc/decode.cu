@@ -838,13 +838,13 @@ extern "C" cudaError_t fo_launch_decode_one(const fo_decode_page *page, int form
     return launch_decode(*page, nullptr, 1, format, groups, fast_exp, page->splits, page->rows, stream);
 }
 
-extern "C" cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream) {
-    return launch_merge(*page, nullptr, 1, groups, page->splits, page->rows, stream);
-}
-
 extern "C" cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format,
                                               int64_t groups, int fast_exp, int64_t max_splits, int max_rows,
                                               cudaStream_t stream) {
     fo_decode_page none{};
     return launch_decode(none, dev_pages, n_pages, format, groups, fast_exp, max_splits, max_rows, stream);
+}
+
+extern "C" cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream) {
+    return launch_merge(*page, nullptr, 1, groups, page->splits, page->rows, stream);
 }

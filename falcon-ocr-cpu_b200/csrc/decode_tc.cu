@@ -14,33 +14,36 @@
 //   unit      `chunk` consecutive splits of one group (chunk chosen from the
 //             prefix length so that the units about fill the GPU); a CTA
 //             walks whole units and leaves one partial per unit and row;
-//   TMA warp  (warp 10) boxes of 128 records x 64 BF16 (128-byte swizzle) through a
+//   TMA warp  (warp 8) boxes of 128 records x 64 BF16 (128-byte swizzle) through a
 //             3-stage ring: [T|S0], [S1|V0..31] and [V] of prefix records,
 //             [K] and [V] of tail records;
-//   MMA warp  (warp 11) S = keys x Q' (M128 K64, keys in TMEM lanes: the temporal
-//             half for both heads at N64, each spatial half at N32); then
-//             O = P' x V (M64 N64 K128) and the row sums l = P' x 1 (N8),
-//             S, P', O and l double-buffered;
-//   8 warps   (warps 2-9) one thread per (head, key): logits, the row maxima
-//             over the split (redux, then the head's four warps through a
-//             named barrier and shared memory), p = exp(s - max), P' to shared
-//             memory;
-//   2 warps   (warps 0, 1: TMEM lane quadrants 0 and 1) read O's hi and lo
-//             rows and fold each split into its unit's running partial,
-//             written at the unit's end, off the key warps' path.
+//   QK warp   (warp 9) S = keys x Q' (M128 K64, keys in TMEM lanes: the temporal
+//             half for both heads at N64, each spatial half at N32), S and P'
+//             double-buffered;
+//   PV warp   (warp 10) O += P' x V (M64 N64 K128), summed in TMEM over the
+//             whole unit;
+//   8 warps   (warps 0-7) one thread per (head, key): logits, p = exp(s -
+//             m_ref) against the row's reference maximum, P' to shared memory,
+//             and the thread's share of the row sums l.  m_ref is the unit's
+//             first maximum and moves only when a split's maximum passes it by
+//             more than TAU (a vote of the head's four warps); the head's two
+//             warps whose TMEM lane quadrants hold its O rows then rescale O in
+//             place, and write the unit's partial at its end.  The split merge
+//             (decode.cu) follows as a programmatic dependent launch.
 //
 // Exactness: Q' holds each FP32 query as three BF16 terms (hi + mid + lo ==
 // q exactly), so every product with a BF16 key is exact and S is the FP32
 // dot product up to accumulation order.  P' holds each probability as two
 // BF16 terms (hi + lo == p to 2^-18) in two groups of M rows, which the
-// epilogue adds, for O and l alike.  The output agrees
+// unit's end adds; the row sums add the FP32 p.  The output agrees
 // with the reference's FP32 decode over the same records within
 // 1e-5 * (1 + |b|).
 //
 // Verify rows: every row's logits, maxima, O and l columns come from its own
 // query and keys only, with the same instructions whatever the number of
-// rows, and a split that holds none of a row's keys leaves that row's unit
-// partial untouched.  Keys a row does not see get p = 0; with finite values
+// rows (a row's reference maximum moves on its own keys only; a rescale
+// multiplies the other rows by exactly 1), and a split that holds none of a
+// row's keys leaves that row's unit partial untouched.  Keys a row does not see get p = 0; with finite values
 // that adds an exact zero to its O column.  A non-finite value in one of the
 // last rows - 1 positions (a NaN draft) is taken out of the MMA and added by
 // the CUDA cores to exactly the rows that see it.  Positions past the cache's
@@ -60,41 +63,44 @@ namespace tc {
 using namespace sm100;
 
 constexpr int KEY_WARPS = 8;
-constexpr int THREADS = 384;  // warps 0-1 epilogue, 2-9 (head, key), 10 TMA, 11 MMA
-constexpr int W_TMA = 10, W_MMA = 11;
-constexpr int RING = 8;       // per-split statistics and window records, by split index mod 8
+constexpr int THREADS = 352;  // warps 0-7 (head, key), 8 TMA, 9 QK issue, 10 PV issue
+constexpr int W_TMA = 8, W_QK = 9, W_PV = 10;
 constexpr int STAGES = 3;
+// A row's reference maximum moves only when a split's maximum passes it by
+// more than TAU, so probabilities stay below e^8 and O is rescaled in TMEM
+// only then (never, for ordinary data, after a unit's first split).
+constexpr float TAU = 8.0f;
 constexpr uint32_t BOX = 128 * 128;   // 128 records x 128 bytes
 constexpr uint32_t STAGE = 3 * BOX;   // three boxes per split
 constexpr uint32_t QTILE = 32 * 128;  // Q' of one head: 32 rows x 64 BF16
 constexpr uint32_t OFF_Q = STAGES * STAGE;
 constexpr uint32_t OFF_P = OFF_Q + 2 * 2 * QTILE;  // two Q' buffers x two heads
-// P' double buffer: [key][64 M rows] BF16, M row = term * 16 + head * 8 + row
-// (term 0 = hi, 1 = lo; rows 32..63 zero).
-constexpr uint32_t OFF_ONES = OFF_P + 2 * BOX;  // 256 bytes of BF16 ones: the row-sum MMA's operand
-constexpr uint32_t OFF_RED = OFF_ONES + 256;
-// row maxima: [RING][2 heads][4 warps][8 rows] floats
-constexpr uint32_t RED_FLOATS = RING * 2 * 4 * 8;
+// P' double buffer: [key][64 M rows] BF16, M row = 32 * head + 16 * term + row
+// (term 0 = hi, 1 = lo), i.e. 16-byte chunk 4 * head + 2 * term of the key's
+// row; the odd chunks stay zero.  An M64 MMA puts M rows 16q .. 16q + 15 in
+// TMEM lanes 32q .. 32q + 15, so head h's hi rows of O lie in lane quadrant
+// 2h and its lo rows in quadrant 2h + 1: the head's own key warps of those
+// quadrants can rescale and read them.
+constexpr uint32_t OFF_RED = OFF_P + 2 * BOX;
+// per-warp row maxima of a split, [split parity][2 heads][4 warps][8 rows],
+// then per-warp row sums of a unit, [2 heads][4 warps][8 rows]
+constexpr uint32_t RED_FLOATS = 2 * 2 * 4 * 8 + 2 * 4 * 8;
 constexpr uint32_t OFF_WIN = OFF_RED + RED_FLOATS * 4;
-// draft-window fallback per [RING][2 heads]: { count, keys[8], p[8 keys][8
-// rows] } in 32-bit words.  The key warps run at most RING - 1 splits ahead
-// of the epilogue (P' of split i waits for PV of split i - 2, which waits for
-// the epilogue of split i - 4), so a slot is free when they come back to it.
-constexpr uint32_t WIN_WORDS = 1 + 8 + 8 * 8;
-// [2 heads][8 rows][68] floats: the epilogue lanes' running unit partials
-// (64 dimensions, padded against bank conflicts); and the lo rows of O handed
-// from one epilogue warp to the other, [2 parities][2 heads][8 rows][68].
+// draft-window list of each head's current unit, 32-bit words: { count,
+// tail row[8], p[8 keys][8 rows], reference max[8 keys][8 rows] }
+constexpr uint32_t WIN_WORDS = 1 + 8 + 64 + 64;
 constexpr uint32_t ACC_STRIDE = 68;
-constexpr uint32_t OFF_ACC = (OFF_WIN + RING * 2 * WIN_WORDS * 4 + 15) / 16 * 16;
-constexpr uint32_t OFF_LO = OFF_ACC + 2 * 8 * ACC_STRIDE * 4;
-constexpr uint32_t OFF_BAR = OFF_LO + 2 * 2 * 8 * ACC_STRIDE * 4;
-// full[3] empty[3] s_full[2] s_empty[2] q_full[2] p_full pv_done[2]
-// o_empty[2] lo_ready[2] mma_done
-constexpr int NBAR = 2 * STAGES + 2 + 2 + 2 + 1 + 2 + 2 + 2 + 1;
+// O's lo rows handed from a head's lo warp to its hi warp at a unit's end:
+// [2 heads][8 rows][68] floats.
+constexpr uint32_t OFF_LO = (OFF_WIN + 2 * WIN_WORDS * 4 + 15) / 16 * 16;
+constexpr uint32_t OFF_BAR = OFF_LO + 2 * 8 * ACC_STRIDE * 4;
+// full[3] empty[3] s_full[2] s_empty[2] q_full[2] p_full pv_done[2] qk_drain pv_drain
+constexpr int NBAR = 2 * STAGES + 2 + 2 + 2 + 1 + 2 + 2;
+// after the barriers: TMEM address and abort flag
 constexpr uint32_t SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-// S, O and the row sums l double-buffered: S [0, 128), O [128, 256), l [256, 272).
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TM_O = 128, TM_L = 256;
+// S double-buffered [0, 128); O [128, 192), summed over a unit.
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TM_O = 128;
 static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 
 // Instruction descriptor, kind::f16, BF16 inputs, FP32 accumulator.
@@ -105,7 +111,7 @@ __host__ __device__ constexpr uint32_t idesc(uint32_t m, uint32_t n, uint32_t a_
 struct Args {
     int64_t H, prefix_len, last, len0;  // len0 = last - rows + 1: keys every row sees
     int32_t prefix_splits, tail_splits, chunk, prefix_units, units;  // units per group and row
-    int64_t n_units;                                                  // groups x units
+    uint32_t n_units;                                                 // groups x units (< 2^24)
 };
 
 __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t phase) {
@@ -114,12 +120,22 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t phase) {
         if (globaltimer() - t0 > FO_WAIT_NS) break;
 }
 
-// The exchange among a head's four key warps (named barrier 1 + head, 128
-// threads).  Every key warp passes it once per split, also after a bounded
-// wait gave up (it then skips the split's work), so no warp waits here for
-// one that left.
-__device__ __forceinline__ void sync_head(int h) {
-    asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory");
+// Named barriers of head h's four key warps: 1 + h, the per-split vote on
+// whether any row's reference maximum moves; 3 + h, the meeting at a unit's
+// end; 5 + h (64 threads), its hi and lo warps there.  Every warp passes each of
+// them the same number of times, also after a bounded wait gave up (it then
+// skips the work), so no warp waits for one that left.
+__device__ __forceinline__ bool vote_head(int h, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, %2, 128, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(1 + h)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void bar_named(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 __device__ __forceinline__ float warp_max_redux(float v) {
@@ -141,10 +157,11 @@ __device__ __forceinline__ float key_exp(float x) {
 }
 
 // Walks a CTA's units and their splits in order: group, split index, and
-// whether the split closes its unit.
+// whether the split opens or closes its unit.
 struct Walk {
-    int64_t U, U_end, g;  // unit, end, the unit's group
-    int u, s, s_end;      // the unit's index within its group, split, end
+    uint32_t U, U_end;
+    int g;                     // unit, end, the unit's group
+    int u, s, s_first, s_end;  // the unit's index within its group, split, first and end split
     __device__ __forceinline__ void unit_bounds(const Args &a) {
         if (u < a.prefix_units) {
             s = u * a.chunk;
@@ -153,18 +170,20 @@ struct Walk {
             s = a.prefix_splits + (u - a.prefix_units) * a.chunk;
             s_end = min(s + a.chunk, a.prefix_splits + a.tail_splits);
         }
+        s_first = s;
     }
-    __device__ __forceinline__ void start(const Args &a, int64_t u0, int64_t u1) {
+    __device__ __forceinline__ void start(const Args &a, uint32_t u0, uint32_t u1) {
         U = u0;
         U_end = u1;
-        g = U / a.units;  // the walk's one division
-        u = (int)(U - g * a.units);
-        s = s_end = 0;
+        g = (int)(U / (uint32_t)a.units);  // the walk's one division
+        u = (int)U - g * a.units;
+        s = s_first = s_end = 0;
         if (U < U_end) unit_bounds(a);
     }
     __device__ __forceinline__ bool valid() const { return U < U_end; }
-    __device__ __forceinline__ int64_t group(const Args &) const { return g; }
+    __device__ __forceinline__ int group(const Args &) const { return g; }
     __device__ __forceinline__ int unit(const Args &) const { return u; }
+    __device__ __forceinline__ bool first_of_unit() const { return s == s_first; }
     __device__ __forceinline__ bool last_of_unit() const { return s + 1 == s_end; }
     __device__ __forceinline__ void next(const Args &a) {
         if (++s >= s_end && ++U < U_end) {
@@ -208,15 +227,17 @@ __device__ __forceinline__ void issue_tma(const fo_decode_page &pg, const Args &
     const int g = (int)wk.group(a);
     const Split x = split_of(a, wk.s);
     uint8_t *dst = smem + st * STAGE;
+    // Records are read once per call: first out of L2.
+    const uint64_t pol = l2_evict_first();
     if (!x.tail) {
         mbar_expect_tx(full + st, 3 * BOX);
-        tma_load_3d(dst, &pg.tc_map, full + st, 0, x.row0, g);
-        tma_load_3d(dst + BOX, &pg.tc_map, full + st, 64, x.row0, g);
-        tma_load_3d(dst + 2 * BOX, &pg.tc_map, full + st, 96, x.row0, g);
+        tma_load_3d_hint(dst, &pg.tc_map, full + st, 0, x.row0, g, pol);
+        tma_load_3d_hint(dst + BOX, &pg.tc_map, full + st, 64, x.row0, g, pol);
+        tma_load_3d_hint(dst + 2 * BOX, &pg.tc_map, full + st, 96, x.row0, g, pol);
     } else {
         mbar_expect_tx(full + st, 2 * BOX);
-        tma_load_3d(dst, &pg.tail_map, full + st, 0, x.row0, g);
-        tma_load_3d(dst + 2 * BOX, &pg.tail_map, full + st, 64, x.row0, g);
+        tma_load_3d_hint(dst, &pg.tail_map, full + st, 0, x.row0, g, pol);
+        tma_load_3d_hint(dst + 2 * BOX, &pg.tail_map, full + st, 64, x.row0, g, pol);
     }
 }
 
@@ -228,18 +249,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *full = bars, *empty = bars + STAGES;
     uint64_t *s_full = bars + 2 * STAGES, *s_empty = s_full + 2, *q_full = s_empty + 2;
-    uint64_t *p_full = q_full + 2, *pv_done = p_full + 1, *o_empty = pv_done + 2, *lo_ready = o_empty + 2;
-    uint64_t *mma_done = lo_ready + 2;
+    uint64_t *p_full = q_full + 2, *pv_done = p_full + 1, *qk_drain = pv_done + 2, *pv_drain = qk_drain + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t u0 = (int64_t)blockIdx.x * a.n_units / gridDim.x;
-    const int64_t u1 = (int64_t)(blockIdx.x + 1) * a.n_units / gridDim.x;
+    const uint32_t u0 = blockIdx.x * a.n_units / gridDim.x;
+    const uint32_t u1 = (blockIdx.x + 1) * a.n_units / gridDim.x;
 
-    // The TMA thread sets the barriers up and starts the first loads before
-    // the CTA-wide barrier (the stage buffers are not touched by the rest of
-    // the setup).
+    // The TMA thread starts the first loads before anything else and sets the
+    // other barriers up before the CTA-wide barrier (the stage buffers are
+    // not touched by the rest of the setup).
     Walk twk;
     int t_issued = 0;
     if (threadIdx.x == W_TMA * 32) {
@@ -247,28 +267,28 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(full + s, 1);
             mbar_init(empty + s, 1);
         }
+        mbar_fence_init();
+        tma_prefetch(&pg.tc_map);
+        twk.start(a, u0, u1);
+        for (; twk.valid() && t_issued < STAGES; t_issued++, twk.next(a)) issue_tma(pg, a, smem, full, twk, t_issued);
         for (int b = 0; b < 2; b++) {
             mbar_init(s_full + b, 1);
             mbar_init(s_empty + b, KEY_WARPS);
             mbar_init(q_full + b, KEY_WARPS);
             mbar_init(pv_done + b, 1);
-            mbar_init(o_empty + b, 2);  // both epilogue warps
-            mbar_init(lo_ready + b, 1);
         }
         mbar_init(p_full, KEY_WARPS);
-        mbar_init(mma_done, 1);
+        mbar_init(qk_drain, 1);
+        mbar_init(pv_drain, 1);
         *abort_flag = 0;
         mbar_fence_init();
-        tma_prefetch(&pg.tc_map);
         if (pg.has_tail_map) tma_prefetch(&pg.tail_map);
-        twk.start(a, u0, u1);
-        for (; twk.valid() && t_issued < STAGES; t_issued++, twk.next(a)) issue_tma(pg, a, smem, full, twk, t_issued);
     }
-    if (warp >= 2 && warp < 2 + KEY_WARPS) {
+    if (warp < KEY_WARPS) {
         // Zero what the loop never writes: Q' rows of absent verify rows and
-        // its padding rows (R..7 of each term, 24..31), and P' rows 32..63
-        // (logical chunks 4..7 of every key's row, both buffers).
-        const int t = threadIdx.x - 64;
+        // its padding rows (R..7 of each term, 24..31), and P' chunks 1, 3, 5
+        // and 7 of every key's row (both buffers); empty window lists.
+        const int t = threadIdx.x;
         for (int idx = t; idx < 2 * 2 * 32 * 8; idx += 32 * KEY_WARPS) {
             const int chunk = idx & 7, row = (idx >> 3) & 31;
             if (row >= 24 || (row & 7) >= R)
@@ -276,16 +296,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                     make_uint4(0, 0, 0, 0);
         }
         for (int idx = t; idx < 2 * 128 * 4; idx += 32 * KEY_WARPS) {
-            const int tile = idx >> 9, key = (idx >> 2) & 127, chunk = 4 + (idx & 3);
+            const int tile = idx >> 9, key = (idx >> 2) & 127, chunk = 2 * (idx & 3) + 1;
             *reinterpret_cast<uint4 *>(smem + OFF_P + tile * BOX + key * 128 + ((chunk ^ (key & 7)) << 4)) =
                 make_uint4(0, 0, 0, 0);
         }
-        if (t < 16)
-            *reinterpret_cast<uint4 *>(smem + OFF_ONES + 16 * t) =
-                make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+        if (t < 2) reinterpret_cast<int *>(smem + OFF_WIN)[t * WIN_WORDS] = 0;
         fence_proxy_async_smem();
     }
-    if (warp == W_MMA) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == W_PV) tmem_alloc(tmem_slot, TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -307,41 +325,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = max(0, t_issued - STAGES); i < t_issued; i++)
                     drain_wait(full + i % STAGES, (i / STAGES) & 1);
         }
-    } else if (warp == W_MMA) {
-        // ---------------------------------------------------------- MMA
-        const uint32_t iT = idesc(128, 64, 0, 0), iS = idesc(128, 32, 0, 0), iPV = idesc(64, 64, 1, 1);
-        const uint32_t iL = idesc(64, 8, 1, 0);
-        const uint32_t sQ = smem_u32(smem + OFF_Q), sP = smem_u32(smem + OFF_P);
-        // The ones operand (N8 x K16, no swizzle): every K step reads the same
-        // 256 bytes of BF16 ones.
-        const uint64_t dOnes = sdesc_none(smem_u32(smem + OFF_ONES), 128, 256);
+    } else if (warp == W_QK) {
+        // ------------------------------------------------------- QK issue
+        // S(i) = keys x Q' once the split's records, Q' (on a group change)
+        // and S buffer i & 1 are in.
+        const uint32_t iT = idesc(128, 64, 0, 0), iS = idesc(128, 32, 0, 0);
+        const uint32_t sQ = smem_u32(smem + OFF_Q);
         bool ok = true;
         int q_uses[2] = {0, 0};
-        int qb = 1;
-        int64_t prev_g = -1;
-        auto issue_pv = [&](int j) {
-            // O = P' V and l = P' 1 over the split's 128 keys (8 K16 steps) into
-            // buffer j & 1.
-            const int st = j % STAGES;
-            const uint64_t dV = sdesc_sw128(smem_u32(smem + st * STAGE + 2 * BOX), BOX, 1024);
-            const uint64_t dP = sdesc_sw128(sP + (j & 1) * BOX, BOX, 1024);
-            if (elect_one()) {
-#pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    mma_bf16(tmem + TM_O + (j & 1) * 64, dP + kk * (2048 >> 4), dV + kk * (2048 >> 4), iPV, kk != 0);
-                    mma_bf16(tmem + TM_L + (j & 1) * 8, dP + kk * (2048 >> 4), dOnes, iL, kk != 0);
-                }
-                mma_commit(pv_done + (j & 1));
-                mma_commit(empty + st);
-            }
-            __syncwarp();
-        };
+        int qb = 1, prev_g = -1;
         Walk wk;
         wk.start(a, u0, u1);
-        int i = 0;
-        for (; wk.valid() && ok; i++, wk.next(a)) {
-            const int st = i % STAGES, u = i / STAGES, sb = i & 1;
-            const int64_t g = wk.group(a);
+        for (int i = 0; wk.valid() && ok; i++, wk.next(a)) {
+            const int st = i % STAGES, sb = i & 1;
+            const int g = wk.group(a);
             if (g != prev_g) {
                 qb ^= 1;
                 ok = __all_sync(0xffffffffu, mbar_wait(q_full + qb, q_uses[qb] & 1, abort_flag, pg.err));
@@ -349,7 +346,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 prev_g = g;
                 if (!ok) break;
             }
-            ok = __all_sync(0xffffffffu, mbar_wait(full + st, u & 1, abort_flag, pg.err));
+            ok = __all_sync(0xffffffffu, mbar_wait(full + st, (i / STAGES) & 1, abort_flag, pg.err));
             if (ok && i >= 2)
                 ok = __all_sync(0xffffffffu, mbar_wait(s_empty + sb, ((i - 2) >> 1) & 1, abort_flag, pg.err));
             if (!ok) break;
@@ -375,54 +372,77 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mma_commit(s_full + sb);
             }
             __syncwarp();
-            if (i >= 1) {
-                // PV of the previous split once its probabilities are in and
-                // the epilogue has read the O two splits back (same buffer).
-                ok = __all_sync(0xffffffffu, mbar_wait(p_full, (i - 1) & 1, abort_flag, pg.err));
-                if (ok && i >= 3)
-                    ok = __all_sync(0xffffffffu,
-                                    mbar_wait(o_empty + ((i - 1) & 1), ((i - 3) >> 1) & 1, abort_flag, pg.err));
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(i - 1);
-            }
         }
-        if (ok && i > 0) {
-            const int j = i - 1;
+        if (elect_one()) mma_commit(qk_drain);
+        __syncwarp();
+        if (lane == 0) drain_wait(qk_drain, 0);
+        __syncwarp();
+    } else if (warp == W_PV) {
+        // ------------------------------------------------------- PV issue
+        // O += P'(j) V(j) over the split's 128 keys (8 K16 steps) once P'(j)
+        // is in (and O rescaled where the split moved a reference maximum);
+        // a unit's first split starts O afresh.  PV(j)'s completion frees P'
+        // buffer j & 1 and the split's stage (its QK finished before its S
+        // was read, which P'(j) waited for).
+        const uint32_t iPV = idesc(64, 64, 1, 1);
+        const uint32_t sP = smem_u32(smem + OFF_P);
+        bool ok = true;
+        Walk wk;
+        wk.start(a, u0, u1);
+        for (int j = 0; wk.valid() && ok; j++, wk.next(a)) {
+            const int st = j % STAGES;
             ok = __all_sync(0xffffffffu, mbar_wait(p_full, j & 1, abort_flag, pg.err));
-            if (ok && j >= 2)
-                ok = __all_sync(0xffffffffu, mbar_wait(o_empty + (j & 1), ((j - 2) >> 1) & 1, abort_flag, pg.err));
-            if (ok) {
-                tc_fence_after();
-                issue_pv(j);
+            if (!ok) break;
+            tc_fence_after();
+            const bool first = wk.first_of_unit();
+            const uint64_t dV = sdesc_sw128(smem_u32(smem + st * STAGE + 2 * BOX), BOX, 1024);
+            const uint64_t dP = sdesc_sw128(sP + (j & 1) * BOX, BOX, 1024);
+            if (elect_one()) {
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++)
+                    mma_bf16(tmem + TM_O, dP + kk * (2048 >> 4), dV + kk * (2048 >> 4), iPV, kk != 0 || !first);
+                mma_commit(pv_done + (j & 1));
+                mma_commit(empty + st);
             }
+            __syncwarp();
         }
-        if (elect_one()) mma_commit(mma_done);
+        if (elect_one()) mma_commit(pv_drain);
         __syncwarp();
-        if (lane == 0) drain_wait(mma_done, 0);
+        if (lane == 0) drain_wait(pv_drain, 0);
         __syncwarp();
-    } else if (warp >= 2) {
+    } else {
         // ---------------------------------------------- (head, key) warps
-        const int hw = warp - 2;         // 0..7
-        const int h = hw >> 2;           // this warp's head of the group
-        const int w4 = hw & 3;           // warp index within the head
-        const int qd = warp & 3;         // TMEM lane quadrant of this warp
+        const int h = warp >> 2;         // this warp's head of the group
+        const int qd = warp & 3;         // TMEM lane quadrant of this warp (and its index in the head)
         const int key = qd * 32 + lane;  // the key this thread owns in a split
+        const bool hi_warp = qd == 2 * h, lo_warp = qd == 2 * h + 1;  // holders of the head's O rows
+        const uint32_t tq = tmem + ((uint32_t)(qd * 32) << 16);
         const int64_t H = a.H;
         const float NEG_INF = -INFINITY;
         float *red = reinterpret_cast<float *>(smem + OFF_RED);
+        float *lsum = red + 2 * 2 * 4 * 8 + h * 32;  // the head's per-warp row sums [warp][row]
+        int *win = reinterpret_cast<int *>(smem + OFF_WIN) + h * WIN_WORDS;
         bool ok = true;
-        int qb = 1;
-        int64_t prev_g = -1;
+        int qb = 1, prev_g = -1;
+        // The unit's reference maxima per row (the same in all the head's
+        // threads): every p of the unit is exp(s - m_ref) with the m_ref of
+        // its split, O and the row sums follow each move of m_ref.  l_acc:
+        // this thread's key slot's share of the row sums.
+        float m_ref[R], l_acc[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            m_ref[r] = NEG_INF;
+            l_acc[r] = 0.0f;
+        }
         Walk wk;
         wk.start(a, u0, u1);
         for (int i = 0; wk.valid(); i++, wk.next(a)) {
-            const int sb = i & 1, slot = i % RING;
-            const int64_t g = wk.group(a);
+            const int sb = i & 1;
+            const int g = wk.group(a);
             const Split x = split_of(a, wk.s);
-            float *sm = red + ((slot * 2 + h) * 4) * 8;  // maxima [warp][row]
-            int *wi = reinterpret_cast<int *>(smem + OFF_WIN) + (slot * 2 + h) * WIN_WORDS;
+            float *sm = red + (sb * 2 + h) * 32;  // this split's maxima [warp][row]
             float lg[R];
+            bool need = false;
             if (ok && g != prev_g) {
                 // Q' of this group's head h: row (term * 8 + r) holds term (hi,
                 // mid, lo) of q[r][2g + h], three BF16 values summing to the
@@ -469,7 +489,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (ok) {
                 tc_fence_after();
                 uint32_t sv[32];
-                FO_TMEM_LD32(tmem + ((uint32_t)(qd * 32) << 16) + sb * 64 + h * 32, sv);
+                FO_TMEM_LD32(tq + sb * 64 + h * 32, sv);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
@@ -484,68 +504,116 @@ __global__ void __launch_bounds__(THREADS, 1)
                                                 __uint_as_float(sv[16 + r]));
                     lg[r] = (pos < x.k1 && pos < a.len0 + r) ? __fmul_rn(dot, 0.125f) : NEG_INF;
                 }
-                // Row maxima over the split's keys: per warp here, over the
-                // head's four warps after the exchange.
+                // This warp's row maxima; a row whose maximum passes its
+                // reference by more than TAU (or gets its first key) asks the
+                // head to move the reference.
 #pragma unroll
                 for (int r = 0; r < R; r++) {
                     const float m = warp_max_redux(lg[r]);
-                    if (lane == 0) sm[w4 * 8 + r] = m;
+                    if (lane == 0) sm[qd * 8 + r] = m;
+                    need |= m_ref[r] == NEG_INF ? m != NEG_INF : m > __fadd_rn(m_ref[r], TAU);
                 }
-                if (w4 == 0 && lane == 0) wi[0] = 0;  // this split's window record
             }
-            sync_head(h);
-            if (!ok || *abort_flag) {
-                ok = false;
-                continue;  // the remaining splits only pass the exchange
-            }
+            need = vote_head(h, need);
+            if (ok && *abort_flag) ok = false;
             float p[R];
+            if (ok) {
+                bool rescale = false;
+                float alpha[R];
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                float m = NEG_INF;
+                for (int r = 0; r < R; r++) alpha[r] = 1.0f;
+                if (need) {
 #pragma unroll
-                for (int ww = 0; ww < 4; ww++) m = rmax(m, sm[ww * 8 + r]);
-                p[r] = lg[r] == NEG_INF ? 0.0f : key_exp<FAST>(__fsub_rn(lg[r], m));
-            }
-            // The draft window [len0, last) of a tail split: a key whose value
-            // row holds a non-finite number leaves the MMA (head 0's thread of
-            // the key zeroes its staged row) and the epilogue adds it to the
-            // rows that see it.  Both heads test the row in global memory, so
-            // neither test depends on the other's zeroing.
-            const int64_t pos = x.k0 + key;
-            bool nonfinite = false;
-            if (x.tail && pos >= a.len0 && pos < x.k1) {
-                const uint4 *vg = reinterpret_cast<const uint4 *>(
-                    reinterpret_cast<const uint16_t *>(pg.tail_codes) +
-                    (g * pg.tail_stride + (pos - a.prefix_len)) * FO_TAIL_RECORD + 64);
+                    for (int r = 0; r < R; r++) {
+                        float m = NEG_INF;
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    const uint4 q4 = vg[c];
-                    const uint32_t ws[4] = {q4.x, q4.y, q4.z, q4.w};
+                        for (int ww = 0; ww < 4; ww++) m = rmax(m, sm[ww * 8 + r]);
+                        if (m_ref[r] == NEG_INF) {
+                            m_ref[r] = m;  // O and the row sums are still zero
+                        } else if (m > __fadd_rn(m_ref[r], TAU)) {
+                            alpha[r] = expf(__fsub_rn(m_ref[r], m));
+                            m_ref[r] = m;
+                            l_acc[r] = __fmul_rn(l_acc[r], alpha[r]);
+                            rescale = true;
+                        }
+                    }
+                }
 #pragma unroll
-                    for (int e = 0; e < 4; e++)
-                        nonfinite |= ((ws[e] & 0x7F80u) == 0x7F80u) || ((ws[e] & 0x7F800000u) == 0x7F800000u);
+                for (int r = 0; r < R; r++) {
+                    p[r] = lg[r] == NEG_INF ? 0.0f : key_exp<FAST>(__fsub_rn(lg[r], m_ref[r]));
+                    l_acc[r] = __fadd_rn(l_acc[r], p[r]);
+                }
+                if (rescale && (hi_warp || lo_warp)) {
+                    // O rows of this head hold the unit so far against the old
+                    // references: scale them once PV of the split before (an
+                    // earlier split of this unit) is in, before PV of this one.
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(pv_done + ((i - 1) & 1), ((i - 1) >> 1) & 1, abort_flag, pg.err));
+                    if (ok) {
+                        tc_fence_after();
+                        float al = 1.0f;
+#pragma unroll
+                        for (int r = 0; r < R; r++)
+                            if (lane == r) al = alpha[r];
+#pragma unroll
+                        for (int half = 0; half < 2; half++) {
+                            uint32_t o[32];
+                            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int d = 0; d < 32; d++) o[d] = __float_as_uint(__fmul_rn(__uint_as_float(o[d]), al));
+                            FO_TMEM_ST32(tq + TM_O + 32 * half, o);
+                        }
+                        tmem_wait_st();
+                        tc_fence_before();
+                    }
                 }
             }
-            if (nonfinite) {
-                const int e = atomicAdd(wi, 1);  // at most rows - 1 keys
-                wi[1 + e] = key;
-                float *wp = reinterpret_cast<float *>(wi + 9) + e * 8;
+            if (ok) {
+                // The draft window [len0, last) of a tail split: a key whose value
+                // row holds a non-finite number leaves the MMA (head 0's thread of
+                // the key zeroes its staged row) and the unit's end adds it to the
+                // rows that see it.  Both heads test the row in global memory, so
+                // neither test depends on the other's zeroing.
+                const int64_t pos = x.k0 + key;
+                bool nonfinite = false;
+                if (x.tail && pos >= a.len0 && pos < x.k1) {
+                    const uint4 *vg = reinterpret_cast<const uint4 *>(
+                        reinterpret_cast<const uint16_t *>(pg.tail_codes) +
+                        ((int64_t)g * pg.tail_stride + (pos - a.prefix_len)) * FO_TAIL_RECORD + 64);
 #pragma unroll
-                for (int r = 0; r < 8; r++) wp[r] = r < R ? p[r < R ? r : 0] : 0.0f;
-                if (h == 0) {
-                    drain_wait(full + i % STAGES, (i / STAGES) & 1);  // the row's arrival, observed here
-                    const uint32_t vrow = smem_u32(smem + (i % STAGES) * STAGE + 2 * BOX + key * 128);
+                    for (int c = 0; c < 8; c++) {
+                        const uint4 q4 = vg[c];
+                        const uint32_t ws[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-                    for (int c = 0; c < 8; c++) st_shared_v4(vrow + (c << 4), 0u, 0u, 0u, 0u);
+                        for (int e = 0; e < 4; e++)
+                            nonfinite |= ((ws[e] & 0x7F80u) == 0x7F80u) || ((ws[e] & 0x7F800000u) == 0x7F800000u);
+                    }
                 }
+                if (nonfinite) {
+                    const int e = atomicAdd(win, 1);  // at most rows - 1 keys a unit
+                    win[1 + e] = (int)(pos - a.prefix_len);
+                    float *wp = reinterpret_cast<float *>(win + 9) + e * 8;
+                    float *wm = reinterpret_cast<float *>(win + 9 + 64) + e * 8;
+#pragma unroll
+                    for (int r = 0; r < 8; r++) {
+                        wp[r] = r < R ? p[r < R ? r : 0] : 0.0f;
+                        wm[r] = r < R ? m_ref[r < R ? r : 0] : 0.0f;
+                    }
+                    if (h == 0) {
+                        drain_wait(full + i % STAGES, (i / STAGES) & 1);  // the row's arrival, observed here
+                        const uint32_t vrow = smem_u32(smem + (i % STAGES) * STAGE + 2 * BOX + key * 128);
+#pragma unroll
+                        for (int c = 0; c < 8; c++) st_shared_v4(vrow + (c << 4), 0u, 0u, 0u, 0u);
+                    }
+                }
+                // P' of this key into buffer i & 1 once PV of split i - 2 (that
+                // buffer's last reader) is done.
+                if (i >= 2)
+                    ok = __all_sync(0xffffffffu,
+                                    mbar_wait(pv_done + (i & 1), ((i - 2) >> 1) & 1, abort_flag, pg.err));
             }
-            // P' of this key into buffer i & 1 once PV of split i - 2 (that
-            // buffer's last reader) is done: hi terms in M rows 8h .. 8h + 7,
-            // lo terms in rows 16 + 8h .. 16 + 8h + 7.
-            if (i >= 2 && !(ok = __all_sync(0xffffffffu, mbar_wait(pv_done + (i & 1), ((i - 2) >> 1) & 1,
-                                                                   abort_flag, pg.err))))
-                continue;
-            {
+            if (ok) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int r2 = 0; r2 < 4; r2++) {
@@ -557,159 +625,119 @@ __global__ void __launch_bounds__(THREADS, 1)
                                        __fsub_rn(a1, __uint_as_float(ph & 0xFFFF0000u)));
                 }
                 const uint32_t prow = smem_u32(smem + OFF_P + (i & 1) * BOX + key * 128);
-                st_shared_v4(prow + (uint32_t)((h ^ (key & 7)) << 4), hi[0], hi[1], hi[2], hi[3]);
-                st_shared_v4(prow + (uint32_t)(((2 + h) ^ (key & 7)) << 4), lo[0], lo[1], lo[2], lo[3]);
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-        }
-    } else {
-        // ------------------------------------------------ epilogue (warps 0, 1)
-        // Warp 0 reads O's hi rows (TMEM lanes 8h + r of quadrant 0), warp 1
-        // its lo rows (quadrant 1) and hands them over through shared memory;
-        // warp 0 folds hi + lo of each split into the unit's partial (lane
-        // 8h + r: head h, row r) and writes it at the unit's end.
-        const bool hi_warp = warp == 0;
-        const int h = lane >> 3, er = lane & 7;
-        const bool erow = lane < 16 && er < R;
-        const int64_t H = a.H;
-        const float NEG_INF = -INFINITY;
-        const float *red = reinterpret_cast<const float *>(smem + OFF_RED);
-        float *o_acc = reinterpret_cast<float *>(smem + OFF_ACC) + (lane & 15) * ACC_STRIDE;
-        float m_run = NEG_INF, l_run = 0.0f;
-        bool ok = true;
-        Walk wk;
-        wk.start(a, u0, u1);
-        for (int j = 0; wk.valid() && ok; j++, wk.next(a)) {
-            const int slot = j % RING;
-            // Split j's PV: pv_done[j & 1] moves on only after this split's
-            // o_empty, so its phase cannot be overtaken.
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(pv_done + (j & 1), (j >> 1) & 1, abort_flag, pg.err))))
-                break;
-            tc_fence_after();
-            const uint32_t tO = tmem + ((uint32_t)(warp * 32) << 16) + TM_O + (j & 1) * 64;
-            float *lo = reinterpret_cast<float *>(smem + OFF_LO) + ((j & 1) * 16 + (lane & 15)) * ACC_STRIDE;
-            const float l_part = __uint_as_float(tmem_ld1(tmem + ((uint32_t)(warp * 32) << 16) + TM_L + (j & 1) * 8));
-            if (!hi_warp) {
-                tmem_wait_ld();
-                if (erow) lo[64] = l_part;
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    uint32_t o[32];
-                    FO_TMEM_LD32(tO + 32 * half, o);
-                    tmem_wait_ld();
-                    if (erow) {
-                        float4 *dst = reinterpret_cast<float4 *>(lo + 32 * half);
-#pragma unroll
-                        for (int d = 0; d < 8; d++)
-                            dst[d] = make_float4(__uint_as_float(o[4 * d]), __uint_as_float(o[4 * d + 1]),
-                                                 __uint_as_float(o[4 * d + 2]), __uint_as_float(o[4 * d + 3]));
-                    }
-                }
-                tc_fence_before();
+                st_shared_v4(prow + (uint32_t)(((4 * h) ^ (key & 7)) << 4), hi[0], hi[1], hi[2], hi[3]);
+                st_shared_v4(prow + (uint32_t)(((4 * h + 2) ^ (key & 7)) << 4), lo[0], lo[1], lo[2], lo[3]);
+                fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(lo_ready + (j & 1));
-                    mbar_arrive(o_empty + (j & 1));
-                }
-                continue;
-            }
-            // This split's max of row (h, er): the head's four warps (the key
-            // warps wrote them before this split's P').
-            float m_split = NEG_INF;
-            if (erow) {
-                const float *sm = red + ((slot * 2 + h) * 4) * 8;
-#pragma unroll
-                for (int ww = 0; ww < 4; ww++) m_split = rmax(m_split, sm[ww * 8 + er]);
-            }
-            const bool live = erow && m_split != NEG_INF;
-            const bool first = m_run == NEG_INF;
-            float fa = 1.0f, fb = 1.0f, m_new = m_split;
-            if (live && !first) {
-                m_new = rmax(m_run, m_split);
-                fa = expf(__fsub_rn(m_run, m_new));
-                fb = expf(__fsub_rn(m_split, m_new));
-            }
-            // Non-finite values of the draft window, added for the rows that
-            // see them (the MMA saw their value rows as zero).
-            const int *wr = reinterpret_cast<const int *>(smem + OFF_WIN) + (slot * 2 + h) * WIN_WORDS;
-            const int nw = live ? wr[0] : 0;
-            const Split x = split_of(a, wk.s);
-            const int64_t g = wk.group(a);
-            uint32_t o[2][32];
-            FO_TMEM_LD32(tO, o[0]);
-            FO_TMEM_LD32(tO + 32, o[1]);
-            tmem_wait_ld();
-            tc_fence_before();
-            if (!(ok = __all_sync(0xffffffffu, mbar_wait(lo_ready + (j & 1), (j >> 1) & 1, abort_flag, pg.err))))
-                break;
-            // The split's row sum: the hi and lo terms' l columns.
-            const float l_split = erow ? __fadd_rn(l_part, lo[64]) : 0.0f;
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                if (live) {
-                    float ov[32];
-                    const float4 *lv = reinterpret_cast<const float4 *>(lo + 32 * half);
-#pragma unroll
-                    for (int d = 0; d < 8; d++) {
-                        const float4 l4 = lv[d];
-                        ov[4 * d] = __fadd_rn(__uint_as_float(o[half][4 * d]), l4.x);
-                        ov[4 * d + 1] = __fadd_rn(__uint_as_float(o[half][4 * d + 1]), l4.y);
-                        ov[4 * d + 2] = __fadd_rn(__uint_as_float(o[half][4 * d + 2]), l4.z);
-                        ov[4 * d + 3] = __fadd_rn(__uint_as_float(o[half][4 * d + 3]), l4.w);
-                    }
-                    for (int e = 0; e < nw; e++) {
-                        const int kl = wr[1 + e];
-                        if (x.k0 + kl >= a.len0 + er) continue;  // this row does not see it
-                        const float pk = reinterpret_cast<const float *>(wr + 9)[e * 8 + er];
-                        const uint16_t *vr = reinterpret_cast<const uint16_t *>(pg.tail_codes) +
-                                             (g * pg.tail_stride + (x.k0 + kl - a.prefix_len)) * FO_TAIL_RECORD + 64 +
-                                             32 * half;
-                        for (int d = 0; d < 32; d++) ov[d] = fmaf(pk, bf16_f32(vr[d]), ov[d]);
-                    }
-                    float4 *acc = reinterpret_cast<float4 *>(o_acc + 32 * half);
-#pragma unroll
-                    for (int d = 0; d < 8; d++) {
-                        float4 y = first ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[d];
-                        y.x = first ? ov[4 * d] : fmaf(ov[4 * d], fb, __fmul_rn(y.x, fa));
-                        y.y = first ? ov[4 * d + 1] : fmaf(ov[4 * d + 1], fb, __fmul_rn(y.y, fa));
-                        y.z = first ? ov[4 * d + 2] : fmaf(ov[4 * d + 2], fb, __fmul_rn(y.z, fa));
-                        y.w = first ? ov[4 * d + 3] : fmaf(ov[4 * d + 3], fb, __fmul_rn(y.w, fa));
-                        acc[d] = y;
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(o_empty + (j & 1));
-            if (live) {
-                l_run = first ? l_split : fmaf(l_split, fb, __fmul_rn(l_run, fa));
-                m_run = m_new;
+                if (lane == 0) mbar_arrive(p_full);
             }
             if (wk.last_of_unit()) {
-                if (erow) {
-                    const int64_t row_head = (int64_t)er * H + 2 * g + h;
-                    const int64_t idx = row_head * pg.splits + wk.unit(a);
-                    float4 *dst = reinterpret_cast<float4 *>(pg.part_o + idx * FO_HD);
-                    const float4 *acc = reinterpret_cast<const float4 *>(o_acc);
-                    if (m_run == NEG_INF) {
-                        // No key of the unit is this row's: an empty partial.
+                // The unit's end: the row sums over the head's 128 key slots
+                // (a butterfly per warp, then the four warps in order); once
+                // the unit's last PV is in, the head's hi warp adds O's lo rows
+                // to its hi rows, adds the draft window's non-finite values and
+                // writes the unit's partial (lane r: row r).  The meeting
+                // orders the window list and the row sums.
 #pragma unroll
-                        for (int d = 0; d < 16; d++) dst[d] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    } else {
+                for (int r = 0; r < R; r++) {
+                    float v = l_acc[r];
 #pragma unroll
-                        for (int d = 0; d < 16; d++) dst[d] = acc[d];
-                    }
-                    *reinterpret_cast<float2 *>(pg.part_ml + idx * 2) = make_float2(m_run, l_run);
+                    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                    if (lane == 0) lsum[qd * 8 + r] = v;
+                    l_acc[r] = 0.0f;
                 }
-                m_run = NEG_INF;
-                l_run = 0.0f;
+                bar_named(3 + h, 128);
+                if (hi_warp || lo_warp) {
+                    const bool o_ok =
+                        ok && __all_sync(0xffffffffu, mbar_wait(pv_done + (i & 1), (i >> 1) & 1, abort_flag, pg.err));
+                    if (o_ok) tc_fence_after();
+                    float *lo = reinterpret_cast<float *>(smem + OFF_LO) + (h * 8 + (lane & 7)) * ACC_STRIDE;
+                    if (lo_warp && o_ok) {
+#pragma unroll
+                        for (int half = 0; half < 2; half++) {
+                            uint32_t o[32];
+                            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
+                            tmem_wait_ld();
+                            if (lane < R) {
+                                float4 *dst = reinterpret_cast<float4 *>(lo + 32 * half);
+#pragma unroll
+                                for (int d = 0; d < 8; d++)
+                                    dst[d] = make_float4(__uint_as_float(o[4 * d]), __uint_as_float(o[4 * d + 1]),
+                                                         __uint_as_float(o[4 * d + 2]), __uint_as_float(o[4 * d + 3]));
+                            }
+                        }
+                    }
+                    bar_named(5 + h, 64);
+                    if (hi_warp && o_ok) {
+                        float m_fin = NEG_INF;
+#pragma unroll
+                        for (int r = 0; r < R; r++)
+                            if (lane == r) m_fin = m_ref[r];
+                        const int64_t row_head = (int64_t)lane * H + 2 * g + h;
+                        const int64_t idx = row_head * pg.splits + wk.unit(a);
+                        float4 *dst = reinterpret_cast<float4 *>(pg.part_o + idx * FO_HD);
+                        const bool live = lane < R && m_fin != NEG_INF;
+                        const int nw = live ? win[0] : 0;
+                        const float *wp = reinterpret_cast<const float *>(win + 9);
+                        const float *wm = reinterpret_cast<const float *>(win + 9 + 64);
+#pragma unroll
+                        for (int half = 0; half < 2; half++) {
+                            uint32_t o[32];
+                            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
+                            tmem_wait_ld();
+                            if (live) {
+                                float ov[32];
+                                const float4 *lv = reinterpret_cast<const float4 *>(lo + 32 * half);
+#pragma unroll
+                                for (int d = 0; d < 8; d++) {
+                                    const float4 l4 = lv[d];
+                                    ov[4 * d] = __fadd_rn(__uint_as_float(o[4 * d]), l4.x);
+                                    ov[4 * d + 1] = __fadd_rn(__uint_as_float(o[4 * d + 1]), l4.y);
+                                    ov[4 * d + 2] = __fadd_rn(__uint_as_float(o[4 * d + 2]), l4.z);
+                                    ov[4 * d + 3] = __fadd_rn(__uint_as_float(o[4 * d + 3]), l4.w);
+                                }
+                                for (int e = 0; e < nw; e++) {
+                                    const int tr = win[1 + e];
+                                    if (a.prefix_len + tr >= a.len0 + lane) continue;  // this row does not see it
+                                    const float pk =
+                                        __fmul_rn(wp[e * 8 + lane], expf(__fsub_rn(wm[e * 8 + lane], m_fin)));
+                                    const uint16_t *vr = reinterpret_cast<const uint16_t *>(pg.tail_codes) +
+                                                         ((int64_t)g * pg.tail_stride + tr) * FO_TAIL_RECORD + 64 +
+                                                         32 * half;
+#pragma unroll
+                                    for (int d = 0; d < 32; d++) ov[d] = fmaf(pk, bf16_f32(vr[d]), ov[d]);
+                                }
+#pragma unroll
+                                for (int d = 0; d < 8; d++)
+                                    dst[half * 8 + d] = make_float4(ov[4 * d], ov[4 * d + 1], ov[4 * d + 2], ov[4 * d + 3]);
+                            } else if (lane < R) {
+                                // No key of the unit is this row's: an empty partial.
+#pragma unroll
+                                for (int d = 0; d < 8; d++) dst[half * 8 + d] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+                        }
+                        if (lane < R) {
+                            float l_run = 0.0f;
+                            if (live)
+                                l_run = __fadd_rn(__fadd_rn(__fadd_rn(lsum[lane], lsum[8 + lane]), lsum[16 + lane]),
+                                                  lsum[24 + lane]);
+                            *reinterpret_cast<float2 *>(pg.part_ml + idx * 2) = make_float2(m_fin, l_run);
+                        }
+                    }
+                    if (o_ok) tc_fence_before();
+                    if (hi_warp) {
+                        __syncwarp();
+                        if (lane == 0) win[0] = 0;  // this warp is the list's last reader
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < R; r++) m_ref[r] = NEG_INF;
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == W_MMA) {
+    if (warp == W_PV) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
@@ -804,10 +832,12 @@ static cudaError_t launch_tc(const fo_decode_page &pg, int64_t groups, cudaStrea
     a.chunk = pg.chunk;
     a.prefix_units = (pg.prefix_splits + pg.chunk - 1) / pg.chunk;
     a.units = pg.splits;
-    a.n_units = (int64_t)pg.splits * groups;
+    if ((int64_t)pg.splits * groups >= (int64_t(1) << 24)) return cudaErrorInvalidValue;
+    a.n_units = (uint32_t)(pg.splits * groups);
     const unsigned grid = (unsigned)std::min<int64_t>(a.n_units, device_sms());
     fo::tc::decode_tc_kernel<FAST, R><<<grid, fo::tc::THREADS, fo::tc::SMEM, stream>>>(pg, a);
-    return cudaGetLastError();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    return fo_launch_decode_merge(&pg, groups, stream);
 }
 
 extern "C" cudaError_t fo_launch_decode_tc(const fo_decode_page *page, int64_t groups, int fast_exp,
@@ -830,6 +860,5 @@ extern "C" cudaError_t fo_launch_decode_tc(const fo_decode_page *page, int64_t g
         FO_TC_ROWS(8)
     }
 #undef FO_TC_ROWS
-    if (e != cudaSuccess) return e;
-    return fo_launch_decode_merge(page, groups, stream);
+    return e;
 }

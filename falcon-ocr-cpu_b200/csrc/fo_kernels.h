@@ -85,8 +85,8 @@ bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t
 // One page (descriptor read on the host, passed by value).
 cudaError_t fo_launch_decode_one(const fo_decode_page *page, int format, int64_t groups, int fast_exp,
                                  cudaStream_t stream);
-// One page of BF16 records on the tensor cores (decode_tc.cu); the page has
-// prefix_splits set and its tc maps built.
+// One page of BF16 records on the tensor cores (decode_tc.cu) and its split
+// merge; the page has prefix_splits and its tc maps set.
 cudaError_t fo_launch_decode_tc(const fo_decode_page *page, int64_t groups, int fast_exp, cudaStream_t stream);
 // The split merge of one page (a programmatic dependent of the decode just
 // launched on `stream`).

@@ -143,8 +143,11 @@ def test_baseline_c1_causal_fp32(ctx):
 FORMATS = [F.KV_F32, F.KV_Q16, F.KV_Q8, F.KV_BF16]
 
 
-def sealed_pair(fmt, p, generated, seed, capacity=None):
+def sealed_pair(fmt, p, generated, seed, capacity=None, key_scale=None):
     k, v, q = G.kv_fixture(p, seed)
+    if key_scale is not None:
+        # per-position factors on every head's key (pairs stay shared)
+        k = (k.reshape(p, -1) * key_scale.astype(np.float32)[:, None]).astype(np.float32).reshape(-1)
     capacity = capacity or p + max(generated, 1)
     ref = O.SplitCache(k, v, p, capacity, fmt=fmt)
     gpu = F.SplitPrefix.from_compact(dev(k), dev(v), p, capacity, fmt=fmt)
@@ -243,6 +246,28 @@ def test_verification_rows_are_bitwise_single_rows(ctx, fmt):
             single = np.zeros(1024, np.float32)
             gpu.attention_decode(q[r * 1024:(r + 1) * 1024], p + gpu.tail_len, sinks, single)
             assert np.array_equal(joint[r * 1024:(r + 1) * 1024].view(np.uint32), single.view(np.uint32)), (p, r)
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_growing_logits_move_the_running_maximum(ctx, fmt):
+    """Keys scaled per block of 128 positions so that the largest logit grows
+    by about 10 (more than a factor e^8 in p) from one block to the next,
+    within the runs of consecutive blocks a decode sums as one: the running
+    sums are rescaled on the way and still match the oracle, and every verify
+    row still equals its single-row decode bit for bit."""
+    p, generated, rows = 8192, 6, 5
+    scale = 1.0 + 30.0 * ((np.arange(p) // 128) % 4)
+    ref, gpu, _ = sealed_pair(fmt, p, generated, 7, key_scale=scale)
+    q = G.kv_rows_query(rows)
+    sinks = np.array([h * 0.25 - 1.0 for h in range(16)], np.float32)
+    joint = np.zeros(rows * 1024, np.float32)
+    gpu.attention_decode_rows(q, rows, sinks, joint)
+    close(joint, ref.decode_rows(q, rows, sinks), 1e-5, 1e-5)
+    for r in reversed(range(rows)):
+        gpu.truncate_tail(generated - (rows - 1 - r))
+        single = np.zeros(1024, np.float32)
+        gpu.attention_decode(q[r * 1024:(r + 1) * 1024], p + gpu.tail_len, sinks, single)
+        assert np.array_equal(joint[r * 1024:(r + 1) * 1024].view(np.uint32), single.view(np.uint32)), r
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
