@@ -584,6 +584,100 @@ def time_decode(run, args, lengths=(DECODE_L,)):
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # 148 SMs x 128 FP32 FMA/clk x 1.965 GHz
 
 
+PAGES = 64  # BASELINE config 5(a): independent pages, sharded by page
+PAGE_STEPS = 2048  # single-row decode steps per page after its prefill
+
+
+def time_pages(run, args):
+    """BASELINE config 5(a): 64 independent pages, each a 6,544-token
+    prefix-LM prefill (C2, BF16 static shift) and then 2,048 single-row
+    decode steps against its own growing BF16 split cache (KV 6,545 ->
+    8,592), pages round-robin over the ranks with no collective.  Each step
+    appends the new row to every page of the rank (fo_kv_append_batch) and
+    decodes one row per page (fo_kv_attention_decode_batch), as
+    Model::decode_batch_next does per layer (src/model/mod.rs:760-852).
+    The caches are allocated and sealed from the pages' K/V before the timed
+    region (allocation is not a per-page cost); the timed job is every
+    prefill, append and decode of the rank's pages, device time max over
+    ranks.  Synthetic pages: C2's inputs (seed 4) with each GQA pair's
+    temporal key half shared, as the split cache's records require."""
+    import ctypes
+    import generators as G
+    torch, F = run.torch, run.F
+    mine = list(range(run.rank, PAGES, run.world))
+    n = len(mine)
+    q, k, v, sinks, geo = G.c2_inputs(seed=4)
+    k = k.copy()
+    k[:, 1::2, :32] = k[:, 0::2, :32]
+    qd, kd, vd = (torch.from_numpy(x).to(run.dev) for x in (q, k, v))
+    kb, vb = kd.to(torch.bfloat16), vd.to(torch.bfloat16)
+    sd = torch.from_numpy(sinks).to(run.dev)
+    outs = [torch.empty(SEQ * HEADS * 64, device=run.dev) for _ in range(2)]
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
+    warm = 4
+    caches = [F.SplitPrefix.from_compact(kd, vd, SEQ, SEQ + PAGE_STEPS + warm, fmt="bf16", ctx=run.ctx)
+              for _ in mine]
+    rng = np.random.default_rng(40 + run.rank)
+    row = rng.standard_normal((2, 1, KV_HEADS, 1, 64)).astype(np.float32)
+    row = torch.from_numpy(np.repeat(row, 2, axis=3).reshape(2, -1)).to(run.dev)  # expanded K, V rows
+    qrow = torch.from_numpy(rng.standard_normal(HEADS * 64).astype(np.float32)).to(run.dev)
+    dec_out = torch.empty((n, HEADS * 64), device=run.dev)
+    L = F.lib()
+    arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
+    a_c = arr([c.handle.value for c in caches])
+    a_k, a_v = arr([row[0].data_ptr()] * n), arr([row[1].data_ptr()] * n)
+    a_q, a_s = arr([qrow.data_ptr()] * n), arr([sd.data_ptr()] * n)
+    a_o = arr([dec_out[i].data_ptr() for i in range(n)])
+
+    def prefill(i):
+        F.attention_prefill_bf16(qd, kd, vd, geo, sd, outs[i & 1], HEADS, KV_HEADS, keys_bf16=kb, values_bf16=vb,
+                                 options=opts, ctx=run.ctx)
+
+    def step():
+        F.check(L.fo_kv_append_batch(a_c, n, a_k, a_v, 1))
+        F.check(L.fo_kv_attention_decode_batch(a_c, n, a_q, a_s, a_o))
+
+    for i in range(warm):  # untimed: warm both paths, then give the tails back
+        prefill(i)
+        step()
+    for c in caches:
+        c.truncate_tail(0)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    run.barrier()
+    ev[0].record()
+    for i in range(n):
+        prefill(i)
+    ev[1].record()
+    for _ in range(PAGE_STEPS):
+        step()
+    ev[2].record()
+    run.barrier()
+    assert all(c.tail_len == PAGE_STEPS for c in caches)
+    total_ms = run.max_over_ranks(ev[0].elapsed_time(ev[2]))
+    prefill_ms = run.max_over_ranks(ev[0].elapsed_time(ev[1]))
+    decode_ms = run.max_over_ranks(ev[1].elapsed_time(ev[2]))
+    # per step the rank's decode reads every page's records once
+    pos = sum(SEQ + s + 1 for s in range(PAGE_STEPS)) / PAGE_STEPS
+    step_bytes = n * pos * RECORD_BYTES["bf16"]
+    gbs = step_bytes / (decode_ms / PAGE_STEPS * 1e-3) / 1e9
+    res = {"workload": f"C5a: {PAGES} pages x (C2 prefill + {PAGE_STEPS} single-row decode steps), BF16 cache, "
+                       "pages round-robin over ranks, no collective",
+           "pages_per_s": round(PAGES / (total_ms / 1e3), 2), "seconds": round(total_ms / 1e3, 4),
+           "pages_per_rank": n, "prefill_ms": round(prefill_ms, 3), "decode_ms": round(decode_ms, 3),
+           "decode_us_per_step": round(decode_ms * 1e3 / PAGE_STEPS, 2),
+           "decode_roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"], "unit": "GB/s",
+                               "frac": round(gbs / run.peaks["hbm_gbs"], 4),
+                               "note": "record bytes of every page per step (prefix records 2,560 B per position; "
+                                       "tail records counted at the same size)"},
+           "gpu_launches": n + 3 * PAGE_STEPS, "scaling": "weak per page, strong per job",
+           "note": "caches sealed before the timed region; one append, one decode and one merge launch per step"}
+    for c in caches:
+        c.close()
+    del outs, dec_out
+    torch.cuda.empty_cache()
+    return res
+
+
 def time_prefill_rows(run, args, inputs):
     """Secondary prefill rows of the C2 page: the FP32 exact tiles
     (fo_attention, platform-exact exp; bound by FP32 CUDA cores) and the
@@ -667,6 +761,8 @@ def run_ours(args, world, rank, local):
         extra["decode_c4"] = time_c4(run, args)
     if args.mode in ("full", "sharded"):
         extra["sharded_prefill"] = time_sharded(run, args)
+    if args.mode in ("full", "pages"):
+        extra["pages"] = time_pages(run, args)
     if args.mode == "full":
         extra["prefill_rows"] = time_prefill_rows(run, args, inputs)
     cpu_decode_us = None
@@ -698,7 +794,7 @@ def main():
                     help="key ranges per query pair in the sharded prefill (0: chosen from the CTA count)")
     ap.add_argument("--bands", type=int, default=1,
                     help="query-row bands of the sharded prefill (C5b); one band measured fastest at 2 ranks")
-    ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded"], default="full",
+    ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded", "pages"], default="full",
                     help="full: the contract line; prefill/decode: only that part (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()

@@ -142,6 +142,8 @@ struct fo_ctx {
     DevBuf split_o, split_ml;                  // key-range split partials of the row-band prefill
     DevBuf pages;                              // decode batch descriptors (device)
     HostDesc host_pages;                       // and their pinned staging
+    DevBuf append_pages;                       // batched-append descriptors (device)
+    HostDesc host_append_pages;
     DevBuf i8_pages;                           // INT8-format decode descriptors (device)
     HostDesc host_i8_pages;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -406,6 +408,8 @@ int fo_ctx_create(int device, void *stream, fo_ctx **out) {
     if (e == cudaSuccess) e = cudaEventCreate(&ctx->ev1);
     if (e == cudaSuccess) e = ctx->pages.ensure(sizeof(fo_decode_page) * FO_BATCH_PAGES);
     if (e == cudaSuccess) e = ctx->host_pages.ensure(sizeof(fo_decode_page) * FO_BATCH_PAGES);
+    if (e == cudaSuccess) e = ctx->append_pages.ensure(sizeof(fo_append_page) * FO_BATCH_PAGES);
+    if (e == cudaSuccess) e = ctx->host_append_pages.ensure(sizeof(fo_append_page) * FO_BATCH_PAGES);
     if (e == cudaSuccess) e = ctx->i8_pages.ensure(sizeof(fo_i8_page) * FO_BATCH_PAGES);
     if (e == cudaSuccess) e = ctx->host_i8_pages.ensure(sizeof(fo_i8_page) * FO_BATCH_PAGES);
     if (e != cudaSuccess) {
@@ -427,6 +431,8 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     ctx->split_ml.release();
     ctx->pages.release();
     ctx->host_pages.release();
+    ctx->append_pages.release();
+    ctx->host_append_pages.release();
     ctx->i8_pages.release();
     ctx->host_i8_pages.release();
     if (ctx->flags) cudaFree(ctx->flags);
@@ -747,6 +753,48 @@ int fo_kv_append(fo_kv_cache *c, const float *k, const float *v, int64_t rows, i
         if (mem == FO_MEM_HOST) FO_CUDA(cudaStreamSynchronize(c->ctx->stream), "cudaStreamSynchronize");
         c->tail_len += n;
         done += n;
+    }
+    return FO_OK;
+}
+
+int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const *k, const float *const *v,
+                       int64_t rows) {
+    if (!caches || !k || !v || n < 0 || rows < 0) return fail(FO_ERR_INVALID, "append batch: bad argument");
+    if (n == 0 || rows == 0) return FO_OK;
+    fo_ctx *ctx = caches[0] ? caches[0]->ctx : nullptr;
+    if (!ctx) return fail(FO_ERR_INVALID, "append batch: null cache");
+    const fo_kv_cache *c0 = caches[0];
+    for (int64_t i = 0; i < n; i++) {
+        const fo_kv_cache *c = caches[i];
+        if (!c || !k[i] || !v[i]) return fail(FO_ERR_INVALID, "append batch: null entry %lld", (long long)i);
+        if (c->ctx != ctx || c->format != c0->format || c->heads != c0->heads)
+            return fail(FO_ERR_INVALID, "append batch: caches must share context, format and heads");
+        if (c->tail_len + rows > c->tail_capacity)
+            return fail(FO_ERR_CAPACITY, "append batch: cache %lld: split tail capacity", (long long)i);
+    }
+    {  // each cache's tail grows once per call
+        std::vector<const fo_kv_cache *> seen(caches, caches + n);
+        std::sort(seen.begin(), seen.end());
+        if (std::adjacent_find(seen.begin(), seen.end()) != seen.end())
+            return fail(FO_ERR_INVALID, "append batch: a cache appears twice");
+    }
+    DeviceGuard guard(ctx->device);
+    for (int64_t base = 0; base < n; base += FO_BATCH_PAGES) {
+        const int64_t m = std::min<int64_t>(FO_BATCH_PAGES, n - base);
+        int slot = 0;
+        fo_append_page *hp = static_cast<fo_append_page *>(ctx->host_append_pages.acquire(slot));
+        for (int64_t i = 0; i < m; i++) {
+            fo_kv_cache *c = caches[base + i];
+            hp[i] = {k[base + i], v[base + i], c->tail_codes, c->tail_scales, c->tail_stride, c->tail_len};
+        }
+        FO_CUDA(cudaMemcpyAsync(ctx->append_pages.ptr, hp, (size_t)m * sizeof(fo_append_page),
+                                cudaMemcpyHostToDevice, ctx->stream),
+                "H2D(append pages)");
+        FO_CUDA(ctx->host_append_pages.uploaded(slot, ctx->stream), "cudaEventRecord");
+        cudaError_t e = fo_launch_append_batch((const fo_append_page *)ctx->append_pages.ptr, m, rows, c0->heads,
+                                               c0->groups, c0->format, ctx->stream);
+        if (e != cudaSuccess) return cuda_fail(e, "append batch launch");
+        for (int64_t i = 0; i < m; i++) caches[base + i]->tail_len += rows;
     }
     return FO_OK;
 }

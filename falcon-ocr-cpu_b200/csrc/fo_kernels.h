@@ -28,6 +28,16 @@ cudaError_t fo_launch_convert_bf16(const float *src, uint16_t *dst, int64_t n, c
 cudaError_t fo_launch_seal(const float *k, const float *v, int64_t prefix_len, int64_t heads, int64_t groups,
                            int format, void *codes, uint16_t *scales, int64_t stride, unsigned *flags,
                            cudaStream_t stream);
+// One cache's share of a batched append: its expanded rows and tail.
+struct fo_append_page {
+    const float *k, *v;  // [rows][H][64]
+    void *tail_codes;
+    uint16_t *tail_scales;
+    int64_t tail_stride, first;
+};
+// Append `rows` expanded rows to each of n pages in one launch.
+cudaError_t fo_launch_append_batch(const fo_append_page *pages, int64_t n, int64_t rows, int64_t heads, int64_t groups,
+                                   int format, cudaStream_t stream);
 // Append rows of expanded K, V [rows][H][64] as tail records at index first..
 cudaError_t fo_launch_append(const float *k, const float *v, int64_t rows, int64_t heads, int64_t groups, int format,
                              void *tail_codes, uint16_t *tail_scales, int64_t tail_stride, int64_t first,

@@ -100,14 +100,11 @@ __global__ void seal_kernel(const float *__restrict__ k, const float *__restrict
     for (int b = 0; b < 5; b++) encode_block(x[b], format, codes, scales, base + 32 * b, false, flags);
 }
 
-// One warp per (row, group) tail record: the group's first head (kv.rs:437-447).
-__global__ void append_kernel(const float *__restrict__ k, const float *__restrict__ v, int64_t rows, int64_t heads,
-                              int64_t groups, int format, void *tail_codes, uint16_t *tail_scales,
-                              int64_t tail_stride, int64_t first) {
-    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (w >= rows * groups) return;
-    const int64_t r = w / groups, g = w % groups;
+// Tail record `first + r` of group g from expanded row r: the group's first
+// head (kv.rs:437-447); one warp, a lane per dimension pair.
+__device__ __forceinline__ void append_record(const float *__restrict__ k, const float *__restrict__ v, int64_t r,
+                                              int64_t g, int64_t heads, int format, void *tail_codes,
+                                              uint16_t *tail_scales, int64_t tail_stride, int64_t first, int lane) {
     const float *kr = k + (r * heads + 2 * g) * FO_HD;
     const float *vr = v + (r * heads + 2 * g) * FO_HD;
     const int64_t base = (g * tail_stride + first + r) * FO_TAIL_RECORD;
@@ -115,6 +112,28 @@ __global__ void append_kernel(const float *__restrict__ k, const float *__restri
     encode_block(kr[32 + lane], format, tail_codes, tail_scales, base + 32, true, nullptr);
     encode_block(vr[lane], format, tail_codes, tail_scales, base + 64, true, nullptr);
     encode_block(vr[32 + lane], format, tail_codes, tail_scales, base + 96, true, nullptr);
+}
+
+// One warp per (row, group) tail record.
+__global__ void append_kernel(const float *__restrict__ k, const float *__restrict__ v, int64_t rows, int64_t heads,
+                              int64_t groups, int format, void *tail_codes, uint16_t *tail_scales,
+                              int64_t tail_stride, int64_t first) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (w >= rows * groups) return;
+    append_record(k, v, w / groups, w % groups, heads, format, tail_codes, tail_scales, tail_stride, first,
+                  threadIdx.x & 31);
+}
+
+// The same over many caches at once: one warp per (page, row, group).
+__global__ void append_batch_kernel(const fo_append_page *__restrict__ pages, int64_t n, int64_t rows,
+                                    int64_t heads, int64_t groups, int format) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t per_page = rows * groups;
+    if (w >= n * per_page) return;
+    const int64_t i = w / per_page, rg = w - i * per_page;
+    const fo_append_page &pg = pages[i];
+    append_record(pg.k, pg.v, rg / groups, rg % groups, heads, format, pg.tail_codes, pg.tail_scales,
+                  pg.tail_stride, pg.first, threadIdx.x & 31);
 }
 
 // FP32 -> BF16, eight values per thread (16-byte stores).
@@ -157,6 +176,16 @@ extern "C" cudaError_t fo_launch_append(const float *k, const float *v, int64_t 
     const int64_t blocks = (warps * 32 + threads - 1) / threads;
     fo::append_kernel<<<(unsigned)blocks, threads, 0, stream>>>(k, v, rows, heads, groups, format, tail_codes,
                                                                 tail_scales, tail_stride, first);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t fo_launch_append_batch(const fo_append_page *pages, int64_t n, int64_t rows, int64_t heads,
+                                              int64_t groups, int format, cudaStream_t stream) {
+    const int64_t warps = n * rows * groups;
+    if (warps == 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    fo::append_batch_kernel<<<(unsigned)blocks, threads, 0, stream>>>(pages, n, rows, heads, groups, format);
     return cudaGetLastError();
 }
 

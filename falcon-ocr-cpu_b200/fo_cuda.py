@@ -92,7 +92,7 @@ EXPORTS = [
     "fo_attention", "fo_attention_prefill_bf16", "fo_convert_bf16", "fo_kv_seal", "fo_kv_destroy",
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
-    "fo_kv_attention_decode_batch", "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
+    "fo_kv_attention_decode_batch", "fo_kv_append_batch", "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
     "fo_i8_decode_batch",
@@ -134,6 +134,7 @@ def lib() -> ctypes.CDLL:
         "fo_kv_attention_decode": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_rows": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_batch": (I, [PP, I64, PP, PP, PP]),
+        "fo_kv_append_batch": (I, [PP, I64, PP, PP, I64]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
         "fo_decode_static_scratch_status": (I, [P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
@@ -384,6 +385,15 @@ def decode_batch(caches: Sequence[SplitPrefix], qs, sinks, outputs):
     check(lib().fo_kv_attention_decode_batch(arr([c.handle.value for c in caches]), n, arr([q.data_ptr() for q in qs]),
                                              arr([s.data_ptr() for s in sinks]),
                                              arr([o.data_ptr() for o in outputs])))
+
+
+def append_batch(caches: Sequence[SplitPrefix], ks, vs, rows: int):
+    """fo_kv_append_batch: `rows` expanded rows into each cache in one launch
+    (device tensors ks[i], vs[i] of [rows][heads][64])."""
+    n = len(caches)
+    arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
+    check(lib().fo_kv_append_batch(arr([c.handle.value for c in caches]), n, arr([k.data_ptr() for k in ks]),
+                                   arr([v.data_ptr() for v in vs]), rows))
 
 
 class Int8Cache:

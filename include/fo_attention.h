@@ -19,6 +19,8 @@
  *   fo_kv_attention_decode_rows  SplitPrefix::attention_decode_rows src/quant/kv.rs:856-865
  *   fo_kv_attention_decode_batch one decode row per page, as Model::decode_batch_next
  *                                  calls LayerCache::attention per page (src/model/mod.rs:827-852)
+ *   fo_kv_append_batch           one append per page, as Model::decode_batch_next calls
+ *                                  SplitPrefix::append per page (src/model/mod.rs:760-852)
  *
  * Entry points with no single reference counterpart (each says why below):
  *   fo_attention_prefill_bf16_rows[_split]  query-row bands of the BF16 prefill
@@ -205,6 +207,14 @@ int fo_kv_set_fast_exp(fo_kv_cache *cache, int32_t fast);
  * [rows][n_heads][64], identical inside each GQA pair; the pair's first
  * head is stored.  Non-finite values give NaN blocks (kv.rs:451-455). */
 int fo_kv_append(fo_kv_cache *cache, const float *k, const float *v, int64_t rows, int mem);
+/* fo_kv_append on n caches in one launch, as the per-page appends of
+ * Model::decode_batch_next (src/model/mod.rs:760-852): cache i takes `rows`
+ * expanded rows from the DEVICE pointers k[i], v[i].  The caches share a
+ * context, format and heads and are distinct; every capacity is checked
+ * before anything is written (FO_ERR_CAPACITY leaves all caches as they
+ * were).  The records equal those of n separate fo_kv_append calls. */
+int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const *k, const float *const *v,
+                       int64_t rows);
 /* SplitPrefix::truncate_tail (kv.rs:846-849). */
 int fo_kv_truncate_tail(fo_kv_cache *cache, int64_t tail_len);
 int64_t fo_kv_tail_len(const fo_kv_cache *cache);

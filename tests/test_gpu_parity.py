@@ -195,6 +195,53 @@ def test_seal_and_append_are_bit_exact(ctx, fmt, p, generated):
                               ref.tail_scales.reshape(8, -1, 4)[:, :generated])
 
 
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_append_batch_equals_per_page_appends(ctx, fmt):
+    """fo_kv_append_batch (the per-page appends of Model::decode_batch_next,
+    src/model/mod.rs:760-852, in one launch) writes the same tail records,
+    bit for bit, as one fo_kv_append per cache; capacity and duplicate
+    refusals leave every cache as it was."""
+    prefixes = [7, 128, 129, 300, 1000]
+    cap = 12
+    singles, batched = [], []
+    for i, p in enumerate(prefixes):
+        k, v, _ = G.kv_fixture(p, 11 + i)
+        singles.append(F.SplitPrefix.from_compact(dev(k), dev(v), p, p + cap, fmt=fmt))
+        batched.append(F.SplitPrefix.from_compact(dev(k), dev(v), p, p + cap, fmt=fmt))
+    rng = np.random.default_rng(5)
+    for step, rows in enumerate([1, 1, 3]):
+        ks, vs = [], []
+        for i in range(len(prefixes)):
+            x = rng.standard_normal((2, rows, 8, 1, 64)).astype(np.float32)
+            x = np.repeat(x, 2, axis=3).reshape(2, -1)  # expanded rows: pairs share the group's row
+            if step == 1 and i == 2:
+                x[1, 5] = np.nan  # a non-finite value gives a NaN block, batched or not
+            ks.append(dev(x[0]))
+            vs.append(dev(x[1]))
+            singles[i].append(ks[i], vs[i])
+        F.append_batch(batched, ks, vs, rows)
+    torch.cuda.synchronize()
+    bits = lambda x: x.view(np.uint32) if x.dtype == np.float32 else x  # noqa: E731
+    for a, b in zip(singles, batched):
+        assert a.tail_len == b.tail_len == 5
+        ra, rb = device_records(a, fmt, 8), device_records(b, fmt, 8)
+        ta = np.ascontiguousarray(ra["tail"].reshape(8, -1, 128)[:, :5])
+        tb = np.ascontiguousarray(rb["tail"].reshape(8, -1, 128)[:, :5])
+        assert np.array_equal(bits(ta), bits(tb))
+        if fmt in (F.KV_Q16, F.KV_Q8):
+            assert np.array_equal(ra["tail_scales"].reshape(8, -1, 4)[:, :5], rb["tail_scales"].reshape(8, -1, 4)[:, :5])
+    # one cache without room: nothing is written anywhere
+    x = dev(np.zeros(8 * 16 * 64, np.float32))
+    with pytest.raises(F.CapacityError):
+        F.append_batch(batched, [x] * 5, [x] * 5, 8)
+    assert [b.tail_len for b in batched] == [5] * 5
+    with pytest.raises(F.FoError):
+        F.append_batch([batched[0], batched[0]], [x] * 2, [x] * 2, 1)
+    assert batched[0].tail_len == 5
+    for c in singles + batched:
+        c.close()
+
+
 def test_seal_errors(ctx):
     """kv.rs:248-295 and src/quant/kv/tests.rs:355-367"""
     k = np.zeros(16 * 64, np.float32)
