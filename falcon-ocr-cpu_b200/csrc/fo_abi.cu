@@ -799,6 +799,40 @@ int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const
     return FO_OK;
 }
 
+static bool aligned8(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+
+int fo_qkv_prefix_rows(fo_ctx *ctx, const float *qkv, const float *rope, int64_t rows, int64_t n_heads,
+                       int64_t n_kv_heads, float *q, float *k, float *v, uint16_t *k_bf16, uint16_t *v_bf16) {
+    if (!ctx) return fail(FO_ERR_INVALID, "fo_qkv_prefix_rows: null context");
+    if (rows < 0 || !(n_kv_heads >= 1 && n_heads >= n_kv_heads && n_heads % n_kv_heads == 0 && n_heads <= 64))
+        return fail(FO_ERR_INVALID, "fo_qkv_prefix_rows: bad shape");
+    if (rows == 0) return FO_OK;
+    if (!qkv || !rope || !q || !k || !v) return fail(FO_ERR_INVALID, "fo_qkv_prefix_rows: null pointer");
+    if (!aligned8(qkv) || !aligned8(rope) || !aligned8(q) || !aligned8(k) || !aligned8(v) ||
+        (reinterpret_cast<uintptr_t>(k_bf16) & 3) || (reinterpret_cast<uintptr_t>(v_bf16) & 3))
+        return fail(FO_ERR_INVALID, "fo_qkv_prefix_rows: buffers must be 8-byte aligned (BF16 copies 4-byte)");
+    DeviceGuard guard(ctx->device);
+    cudaError_t e = fo_launch_qkv_rows(qkv, rope, rows, (int)n_heads, (int)n_kv_heads, q, k, v, k_bf16, v_bf16,
+                                       ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "fused QKV rows launch");
+    return FO_OK;
+}
+
+int fo_kv_append_qkv(fo_kv_cache *c, const float *qkv, const float *rope, int64_t rows, float *q) {
+    if (!c || rows < 0) return fail(FO_ERR_INVALID, "fo_kv_append_qkv: bad argument");
+    if (rows == 0) return FO_OK;
+    if (!qkv || !rope || !q) return fail(FO_ERR_INVALID, "fo_kv_append_qkv: null pointer");
+    if (!aligned8(qkv) || !aligned8(rope) || !aligned8(q))
+        return fail(FO_ERR_INVALID, "fo_kv_append_qkv: buffers must be 8-byte aligned");
+    if (c->tail_len + rows > c->tail_capacity) return fail(FO_ERR_CAPACITY, "split tail capacity");
+    DeviceGuard guard(c->ctx->device);
+    cudaError_t e = fo_launch_qkv_append(qkv, rope, rows, (int)c->heads, (int)c->groups, q, c->format, c->tail_codes,
+                                         c->tail_scales, c->tail_stride, c->tail_len, c->ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "fused QKV append launch");
+    c->tail_len += rows;
+    return FO_OK;
+}
+
 int fo_kv_truncate_tail(fo_kv_cache *c, int64_t tail_len) {
     if (!c) return fail(FO_ERR_INVALID, "null cache");
     if (tail_len < 0 || tail_len > c->tail_len) return fail(FO_ERR_INVALID, "cannot grow the tail by truncation");

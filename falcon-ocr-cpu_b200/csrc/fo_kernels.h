@@ -28,6 +28,17 @@ cudaError_t fo_launch_convert_bf16(const float *src, uint16_t *dst, int64_t n, c
 cudaError_t fo_launch_seal(const float *k, const float *v, int64_t prefix_len, int64_t heads, int64_t groups,
                            int format, void *codes, uint16_t *scales, int64_t stride, unsigned *flags,
                            cudaStream_t stream);
+// The fused QKV rows (kv_cache.cu): split, per-head RMS norm and RoPE of
+// projection rows qkv [rows][heads*64 + 2*groups*64] with rope
+// [rows][heads][32][2]; q, k [rows][heads][64], v [rows][groups][64] and
+// optional BF16 copies of k and v.
+cudaError_t fo_launch_qkv_rows(const float *qkv, const float *rope, int64_t rows, int heads, int groups, float *q,
+                               float *k, float *v, uint16_t *k_bf16, uint16_t *v_bf16, cudaStream_t stream);
+// The same for decode rows: q, and the new keys and values appended as tail
+// records first.. of a split cache.
+cudaError_t fo_launch_qkv_append(const float *qkv, const float *rope, int64_t rows, int heads, int groups, float *q,
+                                 int format, void *tail_codes, uint16_t *tail_scales, int64_t tail_stride,
+                                 int64_t first, cudaStream_t stream);
 // One cache's share of a batched append: its expanded rows and tail.
 struct fo_append_page {
     const float *k, *v;  // [rows][H][64]

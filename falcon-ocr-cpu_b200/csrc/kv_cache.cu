@@ -136,6 +136,100 @@ __global__ void append_batch_kernel(const fo_append_page *__restrict__ pages, in
                   pg.tail_stride, pg.first, threadIdx.x & 31);
 }
 
+// ------------------------------------------------------- fused QKV rows
+// One head of the fused QKV rows (src/model/fused.rs:96-116 and :184-223):
+// lane l holds dimensions 2l and 2l + 1 (the rotation's pair l).  The sum of
+// squares follows sum_squares_pairwise's tree (src/kernels/mod.rs:535-555):
+// two 32-value leaves (lanes 0-15 and 16-31), in each partial[i] +=
+// partial[i + w] for w = 16, 8, 4, 2, 1 (lanes l and l + w/2 here), then
+// leaf 0 + leaf 1; rms_scale's 1 / sqrt(sum / 64 + f32::EPSILON) with IEEE
+// square root and reciprocal (mod.rs:531-533); then x * scale and the
+// unfused rotation a*cos - b*sin, a*sin + b*cos.
+__device__ __forceinline__ float2 norm_rope_pair(float2 x, float2 cs) {
+    float px = __fmul_rn(x.x, x.x), py = __fmul_rn(x.y, x.y);
+#pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+        const float ox = __shfl_down_sync(0xffffffffu, px, off), oy = __shfl_down_sync(0xffffffffu, py, off);
+        px = __fadd_rn(px, ox);
+        py = __fadd_rn(py, oy);
+    }
+    const float leaf = __fadd_rn(px, py);  // in lanes 0 and 16
+    const float sum = __fadd_rn(__shfl_sync(0xffffffffu, leaf, 0), __shfl_sync(0xffffffffu, leaf, 16));
+    const float scale = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 64.0f), 1.1920928955078125e-7f)));
+    const float a = __fmul_rn(x.x, scale), b = __fmul_rn(x.y, scale);
+    return make_float2(__fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y)),
+                       __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x)));
+}
+
+// Prefill rows (fused_prefix_rows, fused.rs:17-93): one warp per (row, head)
+// writes query head h and key head h (from KV head h / (heads / groups)),
+// rotated by rope[row][h]; warps of heads h < groups also copy value head h.
+// BF16 copies (round to nearest even) when kb / vb are given.
+__global__ void qkv_rows_kernel(const float *__restrict__ qkv, const float *__restrict__ rope, int64_t rows,
+                                int heads, int groups, float *__restrict__ q, float *__restrict__ k,
+                                float *__restrict__ v, uint32_t *__restrict__ kb, uint32_t *__restrict__ vb) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= rows * heads) return;
+    const int64_t r = w / heads;
+    const int h = (int)(w - r * heads);
+    const int64_t qdim = (int64_t)heads * FO_HD, kdim = (int64_t)groups * FO_HD;
+    const float *src = qkv + r * (qdim + 2 * kdim);
+    const float2 cs = reinterpret_cast<const float2 *>(rope + (r * heads + h) * FO_HD)[lane];
+    const float2 yq = norm_rope_pair(reinterpret_cast<const float2 *>(src + h * FO_HD)[lane], cs);
+    const float2 yk =
+        norm_rope_pair(reinterpret_cast<const float2 *>(src + qdim + (h / (heads / groups)) * FO_HD)[lane], cs);
+    const int64_t o = (r * heads + h) * FO_HD;
+    reinterpret_cast<float2 *>(q + o)[lane] = yq;
+    reinterpret_cast<float2 *>(k + o)[lane] = yk;
+    if (kb) kb[o / 2 + lane] = (uint32_t)bf16_rne(yk.x) | ((uint32_t)bf16_rne(yk.y) << 16);
+    if (h < groups) {
+        const float2 xv = reinterpret_cast<const float2 *>(src + qdim + kdim + h * FO_HD)[lane];
+        const int64_t ov = (r * groups + h) * FO_HD;
+        reinterpret_cast<float2 *>(v + ov)[lane] = xv;
+        if (vb) vb[ov / 2 + lane] = (uint32_t)bf16_rne(xv.x) | ((uint32_t)bf16_rne(xv.y) << 16);
+    }
+}
+
+// Decode rows (split_norm_rope, rope.rs:15-85, then SplitPrefix::append,
+// kv.rs:430-449): warps of the first rows * heads write the rotated queries;
+// then one warp per (row, group) builds the pair's first key head (its own
+// rotation) and the group's value and encodes tail record first + row, as
+// append_record does with expanded rows.
+__global__ void qkv_append_kernel(const float *__restrict__ qkv, const float *__restrict__ rope, int64_t rows,
+                                  int heads, int groups, float *__restrict__ q, int format, void *tail_codes,
+                                  uint16_t *tail_scales, int64_t tail_stride, int64_t first) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t qdim = (int64_t)heads * FO_HD, kdim = (int64_t)groups * FO_HD;
+    if (w < rows * heads) {
+        const int64_t r = w / heads;
+        const int h = (int)(w - r * heads);
+        const float *src = qkv + r * (qdim + 2 * kdim);
+        const float2 cs = reinterpret_cast<const float2 *>(rope + (r * heads + h) * FO_HD)[lane];
+        reinterpret_cast<float2 *>(q + (r * heads + h) * FO_HD)[lane] =
+            norm_rope_pair(reinterpret_cast<const float2 *>(src + h * FO_HD)[lane], cs);
+        return;
+    }
+    const int64_t w2 = w - rows * heads;
+    if (w2 >= rows * groups) return;
+    const int64_t r = w2 / groups;
+    const int g = (int)(w2 - r * groups), h = g * (heads / groups);
+    const float *src = qkv + r * (qdim + 2 * kdim);
+    const float2 cs = reinterpret_cast<const float2 *>(rope + (r * heads + h) * FO_HD)[lane];
+    const float2 yk = norm_rope_pair(reinterpret_cast<const float2 *>(src + qdim + g * FO_HD)[lane], cs);
+    // to the record's layout: lane l encodes dimensions l and 32 + l
+    const int sl = lane >> 1;
+    const float a0 = __shfl_sync(0xffffffffu, yk.x, sl), a1 = __shfl_sync(0xffffffffu, yk.y, sl);
+    const float b0 = __shfl_sync(0xffffffffu, yk.x, 16 + sl), b1 = __shfl_sync(0xffffffffu, yk.y, 16 + sl);
+    const float *vr = src + qdim + kdim + g * FO_HD;
+    const int64_t base = ((int64_t)g * tail_stride + first + r) * FO_TAIL_RECORD;
+    encode_block((lane & 1) ? a1 : a0, format, tail_codes, tail_scales, base, true, nullptr);
+    encode_block((lane & 1) ? b1 : b0, format, tail_codes, tail_scales, base + 32, true, nullptr);
+    encode_block(vr[lane], format, tail_codes, tail_scales, base + 64, true, nullptr);
+    encode_block(vr[32 + lane], format, tail_codes, tail_scales, base + 96, true, nullptr);
+}
+
 // FP32 -> BF16, eight values per thread (16-byte stores).
 __global__ void convert_bf16_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, int64_t n) {
     const int64_t i8 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -186,6 +280,31 @@ extern "C" cudaError_t fo_launch_append_batch(const fo_append_page *pages, int64
     const int threads = 256;
     const int64_t blocks = (warps * 32 + threads - 1) / threads;
     fo::append_batch_kernel<<<(unsigned)blocks, threads, 0, stream>>>(pages, n, rows, heads, groups, format);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t fo_launch_qkv_rows(const float *qkv, const float *rope, int64_t rows, int heads, int groups,
+                                          float *q, float *k, float *v, uint16_t *k_bf16, uint16_t *v_bf16,
+                                          cudaStream_t stream) {
+    const int64_t warps = rows * heads;
+    if (warps == 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    fo::qkv_rows_kernel<<<(unsigned)blocks, threads, 0, stream>>>(qkv, rope, rows, heads, groups, q, k, v,
+                                                                  reinterpret_cast<uint32_t *>(k_bf16),
+                                                                  reinterpret_cast<uint32_t *>(v_bf16));
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t fo_launch_qkv_append(const float *qkv, const float *rope, int64_t rows, int heads, int groups,
+                                            float *q, int format, void *tail_codes, uint16_t *tail_scales,
+                                            int64_t tail_stride, int64_t first, cudaStream_t stream) {
+    const int64_t warps = rows * (heads + groups);
+    if (warps == 0) return cudaSuccess;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    fo::qkv_append_kernel<<<(unsigned)blocks, threads, 0, stream>>>(qkv, rope, rows, heads, groups, q, format,
+                                                                    tail_codes, tail_scales, tail_stride, first);
     return cudaGetLastError();
 }
 

@@ -92,7 +92,8 @@ EXPORTS = [
     "fo_attention", "fo_attention_prefill_bf16", "fo_convert_bf16", "fo_kv_seal", "fo_kv_destroy",
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
-    "fo_kv_attention_decode_batch", "fo_kv_append_batch", "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
+    "fo_kv_attention_decode_batch", "fo_kv_append_batch", "fo_qkv_prefix_rows", "fo_kv_append_qkv",
+    "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
     "fo_i8_decode_batch",
@@ -135,6 +136,8 @@ def lib() -> ctypes.CDLL:
         "fo_kv_attention_decode_rows": (I, [P, P, I64, P, P, I]),
         "fo_kv_attention_decode_batch": (I, [PP, I64, PP, PP, PP]),
         "fo_kv_append_batch": (I, [PP, I64, PP, PP, I64]),
+        "fo_qkv_prefix_rows": (I, [P, P, P, I64, I64, I64, P, P, P, P, P]),
+        "fo_kv_append_qkv": (I, [P, P, P, I64, P]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
         "fo_decode_static_scratch_status": (I, [P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
@@ -394,6 +397,22 @@ def append_batch(caches: Sequence[SplitPrefix], ks, vs, rows: int):
     arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
     check(lib().fo_kv_append_batch(arr([c.handle.value for c in caches]), n, arr([k.data_ptr() for k in ks]),
                                    arr([v.data_ptr() for v in vs]), rows))
+
+
+def qkv_prefix_rows(qkv, rope, rows: int, q, k, v, k_bf16=None, v_bf16=None, heads: int = 16, kv_heads: int = 8,
+                    ctx=None):
+    """fo_qkv_prefix_rows on device tensors: the fused split + per-head RMS
+    norm + RoPE of projection rows into q, k (and their BF16 copies)."""
+    ctx = ctx or default_context()
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    check(lib().fo_qkv_prefix_rows(ctx.handle, qkv.data_ptr(), rope.data_ptr(), rows, heads, kv_heads, q.data_ptr(),
+                                   k.data_ptr(), v.data_ptr(), ptr(k_bf16), ptr(v_bf16)))
+
+
+def append_qkv(cache: SplitPrefix, qkv, rope, rows: int, q):
+    """fo_kv_append_qkv on device tensors: decode rows' queries into q, their
+    keys and values appended to the cache's tail."""
+    check(lib().fo_kv_append_qkv(cache.handle, qkv.data_ptr(), rope.data_ptr(), rows, q.data_ptr()))
 
 
 class Int8Cache:

@@ -21,6 +21,10 @@
  *                                  calls LayerCache::attention per page (src/model/mod.rs:827-852)
  *   fo_kv_append_batch           one append per page, as Model::decode_batch_next calls
  *                                  SplitPrefix::append per page (src/model/mod.rs:760-852)
+ *   fo_qkv_prefix_rows           model::fused::fused_prefix_rows (split, per-head RMS norm,
+ *                                  RoPE, compact append, BF16 copies) src/model/fused.rs:17-116
+ *   fo_kv_append_qkv             rope::split_norm_rope then SplitPrefix::append for decode
+ *                                  rows, src/model/rope.rs:15-85, src/quant/kv.rs:430-449
  *
  * Entry points with no single reference counterpart (each says why below):
  *   fo_attention_prefill_bf16_rows[_split]  query-row bands of the BF16 prefill
@@ -215,6 +219,23 @@ int fo_kv_append(fo_kv_cache *cache, const float *k, const float *v, int64_t row
  * were).  The records equal those of n separate fo_kv_append calls. */
 int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const *k, const float *const *v,
                        int64_t rows);
+/* The fused QKV rows of a prefill (fused_prefix_rows, src/model/fused.rs:17-116;
+ * the same arithmetic as split_norm_rope, src/model/rope.rs:15-85), on DEVICE
+ * pointers: qkv [rows][n_heads*64 + 2*n_kv_heads*64] projection rows, rope
+ * [rows][n_heads][32] {cos, sin} pairs.  Query head h and key head h (KV head
+ * h / (n_heads / n_kv_heads)) are RMS-normalized (eps f32::EPSILON, the
+ * reference's pairwise sum of squares) and rotated by rope[row][h]; q and k
+ * get [rows][n_heads][64], v [rows][n_kv_heads][64] (a copy).  k_bf16 and
+ * v_bf16 (nullable) get the BF16 copies (round to nearest even) in the same
+ * layouts, the operands of fo_attention_prefill_bf16.  Bit for bit the
+ * reference's row.  Buffers 8-byte aligned (BF16 copies 4-byte). */
+int fo_qkv_prefix_rows(fo_ctx *ctx, const float *qkv, const float *rope, int64_t rows, int64_t n_heads,
+                       int64_t n_kv_heads, float *q, float *k, float *v, uint16_t *k_bf16, uint16_t *v_bf16);
+/* Decode rows of the same pass: q [rows][n_heads][64] as above, and each
+ * row's keys and values appended to the cache's tail (the pair's first key
+ * head, with its own rotation, and the group's value: what fo_kv_append
+ * stores from split_norm_rope's expanded rows).  DEVICE pointers. */
+int fo_kv_append_qkv(fo_kv_cache *cache, const float *qkv, const float *rope, int64_t rows, float *q);
 /* SplitPrefix::truncate_tail (kv.rs:846-849). */
 int fo_kv_truncate_tail(fo_kv_cache *cache, int64_t tail_len);
 int64_t fo_kv_tail_len(const fo_kv_cache *cache);

@@ -21,6 +21,7 @@
  */
 #include "fo_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -929,4 +930,44 @@ void fo_or_kv_decode_rows(const void *codes, const uint16_t *scales, const void 
     int64_t width = heads * 64;
     for (int64_t r = 0; r < rows; r++)
         decode_one(&st, last + 1 + r - rows, heads, groups, q + r * width, sinks, chunks, fast_exp, out + r * width);
+}
+
+/* ------------------------------------------------------- fused QKV rows */
+/* sum_squares_pairwise on one 32-value leaf (src/kernels/mod.rs:535-555):
+ * squares, then partial[i] += partial[i + w] for w = 16, 8, 4, 2, 1. */
+static float sum_squares_leaf32(const float *x) {
+    float p[32];
+    for (int i = 0; i < 32; i++) p[i] = x[i] * x[i];
+    for (int w = 16; w >= 1; w >>= 1)
+        for (int i = 0; i < w; i++) p[i] = p[i] + p[i + w];
+    return p[0];
+}
+
+/* rms_norm_row (width 64: the tree splits at 32, mod.rs:537-541) and the
+ * rotation of one head (fused.rs:104-113). */
+static void norm_rope_head(const float *x, const float *rope, float *out) {
+    const float sum = sum_squares_leaf32(x) + sum_squares_leaf32(x + 32);
+    const float scale = 1.0f / sqrtf(sum / 64.0f + FLT_EPSILON);
+    float y[64];
+    for (int d = 0; d < 64; d++) y[d] = x[d] * scale;
+    for (int p = 0; p < 32; p++) {
+        const float c = rope[2 * p], s = rope[2 * p + 1], a = y[2 * p], b = y[2 * p + 1];
+        out[2 * p] = a * c - b * s;
+        out[2 * p + 1] = a * s + b * c;
+    }
+}
+
+void fo_or_qkv_rows(const float *qkv, const float *rope, int64_t rows, int64_t heads, int64_t groups, float *q,
+                    float *k, float *v) {
+    const int64_t qdim = heads * 64, kdim = groups * 64, width = qdim + 2 * kdim, group = heads / groups;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        const float *src = qkv + r * width;
+        for (int64_t h = 0; h < heads; h++) {
+            const float *f = rope + (r * heads + h) * 64;
+            norm_rope_head(src + h * 64, f, q + (r * heads + h) * 64);
+            norm_rope_head(src + qdim + (h / group) * 64, f, k + (r * heads + h) * 64);
+        }
+        memcpy(v + r * kdim, src + qdim + kdim, (size_t)kdim * sizeof(float));
+    }
 }

@@ -95,6 +95,17 @@ void fo_or_kv_decode_rows(const void *codes, const uint16_t *scales, const void 
                           int64_t tail_len, int64_t heads, int64_t groups, const float *q, int64_t rows,
                           const float *sinks, int64_t chunks, int fast_exp, float *out);
 
+/* The fused QKV rows (src/model/fused.rs:96-116 `fused_row`, the same
+ * arithmetic as src/model/rope.rs:15-85 `split_norm_rope`): per row, query
+ * head h and key head h (KV head h / (heads / groups) of the projection) get
+ * rms_norm_row (width 64, eps f32::EPSILON, no weight; the pairwise sum of
+ * squares of src/kernels/mod.rs:509-555) and the pairwise rotation by
+ * rope[row][h][pair] = {cos, sin} (a*cos - b*sin, a*sin + b*cos, unfused);
+ * v is copied.  qkv [rows][heads*64 + 2*groups*64], rope [rows][heads][32][2];
+ * q, k [rows][heads][64], v [rows][groups][64]. */
+void fo_or_qkv_rows(const float *qkv, const float *rope, int64_t rows, int64_t heads, int64_t groups, float *q,
+                    float *k, float *v);
+
 /* OpenMP threads used by the parallel oracle loops (0 = library default). */
 void fo_or_set_threads(int threads);
 int fo_or_max_threads(void);

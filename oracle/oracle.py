@@ -76,6 +76,7 @@ def lib() -> ctypes.CDLL:
         "fo_or_kv_push": (None, [P, P, I64, I, I64, I64, P, P]),
         "fo_or_kv_value": (F, [P, P, I, I64, I64, I64]),
         "fo_or_kv_decode_rows": (None, [P, P, P, P, I] + [I64] * 5 + [P, I64, P, I64, I, P]),
+        "fo_or_qkv_rows": (None, [P, P, I64, I64, I64, P, P, P]),
         "fo_or_set_threads": (None, [I]),
         "fo_or_max_threads": (I, []),
     }
@@ -195,6 +196,18 @@ def prefill_bf16(q, k, v, n_heads, n_kv_heads, image, sinks, softmax_static=True
 
 
 # ---------------------------------------------------------- split cache
+def qkv_rows(qkv, rope, rows, heads=16, groups=8):
+    """fo_or_qkv_rows: the fused split + per-head RMS norm + RoPE of the
+    projection rows (src/model/fused.rs:96-116).  Returns q, k [rows][heads][64]
+    and v [rows][groups][64] as flat float32 arrays."""
+    qkv, rope = _f32(qkv), _f32(rope)
+    q = np.zeros(rows * heads * 64, np.float32)
+    k = np.zeros(rows * heads * 64, np.float32)
+    v = np.zeros(rows * groups * 64, np.float32)
+    lib().fo_or_qkv_rows(_p(qkv), _p(rope), rows, heads, groups, _p(q), _p(k), _p(v))
+    return q, k, v
+
+
 class SplitCache:
     """The reference's SplitPrefix (src/quant/kv.rs:155-174) over numpy arrays:
     prefix records [G][P][160], scales [G][P][5]; tail [G][cap][128], [G][cap][4]."""

@@ -131,6 +131,20 @@ def test_null_handles_are_rejected():
     assert L.fo_ctx_create(-1, None, ctypes.byref(h)) != F.OK
 
 
+def test_batched_and_fused_entries_reject_bad_arguments():
+    """fo_kv_append_batch, fo_qkv_prefix_rows and fo_kv_append_qkv refuse
+    null handles and bad shapes before touching a device."""
+    L = F.lib()
+    arr = (ctypes.c_void_p * 1)(None)
+    assert L.fo_kv_append_batch(None, 1, arr, arr, 1) == F.ERR_INVALID
+    assert L.fo_kv_append_batch(arr, 1, arr, arr, 1) == F.ERR_INVALID  # a null cache
+    assert L.fo_kv_append_batch(arr, -1, arr, arr, 1) == F.ERR_INVALID
+    assert L.fo_kv_append_batch(arr, 0, arr, arr, 1) == F.OK  # nothing to do
+    assert L.fo_qkv_prefix_rows(None, None, None, 4, 16, 8, None, None, None, None, None) == F.ERR_INVALID
+    assert L.fo_kv_append_qkv(None, None, None, 1, None) == F.ERR_INVALID
+    assert L.fo_kv_append_qkv(None, None, None, -1, None) == F.ERR_INVALID
+
+
 def test_row_band_entries_reject_a_null_context():
     """The row-band prefill entries (whole and split) refuse a null context
     before touching a device, whatever the number of key ranges."""

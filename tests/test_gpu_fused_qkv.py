@@ -1,0 +1,133 @@
+"""GPU parity of the fused QKV rows (fo_qkv_prefix_rows, fo_kv_append_qkv)
+against the oracle's restatement of src/model/fused.rs:96-116 and
+src/model/rope.rs:15-85: bit for bit, through the C ABI."""
+
+import numpy as np
+import pytest
+
+import fo_cuda as F
+import oracle as O
+from test_fused_qkv_cpu import fixture
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+HEADS, GROUPS = 16, 8
+WIDTH = HEADS * 64 + 2 * GROUPS * 64
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    c = F.Context(0)
+    yield c
+    c.close()
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def bits(x):
+    return np.asarray(x).view(np.uint32)
+
+
+def same(a, b):
+    """Bit for bit where not NaN, NaN where NaN (payloads differ by device)."""
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return np.array_equal(na, nb) and np.array_equal(bits(a[~na]), bits(b[~nb]))
+
+
+def bf16_rne(x):
+    """Round to nearest even (half::bf16::from_f32), NaN kept quiet."""
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+
+
+@pytest.mark.parametrize("rows", [1, 23, 6544])
+def test_prefix_rows_are_the_oracle_bit_for_bit(ctx, rows):
+    qkv, rope = fixture(rows, seed=100 + rows)
+    q_ref, k_ref, v_ref = O.qkv_rows(qkv, rope, rows)
+    q = torch.empty(rows * HEADS * 64, device="cuda")
+    k = torch.empty_like(q)
+    v = torch.empty(rows * GROUPS * 64, device="cuda")
+    kb = torch.empty(rows * HEADS * 64, dtype=torch.bfloat16, device="cuda")
+    vb = torch.empty(rows * GROUPS * 64, dtype=torch.bfloat16, device="cuda")
+    F.qkv_prefix_rows(dev(qkv), dev(rope), rows, q, k, v, kb, vb, ctx=ctx)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(q.cpu().numpy()), bits(q_ref))
+    assert np.array_equal(bits(k.cpu().numpy()), bits(k_ref))
+    assert np.array_equal(bits(v.cpu().numpy()), bits(v_ref))
+    assert np.array_equal(kb.view(torch.int16).cpu().numpy().view(np.uint16), bf16_rne(k_ref))
+    assert np.array_equal(vb.view(torch.int16).cpu().numpy().view(np.uint16), bf16_rne(v_ref))
+
+
+FORMATS = [F.KV_F32, F.KV_Q16, F.KV_Q8, F.KV_BF16]
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_decode_rows_append_what_the_oracle_pushes(ctx, fmt):
+    """fo_kv_append_qkv: the queries equal the oracle's, and the tail records
+    equal the oracle's push of the pair's first key head and the group's
+    value (what SplitPrefix::append keeps of split_norm_rope's rows)."""
+    import generators as G
+    p, gen = 130, 5
+    k0, v0, _ = G.kv_fixture(p, 9)
+    ref = O.SplitCache(k0, v0, p, p + gen + 1, fmt=fmt)
+    gpu = F.SplitPrefix.from_compact(dev(k0), dev(v0), p, p + gen + 1, fmt=fmt, ctx=ctx)
+    qkv, rope = fixture(gen, seed=31)
+    qkv[2 * WIDTH + 5] = np.nan  # a non-finite query value stays in its own row
+    q_ref, k_ref, v_ref = O.qkv_rows(qkv, rope, gen)
+    q = torch.empty(gen * HEADS * 64, device="cuda")
+    F.append_qkv(gpu, dev(qkv[:2 * WIDTH]), dev(rope[:2 * HEADS * 64]), 2, q[:2 * HEADS * 64])
+    F.append_qkv(gpu, dev(qkv[2 * WIDTH:]), dev(rope[2 * HEADS * 64:]), gen - 2, q[2 * HEADS * 64:])
+    torch.cuda.synchronize()
+    assert gpu.tail_len == gen
+    assert same(q.cpu().numpy(), q_ref)
+    assert np.isnan(q_ref.reshape(gen, HEADS, 64)[2, 0]).all() and np.isfinite(q_ref.reshape(gen, HEADS, 64)[3]).all()
+    kr = k_ref.reshape(gen, HEADS, 64)[:, 0::2]  # the pair's first head
+    vr = v_ref.reshape(gen, GROUPS, 64)
+    for t in range(gen):
+        ref.push(np.ascontiguousarray(kr[t]).reshape(-1), np.ascontiguousarray(vr[t]).reshape(-1))
+    (codes, scales, tcodes, tscales), ps, ts = gpu.records()
+    dt = {F.KV_F32: np.float32, F.KV_Q16: np.int16, F.KV_Q8: np.int8, F.KV_BF16: np.uint16}[fmt]
+    tail = F.device_to_host(tcodes, GROUPS * ts * 128, dt).reshape(GROUPS, ts, 128)[:, :gen]
+    want = ref.tail_codes.reshape(GROUPS, -1, 128)[:, :gen]
+    b = (lambda x: x.view(np.uint32)) if dt == np.float32 else (lambda x: x)
+    assert np.array_equal(b(np.ascontiguousarray(tail)), b(np.ascontiguousarray(want)))
+    if fmt in (F.KV_Q16, F.KV_Q8):
+        got = F.device_to_host(tscales, GROUPS * ts * 4, np.uint16).reshape(GROUPS, ts, 4)[:, :gen]
+        assert np.array_equal(got, ref.tail_scales.reshape(GROUPS, -1, 4)[:, :gen])
+    with pytest.raises(F.CapacityError):
+        F.append_qkv(gpu, dev(qkv[:2 * WIDTH]), dev(rope[:2 * HEADS * 64]), 2, q[:2 * HEADS * 64])
+    assert gpu.tail_len == gen
+    gpu.close()
+
+
+def test_fused_prefill_operands_give_the_same_attention(ctx):
+    """A C2-shaped page whose Q, K, V and BF16 copies come from
+    fo_qkv_prefix_rows attends exactly as one whose operands were built from
+    the oracle's rows and converted separately."""
+    rows = 6544
+    qkv, rope = fixture(rows, seed=3)
+    q_ref, k_ref, v_ref = O.qkv_rows(qkv, rope, rows)
+    q = torch.empty(rows * HEADS * 64, device="cuda")
+    k, v = torch.empty_like(q), torch.empty(rows * GROUPS * 64, device="cuda")
+    kb = torch.empty(rows * HEADS * 64, dtype=torch.bfloat16, device="cuda")
+    vb = torch.empty(rows * GROUPS * 64, dtype=torch.bfloat16, device="cuda")
+    F.qkv_prefix_rows(dev(qkv), dev(rope), rows, q, k, v, kb, vb, ctx=ctx)
+    sinks = dev(np.linspace(-1, 1, HEADS).astype(np.float32))
+    geo = (0, 0, 4096)
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
+    out_a = torch.empty_like(q)
+    F.attention_prefill_bf16(q, k, v, geo, sinks, out_a, HEADS, GROUPS, keys_bf16=kb, values_bf16=vb, options=opts,
+                             ctx=ctx)
+    qr, kr, vr = dev(q_ref), dev(k_ref), dev(v_ref)
+    out_b = torch.empty_like(q)
+    F.attention_prefill_bf16(qr, kr, vr, geo, sinks, out_b, HEADS, GROUPS, keys_bf16=kr.to(torch.bfloat16),
+                             values_bf16=vr.to(torch.bfloat16), options=opts, ctx=ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(out_a.view(torch.int32), out_b.view(torch.int32))
