@@ -71,7 +71,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, len(sources))) as ex:
         objs = list(ex.map(lambda s: compile_one(s, force, verbose), sources))
     if force or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

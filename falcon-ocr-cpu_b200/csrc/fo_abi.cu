@@ -20,8 +20,9 @@
 #define FO_MAX_ROWS_ABI 8     // verification rows (src/quant/kv.rs:68)
 
 extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
-                                              const float *sinks, float *out, int64_t total, int64_t n_heads,
-                                              int64_t n_kv_heads, int64_t image_start, int64_t image_end,
+                                              const float *sinks, void *out, int out_bf16, int64_t total,
+                                              int64_t n_heads, int64_t n_kv_heads, int64_t image_start,
+                                              int64_t image_end,
                                               int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
                                               unsigned *err, int n_split, float *part_o, float *part_ml,
                                               cudaStream_t stream);
@@ -151,6 +152,9 @@ struct fo_ctx {
     // Host-buffer prefill pipeline: copy streams and per-band events.
     cudaStream_t h2d = nullptr, d2h = nullptr;
     std::vector<cudaEvent_t> band_ev;
+    // Head-sharded prefill: the gathers' stream and its events.
+    cudaStream_t comm = nullptr;
+    std::vector<cudaEvent_t> comm_ev;
 };
 
 struct fo_kv_cache {
@@ -357,7 +361,7 @@ int prefill_bf16_host_pipelined(fo_ctx *ctx, const float *q, const fo_compact_kv
         if (e == cudaSuccess)
             e = fo_launch_convert_bf16(dv + r0 * G * 64, vb + r0 * G * 64, (r1 - r0) * G * 64, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "convert kernel launch");
-        e = fo_launch_prefill_bf16(dq, kb, vb, ds, dout, T, H, G, geometry.image_start, geometry.image_end, r0, r1,
+        e = fo_launch_prefill_bf16(dq, kb, vb, ds, dout, 0, T, H, G, geometry.image_start, geometry.image_end, r0, r1,
                                    options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err, 1,
                                    nullptr, nullptr, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
@@ -441,7 +445,10 @@ int fo_ctx_destroy(fo_ctx *ctx) {
     if (ctx->ev1) cudaEventDestroy(ctx->ev1);
     if (ctx->h2d) cudaStreamSynchronize(ctx->h2d);
     if (ctx->d2h) cudaStreamSynchronize(ctx->d2h);
+    if (ctx->comm) cudaStreamSynchronize(ctx->comm);
     for (cudaEvent_t e : ctx->band_ev) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->comm_ev) cudaEventDestroy(e);
+    if (ctx->comm) cudaStreamDestroy(ctx->comm);
     if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
     if (ctx->d2h) cudaStreamDestroy(ctx->d2h);
     if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -553,7 +560,7 @@ int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *
     }
     if (!aligned16(kb) || !aligned16(vb) || !aligned16(s.q) || !aligned16(s.out))
         return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
-    e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, T, H, G, geometry.image_start, geometry.image_end, 0, T,
+    e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, 0, T, H, G, geometry.image_start, geometry.image_end, 0, T,
                                options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err, 1,
                                nullptr, nullptr, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
@@ -566,14 +573,14 @@ int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *
                                    fo_geometry geometry, const float *sinks, float *output, int64_t query_begin,
                                    int64_t query_end, fo_prefill_options options) {
     return fo_attention_prefill_bf16_rows_split(ctx, q, keys_bf16, values_bf16, total_len, n_heads, n_kv_heads,
-                                                geometry, sinks, output, query_begin, query_end, options, 1);
+                                                geometry, sinks, output, 0, query_begin, query_end, options, 1);
 }
 
 int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint16_t *keys_bf16,
                                          const uint16_t *values_bf16, int64_t total_len, int64_t n_heads,
-                                         int64_t n_kv_heads, fo_geometry geometry, const float *sinks, float *output,
-                                         int64_t query_begin, int64_t query_end, fo_prefill_options options,
-                                         int32_t kv_splits) {
+                                         int64_t n_kv_heads, fo_geometry geometry, const float *sinks, void *output,
+                                         int32_t out_bf16, int64_t query_begin, int64_t query_end,
+                                         fo_prefill_options options, int32_t kv_splits) {
     if (!ctx) return fail(FO_ERR_INVALID, "null context");
     if (kv_splits < 1 || kv_splits > 64) return fail(FO_ERR_INVALID, "kv_splits must be 1..64");
     if (!q || !keys_bf16 || !values_bf16 || !sinks || !output) return fail(FO_ERR_INVALID, "null argument");
@@ -595,11 +602,96 @@ int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint
         po = (float *)ctx->split_o.ptr;
         pml = (float *)ctx->split_ml.ptr;
     }
-    cudaError_t e = fo_launch_prefill_bf16(q, keys_bf16, values_bf16, sinks, output, total_len, n_heads, n_kv_heads,
+    cudaError_t e = fo_launch_prefill_bf16(q, keys_bf16, values_bf16, sinks, output, out_bf16 != 0, total_len, n_heads,
+                                           n_kv_heads,
                                            geometry.image_start, geometry.image_end, query_begin, query_end,
                                            options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST,
                                            ctx->dev_err, kv_splits, po, pml, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
+    return FO_OK;
+}
+
+// ------------------------------------------------- head-sharded prefill
+int fo_nccl_unique_id(uint8_t *id) {
+    if (!id) return fail(FO_ERR_INVALID, "fo_nccl_unique_id: null buffer");
+    char msg[256];
+    if (fo_nccl_unique_id_impl(id, msg, sizeof msg)) return fail(FO_ERR_CUDA, "%s", msg);
+    return FO_OK;
+}
+
+int fo_nccl_comm_init(fo_ctx *ctx, int32_t world, int32_t rank, const uint8_t *id, void **comm) {
+    if (!ctx || !id || !comm) return fail(FO_ERR_INVALID, "fo_nccl_comm_init: null argument");
+    if (world < 1 || rank < 0 || rank >= world) return fail(FO_ERR_INVALID, "fo_nccl_comm_init: bad rank %d of %d", rank, world);
+    *comm = nullptr;
+    DeviceGuard guard(ctx->device);
+    char msg[256];
+    if (fo_nccl_comm_init_impl(world, rank, id, comm, msg, sizeof msg)) return fail(FO_ERR_CUDA, "%s", msg);
+    return FO_OK;
+}
+
+int fo_nccl_comm_destroy(void *comm) {
+    if (!comm) return FO_OK;
+    char msg[256];
+    if (fo_nccl_comm_destroy_impl(comm, msg, sizeof msg)) return fail(FO_ERR_CUDA, "%s", msg);
+    return FO_OK;
+}
+
+int fo_sharded_prefill_bf16(fo_ctx *ctx, void *comm, int32_t rank, int32_t world, const float *q,
+                            const uint16_t *keys_bf16, const uint16_t *values_bf16, int64_t total_len,
+                            int64_t n_heads, int64_t n_kv_heads, fo_geometry geometry, const float *sinks,
+                            fo_prefill_options options, int32_t n_bands, int32_t kv_splits, uint16_t *gathered) {
+    if (!ctx || !comm || !gathered) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16: null argument");
+    if (world < 1 || rank < 0 || rank >= world) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16: bad rank");
+    if (n_bands < 1 || kv_splits < 0 || kv_splits > 64) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16: bad bands or kv_splits");
+    if (!aligned16(gathered)) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16: gathered must be 16-byte aligned");
+    if (total_len < 4 || n_heads < 1) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16: bad shape");
+    DeviceGuard guard(ctx->device);
+    // Bands of about equal size on 256-row boundaries (the kernel's query pairs).
+    const int64_t pairs = (total_len + 255) / 256;
+    const int64_t nb = std::max<int64_t>(1, std::min<int64_t>(n_bands, pairs));
+    std::vector<std::pair<int64_t, int64_t>> band;
+    for (int64_t i = 0; i < nb; i++) {
+        const int64_t b = (pairs * i / nb) * 256, e = std::min(total_len, (pairs * (i + 1) / nb) * 256);
+        if (e > b) band.emplace_back(b, e);
+    }
+    if (kv_splits == 0) {
+        // Enough key ranges that a band's launch has a CTA per SM (at most 8).
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+        int64_t least = pairs;
+        for (auto &be : band) least = std::min<int64_t>(least, (be.second - be.first + 255) / 256);
+        kv_splits = 1;
+        while (kv_splits < 8 && least * n_heads * kv_splits < sms) kv_splits *= 2;
+    }
+    if (!ctx->comm) FO_CUDA(cudaStreamCreateWithFlags(&ctx->comm, cudaStreamNonBlocking), "cudaStreamCreate");
+    while (ctx->comm_ev.size() < band.size() + 2) {
+        cudaEvent_t e;
+        FO_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        ctx->comm_ev.push_back(e);
+    }
+    // The gathers write peers' rows: after whatever the caller queued before.
+    FO_CUDA(cudaEventRecord(ctx->comm_ev[0], ctx->stream), "cudaEventRecord");
+    FO_CUDA(cudaStreamWaitEvent(ctx->comm, ctx->comm_ev[0], 0), "cudaStreamWaitEvent");
+    const int64_t row_elems = n_heads * 64;
+    char msg[256];
+    for (int64_t i = (int64_t)band.size() - 1; i >= 0; i--) {
+        const int64_t b = band[i].first, e = band[i].second, rows = e - b;
+        uint16_t *block = gathered + world * b * row_elems;
+        // Row r of this rank's slot lands at block + (rank * rows + r - b) * row_elems.
+        uint16_t *out = block + (rank * rows - b) * row_elems;
+        int st = fo_attention_prefill_bf16_rows_split(ctx, q, keys_bf16, values_bf16, total_len, n_heads, n_kv_heads,
+                                                      geometry, sinks, out, 1, b, e, options, kv_splits);
+        if (st != FO_OK) return st;
+        cudaEvent_t done = ctx->comm_ev[1 + i];
+        FO_CUDA(cudaEventRecord(done, ctx->stream), "cudaEventRecord");
+        FO_CUDA(cudaStreamWaitEvent(ctx->comm, done, 0), "cudaStreamWaitEvent");
+        if (fo_nccl_gather_bf16(comm, block, (size_t)(rows * row_elems), rank, ctx->comm, msg, sizeof msg))
+            return fail(FO_ERR_CUDA, "%s", msg);
+    }
+    // The caller's stream sees the whole gathered page.
+    cudaEvent_t all = ctx->comm_ev[band.size() + 1];
+    FO_CUDA(cudaEventRecord(all, ctx->comm), "cudaEventRecord");
+    FO_CUDA(cudaStreamWaitEvent(ctx->stream, all, 0), "cudaStreamWaitEvent");
     return FO_OK;
 }
 

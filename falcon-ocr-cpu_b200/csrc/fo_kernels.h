@@ -39,6 +39,15 @@ cudaError_t fo_launch_qkv_rows(const float *qkv, const float *rope, int64_t rows
 cudaError_t fo_launch_qkv_append(const float *qkv, const float *rope, int64_t rows, int heads, int groups, float *q,
                                  int format, void *tail_codes, uint16_t *tail_scales, int64_t tail_stride,
                                  int64_t first, cudaStream_t stream);
+// NCCL for the head-sharded prefill (sharded.cu), resolved at run time from
+// libnccl.so.2; each returns 0, or -1 with a message in msg.
+#define FO_NCCL_ID_BYTES 128
+int fo_nccl_unique_id_impl(uint8_t *id, char *msg, size_t n);
+int fo_nccl_comm_init_impl(int world, int rank, const uint8_t *id, void **comm, char *msg, size_t n);
+int fo_nccl_comm_destroy_impl(void *comm, char *msg, size_t n);
+int fo_nccl_gather_bf16(void *comm, uint16_t *block, size_t count, int rank, cudaStream_t stream, char *msg,
+                        size_t n);
+
 // One cache's share of a batched append: its expanded rows and tail.
 struct fo_append_page {
     const float *k, *v;  // [rows][H][64]

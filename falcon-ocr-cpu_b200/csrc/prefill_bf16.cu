@@ -53,7 +53,8 @@ constexpr uint32_t TMEM_COLS = 512;
 
 struct Bf16Args {
     const float *q, *sinks;
-    float *out;
+    void *out;      // [T][H][64] FP32, or BF16 when out_bf16
+    int out_bf16;   // round the output to BF16 (nearest even) as it is stored
     unsigned *err;
     int64_t total, n_heads, n_kv_heads, image_start, image_end;
     int64_t pair_begin, pair_end;  // the 256-query pairs [begin, end) this launch computes
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             } else if (row < T) {
                 const float lse = STATIC ? logf(l) : m2 * 0.69314718055994530942f + logf(l);
                 const float ss = sink_scale(a.sinks[head], lse);
-                float4 *dst = reinterpret_cast<float4 *>(a.out + (row * H + head) * FO_HD);
+                const int64_t at = (row * H + head) * FO_HD;
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     float4 v;
@@ -336,7 +337,12 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
                     v.y = (__uint_as_float(o[4 * i + 1]) / l) * ss;
                     v.z = (__uint_as_float(o[4 * i + 2]) / l) * ss;
                     v.w = (__uint_as_float(o[4 * i + 3]) / l) * ss;
-                    dst[i] = v;
+                    if (a.out_bf16)
+                        reinterpret_cast<uint2 *>(static_cast<uint16_t *>(a.out) + at)[i] =
+                            make_uint2((uint32_t)bf16_rne(v.x) | ((uint32_t)bf16_rne(v.y) << 16),
+                                       (uint32_t)bf16_rne(v.z) | ((uint32_t)bf16_rne(v.w) << 16));
+                    else
+                        reinterpret_cast<float4 *>(static_cast<float *>(a.out) + at)[i] = v;
                 }
             }
         }
@@ -488,8 +494,8 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
 // scaled by 2^(m_r - M) first.
 template <bool STATIC>
 __global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *part_o, const float *part_ml,
-                                                                  const float *sinks, float *out, int64_t T,
-                                                                  int64_t H, int64_t row0, int64_t rows,
+                                                                  const float *sinks, void *out, int out_bf16,
+                                                                  int64_t T, int64_t H, int64_t row0, int64_t rows,
                                                                   int n_split) {
     const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (w >= rows * H) return;
@@ -516,7 +522,13 @@ __global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *p
     }
     const float lse = STATIC ? logf(l) : M * 0.69314718055994530942f + logf(l);
     const float ss = sink_scale(sinks[head], lse);
-    *reinterpret_cast<float2 *>(out + (row * H + head) * FO_HD + 2 * lane) = make_float2((o0 / l) * ss, (o1 / l) * ss);
+    const float y0 = (o0 / l) * ss, y1 = (o1 / l) * ss;
+    const int64_t at = (row * H + head) * FO_HD + 2 * lane;
+    if (out_bf16)
+        *reinterpret_cast<uint32_t *>(static_cast<uint16_t *>(out) + at) =
+            (uint32_t)bf16_rne(y0) | ((uint32_t)bf16_rne(y1) << 16);
+    else
+        *reinterpret_cast<float2 *>(static_cast<float *>(out) + at) = make_float2(y0, y1);
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -547,7 +559,8 @@ static bool make_map(CUtensorMap *m, const uint16_t *base, int64_t rows, int64_t
 }  // namespace fo
 
 extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *keys_bf16, const uint16_t *values_bf16,
-                                              const float *sinks, float *out, int64_t total, int64_t n_heads,
+                                              const float *sinks, void *out, int out_bf16, int64_t total,
+                                              int64_t n_heads,
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
                                               int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
                                               unsigned *err, int n_split, float *part_o, float *part_ml,
@@ -559,7 +572,7 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
     if (!fo::make_map(&mk, keys_bf16, total, n_heads) || !fo::make_map(&mv, values_bf16, total, n_kv_heads))
         return cudaErrorInvalidValue;
     const int64_t pb = query_begin / 256, pe = (query_end + 255) / 256;
-    fo::Bf16Args args{q, sinks, out, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe,
+    fo::Bf16Args args{q, sinks, out, out_bf16 != 0, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe,
                       n_split, part_o, part_ml};
     if ((pe - pb) * n_split > 65535) return cudaErrorInvalidValue;  // grid y limit
     dim3 grid((unsigned)n_heads, (unsigned)((pe - pb) * n_split));
@@ -579,10 +592,10 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
     const int64_t rows = query_end - query_begin;
     const unsigned blocks = (unsigned)((rows * n_heads + 7) / 8);
     if (softmax_static)
-        fo::prefill_split_merge_kernel<true><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, total, n_heads,
-                                                                         query_begin, rows, n_split);
+        fo::prefill_split_merge_kernel<true><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, out_bf16,
+                                                                         total, n_heads, query_begin, rows, n_split);
     else
-        fo::prefill_split_merge_kernel<false><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, total,
-                                                                          n_heads, query_begin, rows, n_split);
+        fo::prefill_split_merge_kernel<false><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, out_bf16,
+                                                                          total, n_heads, query_begin, rows, n_split);
     return cudaGetLastError();
 }

@@ -93,6 +93,7 @@ EXPORTS = [
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
     "fo_kv_attention_decode_batch", "fo_kv_append_batch", "fo_qkv_prefix_rows", "fo_kv_append_qkv",
+    "fo_sharded_prefill_bf16", "fo_nccl_unique_id", "fo_nccl_comm_init", "fo_nccl_comm_destroy",
     "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
@@ -138,11 +139,16 @@ def lib() -> ctypes.CDLL:
         "fo_kv_append_batch": (I, [PP, I64, PP, PP, I64]),
         "fo_qkv_prefix_rows": (I, [P, P, P, I64, I64, I64, P, P, P, P, P]),
         "fo_kv_append_qkv": (I, [P, P, P, I64, P]),
+        "fo_sharded_prefill_bf16": (I, [P, P, I32, I32, P, P, P, I64, I64, I64, Geometry, P, PrefillOptions, I32,
+                                        I32, P]),
+        "fo_nccl_unique_id": (I, [P]),
+        "fo_nccl_comm_init": (I, [P, I32, I32, P, ctypes.POINTER(P)]),
+        "fo_nccl_comm_destroy": (I, [P]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
         "fo_decode_static_scratch_status": (I, [P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
         "fo_attention_prefill_bf16_rows": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64, PrefillOptions]),
-        "fo_attention_prefill_bf16_rows_split": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I64, I64,
+        "fo_attention_prefill_bf16_rows_split": (I, [P, P, P, P, I64, I64, I64, Geometry, P, P, I32, I64, I64,
                                                      PrefillOptions, I]),
         "fo_i8_seal": (I, [P, P, P, I64, I64, I, ctypes.POINTER(P)]),
         "fo_i8_destroy": (I, [P]),
@@ -284,7 +290,8 @@ def attention_prefill_bf16_rows(q, keys_bf16, values_bf16, geometry, sinks, outp
     """fo_attention_prefill_bf16_rows: the BF16 prefill of query rows
     [query_begin, query_end) of a pure prefix (CUDA tensors; BF16 keys and
     values already converted).  Rows outside the range are left as they are.
-    kv_splits > 1 cuts each query pair's keys into that many ranges
+    kv_splits > 1 cuts each query pair's keys into that many ranges, and a
+    BF16 `output` takes the rounded result directly
     (fo_attention_prefill_bf16_rows_split)."""
     ctx = ctx or default_context()
     for a in (q, keys_bf16, values_bf16, sinks, output):
@@ -293,7 +300,8 @@ def attention_prefill_bf16_rows(q, keys_bf16, values_bf16, geometry, sinks, outp
     total = q.numel() // (n_heads * 64)
     if options is None:
         options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
-    if kv_splits == 1:
+    out_bf16 = 1 if str(output.dtype) == "torch.bfloat16" else 0
+    if kv_splits == 1 and not out_bf16:
         check(lib().fo_attention_prefill_bf16_rows(ctx.handle, q.data_ptr(), keys_bf16.data_ptr(),
                                                    values_bf16.data_ptr(), total, n_heads, n_kv_heads,
                                                    Geometry(*geometry), sinks.data_ptr(), output.data_ptr(),
@@ -302,7 +310,7 @@ def attention_prefill_bf16_rows(q, keys_bf16, values_bf16, geometry, sinks, outp
         check(lib().fo_attention_prefill_bf16_rows_split(ctx.handle, q.data_ptr(), keys_bf16.data_ptr(),
                                                          values_bf16.data_ptr(), total, n_heads, n_kv_heads,
                                                          Geometry(*geometry), sinks.data_ptr(), output.data_ptr(),
-                                                         query_begin, query_end, options, kv_splits))
+                                                         out_bf16, query_begin, query_end, options, kv_splits))
     return output
 
 
@@ -413,6 +421,46 @@ def append_qkv(cache: SplitPrefix, qkv, rope, rows: int, q):
     """fo_kv_append_qkv on device tensors: decode rows' queries into q, their
     keys and values appended to the cache's tail."""
     check(lib().fo_kv_append_qkv(cache.handle, qkv.data_ptr(), rope.data_ptr(), rows, q.data_ptr()))
+
+
+class NcclComm:
+    """An NCCL communicator from the library's NCCL (fo_nccl_comm_init); rank 0
+    makes the id with nccl_unique_id() and the caller shares it."""
+
+    def __init__(self, world: int, rank: int, uid: bytes, ctx=None):
+        ctx = ctx or default_context()
+        if len(uid) != 128:
+            raise FoError("an NCCL unique id is 128 bytes")
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(uid)
+        h = ctypes.c_void_p()
+        check(lib().fo_nccl_comm_init(ctx.handle, world, rank, buf, ctypes.byref(h)))
+        self.handle, self.world, self.rank = h, world, rank
+
+    def close(self):
+        if self.handle:
+            check(lib().fo_nccl_comm_destroy(self.handle))
+            self.handle = None
+
+
+def nccl_unique_id() -> bytes:
+    buf = (ctypes.c_uint8 * 128)()
+    check(lib().fo_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+def sharded_prefill_bf16(comm: NcclComm, q, keys_bf16, values_bf16, geometry, sinks, gathered, n_heads, n_kv_heads,
+                         n_bands=1, kv_splits=0, options=None, ctx=None):
+    """fo_sharded_prefill_bf16 on this rank's heads (contiguous CUDA tensors);
+    `gathered` BF16 holds the bands' rank-major blocks one after another."""
+    ctx = ctx or default_context()
+    total = q.numel() // (n_heads * 64)
+    if options is None:
+        options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
+    check(lib().fo_sharded_prefill_bf16(ctx.handle, comm.handle, comm.rank, comm.world, q.data_ptr(),
+                                        keys_bf16.data_ptr(), values_bf16.data_ptr(), total, n_heads, n_kv_heads,
+                                        Geometry(*geometry), sinks.data_ptr(), options, n_bands, kv_splits,
+                                        gathered.data_ptr()))
+    return gathered
 
 
 class Int8Cache:

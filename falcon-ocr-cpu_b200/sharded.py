@@ -158,12 +158,15 @@ class ShardedPrefill:
             return self.gathered
         caller = torch.cuda.current_stream(self.q.device)
         self.compute_stream.wait_stream(caller)
+        # The CUDA kernel stores BF16 rows itself (no conversion pass).
+        direct = self.compute is cuda_band and self.out_lp.dtype == torch.bfloat16
         for i in reversed(range(len(self.bands))):
             b, e = self.bands[i]
             with torch.cuda.stream(self.compute_stream):
                 self.compute(self.q, self.kb, self.vb, self.sinks, self.geometry, self.heads, self.groups, b, e,
-                             self.out, **kwargs)
-                self.out_lp[b:e].copy_(self.out[b:e])
+                             self.out_lp if direct else self.out, **kwargs)
+                if not direct:
+                    self.out_lp[b:e].copy_(self.out[b:e])
                 ev = torch.cuda.Event()
                 ev.record(self.compute_stream)
             with torch.cuda.stream(self.comm_stream):

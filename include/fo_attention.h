@@ -29,6 +29,10 @@
  * Entry points with no single reference counterpart (each says why below):
  *   fo_attention_prefill_bf16_rows[_split]  query-row bands of the BF16 prefill
  *                                  (the head-sharded multi-GPU prefill's unit)
+ *   fo_sharded_prefill_bf16        one page's prefill with heads sharded over the ranks of
+ *                                  an NCCL communicator, output all-gathered (BASELINE
+ *                                  config 5b; the reference prefills on one host)
+ *   fo_nccl_unique_id, fo_nccl_comm_init, fo_nccl_comm_destroy  its communicator
  *   fo_convert_bf16                the Bf16Kv::Convert rounding on its own
  *   fo_decode_rows_static_scratch  verify decode with no device allocation,
  *   fo_decode_static_scratch_status  and its device error report
@@ -184,12 +188,40 @@ int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *
  * GPUs), where the longest pairs would otherwise bound the launch.  Results
  * equal the unsplit call within rounding (the ranges' partial sums add in a
  * different order); the partials live in context scratch
- * (kv_splits x total_len x n_heads x 65 floats). */
+ * (kv_splits x total_len x n_heads x 65 floats).  With out_bf16 set, output is
+ * BF16 [total][n_heads][64] instead (each value the FP32 result rounded to
+ * nearest even as it is stored), the operand of the sharded prefill's
+ * gather; 8-byte aligned then. */
 int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint16_t *keys_bf16,
                                          const uint16_t *values_bf16, int64_t total_len, int64_t n_heads,
-                                         int64_t n_kv_heads, fo_geometry geometry, const float *sinks, float *output,
-                                         int64_t query_begin, int64_t query_end, fo_prefill_options options,
-                                         int32_t kv_splits);
+                                         int64_t n_kv_heads, fo_geometry geometry, const float *sinks, void *output,
+                                         int32_t out_bf16, int64_t query_begin, int64_t query_end,
+                                         fo_prefill_options options, int32_t kv_splits);
+
+/* The head-sharded prefill of one page on this rank (one process per GPU;
+ * `comm` an ncclComm_t of `world` ranks from the process's libnccl.so.2).
+ * This rank holds n_heads query heads and their n_kv_heads KV groups: q
+ * [total_len][n_heads][64] FP32, keys_bf16 [total_len][n_heads][64], values_bf16
+ * [total_len][n_kv_heads][64], sinks [n_heads] (device pointers).  The rows
+ * are computed in n_bands bands (256-row boundaries, latest first) with
+ * kv_splits key ranges (0: enough for one CTA per SM); each band's BF16
+ * output goes straight into this rank's slot of the band's block and the
+ * block is all-gathered in place on the context's own comm stream while the
+ * next band computes.  gathered (BF16, 16-byte aligned) holds the bands one
+ * after another, each [world][rows][n_heads][64] rank-major: head j of rank
+ * w is the page's head w * n_heads + j.  Every rank calls this with the same
+ * shapes and bands.  On return the gathers are ordered before later work on
+ * the context's stream. */
+int fo_sharded_prefill_bf16(fo_ctx *ctx, void *comm, int32_t rank, int32_t world, const float *q,
+                            const uint16_t *keys_bf16, const uint16_t *values_bf16, int64_t total_len,
+                            int64_t n_heads, int64_t n_kv_heads, fo_geometry geometry, const float *sinks,
+                            fo_prefill_options options, int32_t n_bands, int32_t kv_splits, uint16_t *gathered);
+/* NCCL plumbing for it (a host with its own NCCL binding may pass its own
+ * communicator instead): a 128-byte unique id from one rank, shared by the
+ * caller; a communicator on the context's device. */
+int fo_nccl_unique_id(uint8_t *id);
+int fo_nccl_comm_init(fo_ctx *ctx, int32_t world, int32_t rank, const uint8_t *id, void **comm);
+int fo_nccl_comm_destroy(void *comm);
 
 /* FP32 -> BF16 (round to nearest even) of n device values, the conversion
  * fo_attention_prefill_bf16 applies to Bf16Kv::Convert inputs. */

@@ -154,7 +154,7 @@ def test_row_band_entries_reject_a_null_context():
     assert L.fo_attention_prefill_bf16_rows(None, None, None, None, 256, 16, 8, g, None, None, 0, 256,
                                             opts) == F.ERR_INVALID
     for splits in (1, 0, 65):
-        assert L.fo_attention_prefill_bf16_rows_split(None, None, None, None, 256, 16, 8, g, None, None, 0, 256,
+        assert L.fo_attention_prefill_bf16_rows_split(None, None, None, None, 256, 16, 8, g, None, None, 1, 0, 256,
                                                       opts, splits) == F.ERR_INVALID
 
 
