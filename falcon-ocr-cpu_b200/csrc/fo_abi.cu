@@ -695,6 +695,27 @@ int fo_sharded_prefill_bf16(fo_ctx *ctx, void *comm, int32_t rank, int32_t world
     return FO_OK;
 }
 
+int fo_kv_seal_layer(fo_ctx *ctx, int32_t layer, uint64_t kv_q8_layers, int32_t mode, int32_t fast_exps,
+                     int32_t decode_fast_exp, const float *k, const float *v, int64_t filled, int64_t prefix_len,
+                     int64_t capacity, int64_t n_heads, int64_t n_kv_heads, int32_t chunks, fo_kv_cache **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: null output pointer");
+    *out = nullptr;
+    if (layer < 0) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: negative layer");
+    if (mode < FO_KV_F32 || mode > FO_KV_BF16) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: unknown mode %d", mode);
+    // cache.rs:243-246
+    if (filled != prefix_len) return fail(FO_ERR_INVALID, "seal only a complete prefix, before any text decode");
+    // cache.rs:247-251: bit `layer` of the mask picks Q8 records (checked_shr: none past bit 63)
+    const bool q8 = layer < 64 && ((kv_q8_layers >> layer) & 1u);
+    const int32_t format = q8 ? FO_KV_Q8 : mode;
+    fo_kv_cache *c = nullptr;
+    int st = fo_kv_seal(ctx, k, v, prefix_len, capacity, n_heads, n_kv_heads, 64, format, chunks, FO_MEM_DEVICE, &c);
+    if (st != FO_OK) return st;
+    // kv.rs:182-184: the cache's mode, not this layer's format, picks the exp
+    c->fast_exp = decode_fast_exp >= 0 ? decode_fast_exp != 0 : (fast_exps != 0 && mode == FO_KV_Q8);
+    *out = c;
+    return FO_OK;
+}
+
 int fo_kv_destroy(fo_kv_cache *c) {
     if (!c) return FO_OK;
     DeviceGuard guard(c->ctx->device);

@@ -93,7 +93,7 @@ EXPORTS = [
     "fo_kv_set_fast_exp", "fo_kv_append", "fo_kv_truncate_tail", "fo_kv_tail_len", "fo_kv_prefix_len",
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
     "fo_kv_attention_decode_batch", "fo_kv_append_batch", "fo_qkv_prefix_rows", "fo_kv_append_qkv",
-    "fo_sharded_prefill_bf16", "fo_nccl_unique_id", "fo_nccl_comm_init", "fo_nccl_comm_destroy",
+    "fo_sharded_prefill_bf16", "fo_nccl_unique_id", "fo_nccl_comm_init", "fo_nccl_comm_destroy", "fo_kv_seal_layer",
     "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
@@ -144,6 +144,8 @@ def lib() -> ctypes.CDLL:
         "fo_nccl_unique_id": (I, [P]),
         "fo_nccl_comm_init": (I, [P, I32, I32, P, ctypes.POINTER(P)]),
         "fo_nccl_comm_destroy": (I, [P]),
+        "fo_kv_seal_layer": (I, [P, I32, ctypes.c_uint64, I32, I32, I32, P, P, I64, I64, I64, I64, I64, I32,
+                                 ctypes.POINTER(P)]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
         "fo_decode_static_scratch_status": (I, [P]),
         "fo_selftest_bounded_wait": (I, [P, ctypes.c_uint64]),
@@ -332,6 +334,21 @@ class SplitPrefix:
         h = ctypes.c_void_p()
         check(lib().fo_kv_seal(ctx.handle, pk, pv, prefix_len, capacity, heads, kv_heads, head_dim, fmt, chunks, mem,
                                ctypes.byref(h)))
+        return cls(h, ctx, heads)
+
+    @classmethod
+    def seal_layer(cls, layer, k, v, filled, prefix_len, capacity, mode="bf16", kv_q8_layers=0, fast_exps=False,
+                   decode_fast_exp=None, heads=16, kv_heads=8, chunks=0, ctx=None):
+        """fo_kv_seal_layer (model::cache::seal_layer, src/model/cache.rs:218-276)
+        on device tensors k, v: Q8 records where bit `layer` of kv_q8_layers is
+        set, `mode` otherwise."""
+        ctx = ctx or default_context()
+        mode = KV_FORMATS[mode] if isinstance(mode, str) else mode
+        req = -1 if decode_fast_exp is None else int(bool(decode_fast_exp))
+        h = ctypes.c_void_p()
+        check(lib().fo_kv_seal_layer(ctx.handle, layer, kv_q8_layers, mode, int(bool(fast_exps)), req, k.data_ptr(),
+                                     v.data_ptr(), filled, prefix_len, capacity, heads, kv_heads, chunks,
+                                     ctypes.byref(h)))
         return cls(h, ctx, heads)
 
     def close(self):

@@ -11,6 +11,7 @@
  *                                  src/kernels/attention/mod.rs:321-349
  *   fo_kv_seal                   SplitPrefix::from_compact  src/quant/kv.rs:225-236
  *   fo_kv_set_fast_exp           SplitPrefix::with_fast_exp src/quant/kv.rs:423-426
+ *   fo_kv_seal_layer             model::cache::seal_layer   src/model/cache.rs:218-276
  *   fo_kv_append                 SplitPrefix::append        src/quant/kv.rs:430-449
  *   fo_kv_truncate_tail          SplitPrefix::truncate_tail src/quant/kv.rs:846-849
  *   fo_kv_tail_len               SplitPrefix::tail_len      src/quant/kv.rs:841-843
@@ -236,6 +237,18 @@ int fo_convert_bf16(fo_ctx *ctx, const float *src, uint16_t *dst, int64_t n);
 int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, int64_t capacity, int64_t n_heads,
                int64_t n_kv_heads, int64_t head_dim, int32_t format, int32_t chunks, int mem, fo_kv_cache **out);
 int fo_kv_destroy(fo_kv_cache *cache);
+/* seal_layer (src/model/cache.rs:218-276) for layer `layer` after its
+ * prefill, on DEVICE pointers k, v (the compact prefix): filled must equal
+ * prefix_len (a complete prefix); the records are Q8 when bit `layer` of
+ * kv_q8_layers is set (Tuning::kv_q8_layers, cache.rs:247; layers past 63
+ * never) and `mode` otherwise; the decode's fast exp is decode_fast_exp when
+ * it is 0 or 1 (Tuning::decode_fast_exp) and otherwise fast_exps with a Q8
+ * mode (default_fast_exp, kv.rs:182-184: the cache's mode, not the layer's
+ * format, decides).  A compact-mode cache is never sealed: the caller keeps
+ * its compact buffers. */
+int fo_kv_seal_layer(fo_ctx *ctx, int32_t layer, uint64_t kv_q8_layers, int32_t mode, int32_t fast_exps,
+                     int32_t decode_fast_exp, const float *k, const float *v, int64_t filled, int64_t prefix_len,
+                     int64_t capacity, int64_t n_heads, int64_t n_kv_heads, int32_t chunks, fo_kv_cache **out);
 /* SplitPrefix::with_fast_exp (kv.rs:423-426): the softmax's exp becomes
  * exp_poly (src/kernels/exp.rs:232-277) for single and verify rows alike. */
 int fo_kv_set_fast_exp(fo_kv_cache *cache, int32_t fast);

@@ -143,6 +143,13 @@ def test_batched_and_fused_entries_reject_bad_arguments():
     assert L.fo_qkv_prefix_rows(None, None, None, 4, 16, 8, None, None, None, None, None) == F.ERR_INVALID
     assert L.fo_kv_append_qkv(None, None, None, 1, None) == F.ERR_INVALID
     assert L.fo_kv_append_qkv(None, None, None, -1, None) == F.ERR_INVALID
+    out = ctypes.c_void_p()
+    seal = L.fo_kv_seal_layer
+    assert seal(None, 0, 0, F.KV_BF16, 0, -1, None, None, 8, 8, 9, 16, 8, 0, None) == F.ERR_INVALID
+    assert seal(None, 0, 0, 7, 0, -1, None, None, 8, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
+    assert seal(None, 0, 0, F.KV_BF16, 0, -1, None, None, 7, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
+    assert "complete prefix" in last_error()
+    assert seal(None, -1, 0, F.KV_BF16, 0, -1, None, None, 8, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
 
 
 def test_row_band_entries_reject_a_null_context():

@@ -131,3 +131,56 @@ def test_fused_prefill_operands_give_the_same_attention(ctx):
                              values_bf16=vr.to(torch.bfloat16), options=opts, ctx=ctx)
     torch.cuda.synchronize()
     assert torch.equal(out_a.view(torch.int32), out_b.view(torch.int32))
+
+
+@pytest.mark.parametrize("mode,fast", [("bf16", False), ("q8", True)])
+def test_layer_flow_stays_on_the_device(ctx, mode, fast):
+    """Three layers of one page with no host round trip (seal_layer,
+    src/model/cache.rs:218-276): fused QKV rows -> prefill attention ->
+    fo_kv_seal_layer (Q8 records on the layer kv_q8_layers names, `mode`
+    elsewhere; fast exp from the cache's mode) -> fused decode rows appended ->
+    verify decode.  Each layer equals the oracle's flow within 1e-5."""
+    T, gen, mask = 300, 3, 0b010
+    qkv_all, rope = fixture(T + gen, seed=77)
+    # The temporal half of the rotation (pairs 0..15) depends on the position
+    # only (rope.rs:99-103), so paired heads keep equal temporal keys.
+    rope = rope.reshape(T + gen, HEADS, 32, 2)
+    rope[:, :, :16] = rope[:, :1, :16]
+    rope = np.ascontiguousarray(rope).reshape(-1)
+    sinks = np.array([h * 0.2 - 1.0 for h in range(HEADS)], np.float32)
+    sd = dev(sinks)
+    for layer in range(3):
+        qkv = (qkv_all * np.float32(1.0 + 0.25 * layer)).astype(np.float32)
+        pre, dec = qkv[:T * WIDTH], qkv[T * WIDTH:]
+        rp, rd = rope[:T * HEADS * 64], rope[T * HEADS * 64:]
+        q = torch.empty(T * HEADS * 64, device="cuda")
+        k, v = torch.empty_like(q), torch.empty(T * GROUPS * 64, device="cuda")
+        F.qkv_prefix_rows(dev(pre), dev(rp), T, q, k, v, ctx=ctx)
+        out = torch.empty_like(q)
+        F.attention_with(q, k, v, T, (0, 0, 0), sd, out, HEADS, GROUPS, 64, ctx=ctx)
+        cache = F.SplitPrefix.seal_layer(layer, k, v, T, T, T + gen, mode=mode, kv_q8_layers=mask, fast_exps=fast,
+                                         ctx=ctx)
+        qd = torch.empty(gen * HEADS * 64, device="cuda")
+        F.append_qkv(cache, dev(dec), dev(rd), gen, qd)
+        dec_out = torch.empty(gen * HEADS * 64, device="cuda")
+        cache.attention_decode_rows(qd, gen, sd, dec_out)
+        torch.cuda.synchronize()
+        # the oracle's flow
+        q_ref, k_ref, v_ref = O.qkv_rows(pre, rp, T)
+        want = O.prefill64(q_ref, k_ref, v_ref, HEADS, GROUPS, (0, 0, 0), sinks)
+        got = out.cpu().numpy()
+        assert (np.abs(got - want) <= 1e-5 * (1 + np.abs(want))).all()
+        fmt = "q8" if (mask >> layer) & 1 else mode
+        ref = O.SplitCache(k_ref, v_ref, T, T + gen, fmt=fmt)
+        ref.fast_exp = fast and mode == "q8"
+        qd_ref, kd_ref, vd_ref = O.qkv_rows(dec, rd, gen)
+        kr = kd_ref.reshape(gen, HEADS, 64)[:, 0::2]
+        for t in range(gen):
+            ref.push(np.ascontiguousarray(kr[t]).reshape(-1), np.ascontiguousarray(vd_ref.reshape(gen, GROUPS, 64)[t])
+                     .reshape(-1))
+        want = ref.decode_rows(qd_ref, gen, sinks)
+        got = dec_out.cpu().numpy()
+        assert (np.abs(got - want) <= 1e-5 * (1 + np.abs(want))).all(), layer
+        cache.close()
+    with pytest.raises(F.FoError):  # only a complete prefix is sealed
+        F.SplitPrefix.seal_layer(0, k, v, T - 1, T, T + gen, ctx=ctx)
