@@ -625,6 +625,16 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
     float4 *part = reinterpret_cast<float4 *>(lk + splits + 4 - (2 * splits) % 4);  // [SLICES][16]
     const float *ml = pp->part_ml + row_head * splits * 2;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    // This thread's output slices of the first 8 * SLICES partials, loaded
+    // now so that they are in flight with the (max, denominator) loads.
+    const int dq = t % (FO_HD / 4), sl = t / (FO_HD / 4);
+    const float4 *po = reinterpret_cast<const float4 *>(pp->part_o + row_head * splits * FO_HD) + dq;
+    float4 o0[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int k = sl + i * MERGE_SLICES;
+        o0[i] = k < n ? __ldcg(po + (int64_t)k * (FO_HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     __shared__ float wred[2][MERGE_THREADS / 32];
     // Row maximum over the splits: per thread, then per warp, then over the
     // warps (a maximum does not depend on the order).
@@ -653,15 +663,13 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
     for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
     if (lane == 0) wred[1][warp] = den;
     __syncthreads();
-    const int dq = t % (FO_HD / 4), sl = t / (FO_HD / 4);
-    const float4 *po = reinterpret_cast<const float4 *>(pp->part_o + row_head * splits * FO_HD) + dq;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k0 = sl; k0 < n; k0 += 8 * MERGE_SLICES) {
         float4 o[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int k = k0 + i * MERGE_SLICES;
-            o[i] = k < n ? __ldcg(po + (int64_t)k * (FO_HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            o[i] = k0 == sl ? o0[i] : k < n ? __ldcg(po + (int64_t)k * (FO_HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int i = 0; i < 8; i++) {

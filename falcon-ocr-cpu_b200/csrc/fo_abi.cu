@@ -597,8 +597,10 @@ int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint
     DeviceGuard guard(ctx->device);
     float *po = nullptr, *pml = nullptr;
     if (kv_splits > 1) {
-        FO_CUDA(ctx->split_o.ensure((size_t)kv_splits * total_len * n_heads * 64 * 4), "cudaMalloc(split partials)");
-        FO_CUDA(ctx->split_ml.ensure((size_t)kv_splits * total_len * n_heads * 2 * 4), "cudaMalloc(split partials)");
+        // Partials of the launch's own query pairs only (rows from its first pair).
+        const int64_t span = ((query_end + 255) / 256 - query_begin / 256) * 256;
+        FO_CUDA(ctx->split_o.ensure((size_t)kv_splits * span * n_heads * 64 * 4), "cudaMalloc(split partials)");
+        FO_CUDA(ctx->split_ml.ensure((size_t)kv_splits * span * n_heads * 2 * 4), "cudaMalloc(split partials)");
         po = (float *)ctx->split_o.ptr;
         pml = (float *)ctx->split_ml.ptr;
     }

@@ -60,7 +60,9 @@ struct Bf16Args {
     int64_t pair_begin, pair_end;  // the 256-query pairs [begin, end) this launch computes
     // Key-range split (SPLIT kernels): each pair's key tiles in n_split
     // consecutive ranges, one CTA per range, writing unnormalized partials
-    // [n_split][T][H][64] and (max in log2 units, denominator) [n_split][T][H].
+    // [n_split][rows][H][64] and (max in log2 units, denominator)
+    // [n_split][rows][H], rows counted from the launch's first pair (rows =
+    // 256 x its pairs).
     int n_split;
     float *part_o, *part_ml;
 };
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             if (threadIdx.x < 256) {
                 const int64_t row = q0 + threadIdx.x;
                 if (row < T) {
-                    const int64_t idx = ((int64_t)part * T + row) * H + head;
+                    const int64_t idx = ((int64_t)part * ((a.pair_end - a.pair_begin) * 256) + (row - a.pair_begin * 256)) * H + head;
                     float4 *dst = reinterpret_cast<float4 *>(a.part_o + idx * FO_HD);
 #pragma unroll
                     for (int i = 0; i < 16; i++) dst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             tmem_wait_ld();
             if (SPLIT && row < T) {
                 // The range's unnormalized output, its max and denominator.
-                const int64_t idx = ((int64_t)part * T + row) * H + head;
+                const int64_t idx = ((int64_t)part * ((a.pair_end - a.pair_begin) * 256) + (row - a.pair_begin * 256)) * H + head;
                 float4 *dst = reinterpret_cast<float4 *>(a.part_o + idx * FO_HD);
 #pragma unroll
                 for (int i = 0; i < 16; i++)
@@ -495,8 +497,8 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
 template <bool STATIC>
 __global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *part_o, const float *part_ml,
                                                                   const float *sinks, void *out, int out_bf16,
-                                                                  int64_t T, int64_t H, int64_t row0, int64_t rows,
-                                                                  int n_split) {
+                                                                  int64_t span, int64_t base, int64_t H, int64_t row0,
+                                                                  int64_t rows, int n_split) {
     const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (w >= rows * H) return;
     const int lane = threadIdx.x & 31;
@@ -504,11 +506,11 @@ __global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *p
     float M = 0.0f;
     if constexpr (!STATIC) {
         M = -INFINITY;
-        for (int r = 0; r < n_split; r++) M = rmax(M, part_ml[(((int64_t)r * T + row) * H + head) * 2]);
+        for (int r = 0; r < n_split; r++) M = rmax(M, part_ml[(((int64_t)r * span + row - base) * H + head) * 2]);
     }
     float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
     for (int r = 0; r < n_split; r++) {
-        const int64_t idx = ((int64_t)r * T + row) * H + head;
+        const int64_t idx = ((int64_t)r * span + row - base) * H + head;
         const float2 ml = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
         float f = 1.0f;
         if constexpr (!STATIC) {
@@ -593,9 +595,11 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
     const unsigned blocks = (unsigned)((rows * n_heads + 7) / 8);
     if (softmax_static)
         fo::prefill_split_merge_kernel<true><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, out_bf16,
-                                                                         total, n_heads, query_begin, rows, n_split);
+                                                                         (pe - pb) * 256, pb * 256, n_heads,
+                                                                         query_begin, rows, n_split);
     else
         fo::prefill_split_merge_kernel<false><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, out_bf16,
-                                                                          total, n_heads, query_begin, rows, n_split);
+                                                                          (pe - pb) * 256, pb * 256, n_heads,
+                                                                          query_begin, rows, n_split);
     return cudaGetLastError();
 }

@@ -189,7 +189,7 @@ int fo_attention_prefill_bf16_rows(fo_ctx *ctx, const float *q, const uint16_t *
  * GPUs), where the longest pairs would otherwise bound the launch.  Results
  * equal the unsplit call within rounding (the ranges' partial sums add in a
  * different order); the partials live in context scratch
- * (kv_splits x total_len x n_heads x 65 floats).  With out_bf16 set, output is
+ * (kv_splits x the launch's rows, rounded to 256, x n_heads x 65 floats).  With out_bf16 set, output is
  * BF16 [total][n_heads][64] instead (each value the FP32 result rounded to
  * nearest even as it is stored), the operand of the sharded prefill's
  * gather; 8-byte aligned then. */
