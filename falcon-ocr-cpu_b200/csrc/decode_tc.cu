@@ -14,9 +14,11 @@
 //   unit      `chunk` consecutive splits of one group (chunk chosen from the
 //             prefix length so that the units about fill the GPU); a CTA
 //             walks whole units and leaves one partial per unit and row;
-//   TMA warp  (warp 8) boxes of 128 records x 64 BF16 (128-byte swizzle) through a
-//             3-stage ring: [T|S0], [S1|V0..31] and [V] of prefix records,
-//             [K] and [V] of tail records;
+//   TMA warps (warps 8 and 11) boxes of 128 records in two 4-stage rings:
+//             the keys ([T|S0] in 64-element boxes with the 128-byte
+//             swizzle and [S1] in 32-element boxes with the 64-byte swizzle
+//             of prefix records, [K] of tail records), freed when their QK
+//             is done, and the values ([V]), freed when their PV is done;
 //   QK warp   (warp 9) S = keys x Q' (M128 K64, keys in TMEM lanes: the temporal
 //             half for both heads at N64, each spatial half at N32), S and P'
 //             double-buffered;
@@ -63,17 +65,21 @@ namespace tc {
 using namespace sm100;
 
 constexpr int KEY_WARPS = 8;
-constexpr int THREADS = 352;  // warps 0-7 (head, key), 8 TMA, 9 QK issue, 10 PV issue
-constexpr int W_TMA = 8, W_QK = 9, W_PV = 10;
-constexpr int STAGES = 3;
+constexpr int THREADS = 384;  // warps 0-7 (head, key), 8 key TMA, 9 QK issue, 10 PV issue, 11 value TMA
+constexpr int W_TMA = 8, W_QK = 9, W_PV = 10, W_VTMA = 11;
+// Separate rings for the keys and the values of a split: a key stage is
+// free once its QK is done, a value stage once its PV is.
+constexpr int KST = 4, VST = 4;
 // A row's reference maximum moves only when a split's maximum passes it by
 // more than TAU, so probabilities stay below e^8 and O is rescaled in TMEM
 // only then (never, for ordinary data, after a unit's first split).
 constexpr float TAU = 8.0f;
-constexpr uint32_t BOX = 128 * 128;   // 128 records x 128 bytes
-constexpr uint32_t STAGE = 3 * BOX;   // three boxes per split
-constexpr uint32_t QTILE = 32 * 128;  // Q' of one head: 32 rows x 64 BF16
-constexpr uint32_t OFF_Q = STAGES * STAGE;
+constexpr uint32_t BOX = 128 * 128;        // 128 records x 128 bytes (64 BF16, 128-byte swizzle)
+constexpr uint32_t HBOX = 128 * 64;        // 128 records x 64 bytes (32 BF16, 64-byte swizzle)
+constexpr uint32_t KSTAGE = BOX + HBOX;    // [T|S0] and [S1] of a prefix split, [K] of a tail split
+constexpr uint32_t OFF_V = KST * KSTAGE;   // value ring: [V] boxes
+constexpr uint32_t QTILE = 32 * 128;       // Q' of one head: 32 rows x 64 BF16
+constexpr uint32_t OFF_Q = OFF_V + VST * BOX;
 constexpr uint32_t OFF_P = OFF_Q + 2 * 2 * QTILE;  // two Q' buffers x two heads
 // P' double buffer: [key][64 M rows] BF16, M row = 32 * head + 16 * term + row
 // (term 0 = hi, 1 = lo), i.e. 16-byte chunk 4 * head + 2 * term of the key's
@@ -94,8 +100,8 @@ constexpr uint32_t ACC_STRIDE = 68;
 // [2 heads][8 rows][68] floats.
 constexpr uint32_t OFF_LO = (OFF_WIN + 2 * WIN_WORDS * 4 + 15) / 16 * 16;
 constexpr uint32_t OFF_BAR = OFF_LO + 2 * 8 * ACC_STRIDE * 4;
-// full[3] empty[3] s_full[2] s_empty[2] q_full[2] p_full pv_done[2] qk_drain pv_drain
-constexpr int NBAR = 2 * STAGES + 2 + 2 + 2 + 1 + 2 + 2;
+// k_full[4] k_empty[4] v_full[4] v_empty[4] s_full[2] s_empty[2] q_full[2] p_full pv_done[2] qk_drain pv_drain
+constexpr int NBAR = 2 * KST + 2 * VST + 2 + 2 + 2 + 1 + 2 + 2;
 // after the barriers: TMEM address and abort flag
 constexpr uint32_t SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
 // S double-buffered [0, 128); O [128, 192), summed over a unit.
@@ -219,25 +225,157 @@ __device__ __forceinline__ Split split_of(const Args &a, int s) {
     return x;
 }
 
-// The TMA loads of local split i (the walk's current split) into stage
-// i mod STAGES: three boxes of a prefix split, two of a tail split.
-__device__ __forceinline__ void issue_tma(const fo_decode_page &pg, const Args &a, uint8_t *smem, uint64_t *full,
-                                          const Walk &wk, int i) {
-    const int st = i % STAGES;
-    const int g = (int)wk.group(a);
+// The key boxes of local split i (the walk's current split) into key stage
+// i mod KST: [T|S0] and [S1] of a prefix split, [K] of a tail split.
+__device__ __forceinline__ void issue_k(const fo_decode_page &pg, const Args &a, uint8_t *smem, uint64_t *k_full,
+                                        const Walk &wk, int i) {
+    const int st = i % KST;
+    const int g = wk.group(a);
     const Split x = split_of(a, wk.s);
-    uint8_t *dst = smem + st * STAGE;
+    uint8_t *dst = smem + st * KSTAGE;
     // Records are read once per call: first out of L2.
     const uint64_t pol = l2_evict_first();
     if (!x.tail) {
-        mbar_expect_tx(full + st, 3 * BOX);
-        tma_load_3d_hint(dst, &pg.tc_map, full + st, 0, x.row0, g, pol);
-        tma_load_3d_hint(dst + BOX, &pg.tc_map, full + st, 64, x.row0, g, pol);
-        tma_load_3d_hint(dst + 2 * BOX, &pg.tc_map, full + st, 96, x.row0, g, pol);
+        mbar_expect_tx(k_full + st, BOX + HBOX);
+        tma_load_3d_hint(dst, &pg.tc_map, k_full + st, 0, x.row0, g, pol);
+        tma_load_3d_hint(dst + BOX, &pg.s1_map, k_full + st, 64, x.row0, g, pol);
     } else {
-        mbar_expect_tx(full + st, 2 * BOX);
-        tma_load_3d_hint(dst, &pg.tail_map, full + st, 0, x.row0, g, pol);
-        tma_load_3d_hint(dst + 2 * BOX, &pg.tail_map, full + st, 64, x.row0, g, pol);
+        mbar_expect_tx(k_full + st, BOX);
+        tma_load_3d_hint(dst, &pg.tail_map, k_full + st, 0, x.row0, g, pol);
+    }
+}
+
+// The value box of local split i into value stage i mod VST.
+__device__ __forceinline__ void issue_v(const fo_decode_page &pg, const Args &a, uint8_t *smem, uint64_t *v_full,
+                                        const Walk &wk, int i) {
+    const int st = i % VST;
+    const int g = wk.group(a);
+    const Split x = split_of(a, wk.s);
+    const uint64_t pol = l2_evict_first();
+    mbar_expect_tx(v_full + st, BOX);
+    tma_load_3d_hint(smem + OFF_V + st * BOX, x.tail ? &pg.tail_map : &pg.tc_map, v_full + st, x.tail ? 64 : 96,
+                     x.row0, g, pol);
+}
+
+// Q' of group g's head h into buffer qb (kept out of the per-split loop):
+// thread key < 64 takes (row r, 8-dimension chunk c) and writes the three
+// BF16 terms of q[r][2g + h] (hi, mid, lo; their sum is the FP32 value).
+__device__ __noinline__ void build_qprime(const float *q, uint8_t *smem, int64_t H, int g, int h, int key, int qb,
+                                          int R) {
+    const int r = key >> 3, c = key & 7;
+    if (key >= 64 || r >= R) return;
+    const float4 *src = reinterpret_cast<const float4 *>(q + ((int64_t)r * H + 2 * g + h) * FO_HD + 8 * c);
+    const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
+    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    uint32_t wv[3][4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        float hi[2], mi[2], lo[2];
+#pragma unroll
+        for (int k2 = 0; k2 < 2; k2++) {
+            const float xv = v[2 * e + k2];
+            hi[k2] = bf16_f32(bf16_rne(xv));
+            const float r1 = __fsub_rn(xv, hi[k2]);
+            mi[k2] = bf16_f32(bf16_rne(r1));
+            lo[k2] = __fsub_rn(r1, mi[k2]);
+        }
+        wv[0][e] = pack_bf16(hi[0], hi[1]);
+        wv[1][e] = pack_bf16(mi[0], mi[1]);
+        wv[2][e] = pack_bf16(lo[0], lo[1]);
+    }
+#pragma unroll
+    for (int term = 0; term < 3; term++) {
+        const int row = term * 8 + r;
+        const uint32_t addr = smem_u32(smem + OFF_Q + (qb * 2 + h) * QTILE + row * 128) + ((c ^ r) << 4);
+        st_shared_v4(addr, wv[term][0], wv[term][1], wv[term][2], wv[term][3]);
+    }
+}
+
+// A unit's end for the head's hi and lo warps (lo_warp: the lo one), kept
+// out of the per-split loop (it runs once per unit): once the unit's last PV
+// is in, the lo warp hands O's lo rows over through shared memory and the hi
+// warp adds them to its hi rows, adds the draft window's non-finite values
+// (the list the key warps recorded, factors rebased to the final reference
+// maximum) and writes the unit's partial (lane r: row r) with the row sums
+// the four warps left in shared memory.  Both warps pass the pair's named
+// barrier whatever happened; a failed wait (ok false) skips the work.
+__device__ __noinline__ void unit_partial(const fo_decode_page &pg, uint8_t *smem, uint32_t tq, int h, bool lo_warp,
+                                          int lane, int R, bool ok, float m_fin, uint64_t *pv_done,
+                                          uint32_t phase, volatile int *abort_flag, int64_t H, int g, int unit,
+                                          int64_t prefix_len, int64_t len0) {
+    const float NEG_INF = -INFINITY;
+    const float *lsum = reinterpret_cast<const float *>(smem + OFF_RED) + 2 * 2 * 4 * 8 + h * 32;
+    int *win = reinterpret_cast<int *>(smem + OFF_WIN) + h * WIN_WORDS;
+    const bool o_ok = ok && __all_sync(0xffffffffu, mbar_wait(pv_done, phase, abort_flag, pg.err));
+    if (o_ok) tc_fence_after();
+    float *lo = reinterpret_cast<float *>(smem + OFF_LO) + (h * 8 + (lane & 7)) * ACC_STRIDE;
+    if (lo_warp && o_ok) {
+        for (int half = 0; half < 2; half++) {
+            uint32_t o[32];
+            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
+            tmem_wait_ld();
+            if (lane < R) {
+                float4 *dst = reinterpret_cast<float4 *>(lo + 32 * half);
+#pragma unroll
+                for (int d = 0; d < 8; d++)
+                    dst[d] = make_float4(__uint_as_float(o[4 * d]), __uint_as_float(o[4 * d + 1]),
+                                         __uint_as_float(o[4 * d + 2]), __uint_as_float(o[4 * d + 3]));
+            }
+        }
+    }
+    bar_named(5 + h, 64);
+    if (!lo_warp && o_ok) {
+        const int64_t row_head = (int64_t)lane * H + 2 * g + h;
+        const int64_t idx = row_head * pg.splits + unit;
+        float4 *dst = reinterpret_cast<float4 *>(pg.part_o + idx * FO_HD);
+        const bool live = lane < R && m_fin != NEG_INF;
+        const int nw = live ? win[0] : 0;
+        const float *wp = reinterpret_cast<const float *>(win + 9);
+        const float *wm = reinterpret_cast<const float *>(win + 9 + 64);
+        for (int half = 0; half < 2; half++) {
+            uint32_t o[32];
+            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
+            tmem_wait_ld();
+            if (live) {
+                float ov[32];
+                const float4 *lv = reinterpret_cast<const float4 *>(lo + 32 * half);
+#pragma unroll
+                for (int d = 0; d < 8; d++) {
+                    const float4 l4 = lv[d];
+                    ov[4 * d] = __fadd_rn(__uint_as_float(o[4 * d]), l4.x);
+                    ov[4 * d + 1] = __fadd_rn(__uint_as_float(o[4 * d + 1]), l4.y);
+                    ov[4 * d + 2] = __fadd_rn(__uint_as_float(o[4 * d + 2]), l4.z);
+                    ov[4 * d + 3] = __fadd_rn(__uint_as_float(o[4 * d + 3]), l4.w);
+                }
+                for (int e = 0; e < nw; e++) {
+                    const int tr = win[1 + e];
+                    if (prefix_len + tr >= len0 + lane) continue;  // this row does not see it
+                    const float pk = __fmul_rn(wp[e * 8 + lane], expf(__fsub_rn(wm[e * 8 + lane], m_fin)));
+                    const uint16_t *vr = reinterpret_cast<const uint16_t *>(pg.tail_codes) +
+                                         ((int64_t)g * pg.tail_stride + tr) * FO_TAIL_RECORD + 64 + 32 * half;
+#pragma unroll
+                    for (int d = 0; d < 32; d++) ov[d] = fmaf(pk, bf16_f32(vr[d]), ov[d]);
+                }
+#pragma unroll
+                for (int d = 0; d < 8; d++)
+                    dst[half * 8 + d] = make_float4(ov[4 * d], ov[4 * d + 1], ov[4 * d + 2], ov[4 * d + 3]);
+            } else if (lane < R) {
+                // No key of the unit is this row's: an empty partial.
+#pragma unroll
+                for (int d = 0; d < 8; d++) dst[half * 8 + d] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        if (lane < R) {
+            float l_run = 0.0f;
+            if (live)
+                l_run = __fadd_rn(__fadd_rn(__fadd_rn(lsum[lane], lsum[8 + lane]), lsum[16 + lane]), lsum[24 + lane]);
+            *reinterpret_cast<float2 *>(pg.part_ml + idx * 2) = make_float2(m_fin, l_run);
+        }
+    }
+    if (o_ok) tc_fence_before();
+    if (!lo_warp) {
+        __syncwarp();
+        if (lane == 0) win[0] = 0;  // this warp is the list's last reader
     }
 }
 
@@ -247,8 +385,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
-    uint64_t *full = bars, *empty = bars + STAGES;
-    uint64_t *s_full = bars + 2 * STAGES, *s_empty = s_full + 2, *q_full = s_empty + 2;
+    uint64_t *k_full = bars, *k_empty = k_full + KST, *v_full = k_empty + KST, *v_empty = v_full + VST;
+    uint64_t *s_full = v_empty + VST, *s_empty = s_full + 2, *q_full = s_empty + 2;
     uint64_t *p_full = q_full + 2, *pv_done = p_full + 1, *qk_drain = pv_done + 2, *pv_drain = qk_drain + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -257,20 +395,37 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t u0 = blockIdx.x * a.n_units / gridDim.x;
     const uint32_t u1 = (blockIdx.x + 1) * a.n_units / gridDim.x;
 
-    // The TMA thread starts the first loads before anything else and sets the
-    // other barriers up before the CTA-wide barrier (the stage buffers are
-    // not touched by the rest of the setup).
+    // The key TMA thread starts the first loads of both rings before anything
+    // else and sets the other barriers up before the CTA-wide barrier (the
+    // ring buffers are not touched by the rest of the setup).
     Walk twk;
     int t_issued = 0;
     if (threadIdx.x == W_TMA * 32) {
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(full + s, 1);
-            mbar_init(empty + s, 1);
+        for (int s = 0; s < KST; s++) {
+            mbar_init(k_full + s, 1);
+            mbar_init(k_empty + s, 1);
+        }
+        for (int s = 0; s < VST; s++) {
+            mbar_init(v_full + s, 1);
+            mbar_init(v_empty + s, 1);
         }
         mbar_fence_init();
         tma_prefetch(&pg.tc_map);
+        tma_prefetch(&pg.s1_map);
+        Walk vwk;
+        vwk.start(a, u0, u1);
         twk.start(a, u0, u1);
-        for (; twk.valid() && t_issued < STAGES; t_issued++, twk.next(a)) issue_tma(pg, a, smem, full, twk, t_issued);
+        for (int i = 0; i < KST || i < VST; i++) {
+            if (i < KST && twk.valid()) {
+                issue_k(pg, a, smem, k_full, twk, i);
+                t_issued = i + 1;
+                twk.next(a);
+            }
+            if (i < VST && vwk.valid()) {
+                issue_v(pg, a, smem, v_full, vwk, i);
+                vwk.next(a);
+            }
+        }
         for (int b = 0; b < 2; b++) {
             mbar_init(s_full + b, 1);
             mbar_init(s_empty + b, KEY_WARPS);
@@ -312,18 +467,36 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == W_TMA) {
-        // ---------------------------------------------------------- TMA
+        // ------------------------------------------------------ key TMA
         if (lane == 0) {
             bool ok = true;
             for (int i = t_issued; twk.valid() && ok; i++, twk.next(a)) {
-                const int st = i % STAGES, u = i / STAGES;
-                if (!(ok = mbar_wait(empty + st, (u - 1) & 1, abort_flag, pg.err))) break;
-                issue_tma(pg, a, smem, full, twk, i);
+                const int st = i % KST, u = i / KST;
+                if (!(ok = mbar_wait(k_empty + st, (u - 1) & 1, abort_flag, pg.err))) break;
+                issue_k(pg, a, smem, k_full, twk, i);
                 t_issued = i + 1;
             }
             if (!ok)
-                for (int i = max(0, t_issued - STAGES); i < t_issued; i++)
-                    drain_wait(full + i % STAGES, (i / STAGES) & 1);
+                for (int i = max(0, t_issued - KST); i < t_issued; i++) drain_wait(k_full + i % KST, (i / KST) & 1);
+        }
+    } else if (warp == W_VTMA) {
+        // ---------------------------------------------------- value TMA
+        // The key TMA thread issued the first VST value stages.
+        if (lane == 0) {
+            Walk wk;
+            wk.start(a, u0, u1);
+            int i = 0, issued = 0;
+            for (; i < VST && wk.valid(); i++) wk.next(a);
+            issued = i;
+            bool ok = true;
+            for (; wk.valid() && ok; i++, wk.next(a)) {
+                const int st = i % VST, u = i / VST;
+                if (!(ok = mbar_wait(v_empty + st, (u - 1) & 1, abort_flag, pg.err))) break;
+                issue_v(pg, a, smem, v_full, wk, i);
+                issued = i + 1;
+            }
+            if (!ok)
+                for (int j = max(0, issued - VST); j < issued; j++) drain_wait(v_full + j % VST, (j / VST) & 1);
         }
     } else if (warp == W_QK) {
         // ------------------------------------------------------- QK issue
@@ -337,7 +510,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         Walk wk;
         wk.start(a, u0, u1);
         for (int i = 0; wk.valid() && ok; i++, wk.next(a)) {
-            const int st = i % STAGES, sb = i & 1;
+            const int st = i % KST, sb = i & 1;
             const int g = wk.group(a);
             if (g != prev_g) {
                 qb ^= 1;
@@ -346,17 +519,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                 prev_g = g;
                 if (!ok) break;
             }
-            ok = __all_sync(0xffffffffu, mbar_wait(full + st, (i / STAGES) & 1, abort_flag, pg.err));
+            ok = __all_sync(0xffffffffu, mbar_wait(k_full + st, (i / KST) & 1, abort_flag, pg.err));
             if (ok && i >= 2)
                 ok = __all_sync(0xffffffffu, mbar_wait(s_empty + sb, ((i - 2) >> 1) & 1, abort_flag, pg.err));
             if (!ok) break;
             tc_fence_after();
             const bool tail = wk.s >= a.prefix_splits;
-            const uint32_t b0 = smem_u32(smem + st * STAGE), b1 = b0 + BOX;
+            const uint32_t b0 = smem_u32(smem + st * KSTAGE), b1 = b0 + BOX;
             const uint64_t dK0 = sdesc_sw128(b0, 16, 1024);
-            // Head 1's spatial half: the [S1|V] box of a prefix record, the
-            // key's own second half in a tail record.
-            const uint64_t dK1s = tail ? dK0 + (64 >> 4) : sdesc_sw128(b1, 16, 1024);
+            // Head 1's spatial half: the [S1] box of a prefix record (64-byte
+            // rows), the key's own second half in a tail record.
+            const uint64_t dK1s = tail ? dK0 + (64 >> 4) : sdesc_sw64(b1, 16, 512);
             const uint64_t dQ0 = sdesc_sw128(sQ + (qb * 2) * QTILE, 16, 1024);
             const uint64_t dQ1 = sdesc_sw128(sQ + (qb * 2 + 1) * QTILE, 16, 1024);
             const uint32_t d = tmem + sb * 64;
@@ -370,6 +543,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mma_bf16(d + 32, dK1s, dQ1 + 4, iS, 1);
                 mma_bf16(d + 32, dK1s + 2, dQ1 + 6, iS, 1);
                 mma_commit(s_full + sb);
+                mma_commit(k_empty + st);
             }
             __syncwarp();
         }
@@ -382,27 +556,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         // O += P'(j) V(j) over the split's 128 keys (8 K16 steps) once P'(j)
         // is in (and O rescaled where the split moved a reference maximum);
         // a unit's first split starts O afresh.  PV(j)'s completion frees P'
-        // buffer j & 1 and the split's stage (its QK finished before its S
-        // was read, which P'(j) waited for).
+        // buffer j & 1 and the split's value stage.
         const uint32_t iPV = idesc(64, 64, 1, 1);
         const uint32_t sP = smem_u32(smem + OFF_P);
         bool ok = true;
         Walk wk;
         wk.start(a, u0, u1);
         for (int j = 0; wk.valid() && ok; j++, wk.next(a)) {
-            const int st = j % STAGES;
+            const int st = j % VST;
             ok = __all_sync(0xffffffffu, mbar_wait(p_full, j & 1, abort_flag, pg.err));
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(v_full + st, (j / VST) & 1, abort_flag, pg.err));
             if (!ok) break;
             tc_fence_after();
             const bool first = wk.first_of_unit();
-            const uint64_t dV = sdesc_sw128(smem_u32(smem + st * STAGE + 2 * BOX), BOX, 1024);
+            const uint64_t dV = sdesc_sw128(smem_u32(smem + OFF_V + st * BOX), BOX, 1024);
             const uint64_t dP = sdesc_sw128(sP + (j & 1) * BOX, BOX, 1024);
             if (elect_one()) {
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++)
                     mma_bf16(tmem + TM_O, dP + kk * (2048 >> 4), dV + kk * (2048 >> 4), iPV, kk != 0 || !first);
                 mma_commit(pv_done + (j & 1));
-                mma_commit(empty + st);
+                mma_commit(v_empty + st);
             }
             __syncwarp();
         }
@@ -450,36 +624,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // chunk c).  The buffer's previous readers (the QK of the group
                 // before last) finished before the last split's S was read.
                 qb ^= 1;
-                const int r = key >> 3, c = key & 7;
-                if (key < 64 && r < R) {
-                    const float4 *src =
-                        reinterpret_cast<const float4 *>(pg.q + ((int64_t)r * H + 2 * g + h) * FO_HD + 8 * c);
-                    const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
-                    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                    uint32_t wv[3][4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        float hi[2], mi[2], lo[2];
-#pragma unroll
-                        for (int k2 = 0; k2 < 2; k2++) {
-                            const float xv = v[2 * e + k2];
-                            hi[k2] = bf16_f32(bf16_rne(xv));
-                            const float r1 = __fsub_rn(xv, hi[k2]);
-                            mi[k2] = bf16_f32(bf16_rne(r1));
-                            lo[k2] = __fsub_rn(r1, mi[k2]);
-                        }
-                        wv[0][e] = pack_bf16(hi[0], hi[1]);
-                        wv[1][e] = pack_bf16(mi[0], mi[1]);
-                        wv[2][e] = pack_bf16(lo[0], lo[1]);
-                    }
-#pragma unroll
-                    for (int term = 0; term < 3; term++) {
-                        const int row = term * 8 + r;
-                        const uint32_t addr =
-                            smem_u32(smem + OFF_Q + (qb * 2 + h) * QTILE + row * 128) + ((c ^ r) << 4);
-                        st_shared_v4(addr, wv[term][0], wv[term][1], wv[term][2], wv[term][3]);
-                    }
-                }
+                build_qprime(pg.q, smem, H, g, h, key, qb, R);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(q_full + qb);
@@ -601,8 +746,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         wm[r] = r < R ? m_ref[r < R ? r : 0] : 0.0f;
                     }
                     if (h == 0) {
-                        drain_wait(full + i % STAGES, (i / STAGES) & 1);  // the row's arrival, observed here
-                        const uint32_t vrow = smem_u32(smem + (i % STAGES) * STAGE + 2 * BOX + key * 128);
+                        drain_wait(v_full + i % VST, (i / VST) & 1);  // the row's arrival, observed here
+                        const uint32_t vrow = smem_u32(smem + OFF_V + (i % VST) * BOX + key * 128);
 #pragma unroll
                         for (int c = 0; c < 8; c++) st_shared_v4(vrow + (c << 4), 0u, 0u, 0u, 0u);
                     }
@@ -648,87 +793,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 bar_named(3 + h, 128);
                 if (hi_warp || lo_warp) {
-                    const bool o_ok =
-                        ok && __all_sync(0xffffffffu, mbar_wait(pv_done + (i & 1), (i >> 1) & 1, abort_flag, pg.err));
-                    if (o_ok) tc_fence_after();
-                    float *lo = reinterpret_cast<float *>(smem + OFF_LO) + (h * 8 + (lane & 7)) * ACC_STRIDE;
-                    if (lo_warp && o_ok) {
+                    float m_fin = NEG_INF;
 #pragma unroll
-                        for (int half = 0; half < 2; half++) {
-                            uint32_t o[32];
-                            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
-                            tmem_wait_ld();
-                            if (lane < R) {
-                                float4 *dst = reinterpret_cast<float4 *>(lo + 32 * half);
-#pragma unroll
-                                for (int d = 0; d < 8; d++)
-                                    dst[d] = make_float4(__uint_as_float(o[4 * d]), __uint_as_float(o[4 * d + 1]),
-                                                         __uint_as_float(o[4 * d + 2]), __uint_as_float(o[4 * d + 3]));
-                            }
-                        }
-                    }
-                    bar_named(5 + h, 64);
-                    if (hi_warp && o_ok) {
-                        float m_fin = NEG_INF;
-#pragma unroll
-                        for (int r = 0; r < R; r++)
-                            if (lane == r) m_fin = m_ref[r];
-                        const int64_t row_head = (int64_t)lane * H + 2 * g + h;
-                        const int64_t idx = row_head * pg.splits + wk.unit(a);
-                        float4 *dst = reinterpret_cast<float4 *>(pg.part_o + idx * FO_HD);
-                        const bool live = lane < R && m_fin != NEG_INF;
-                        const int nw = live ? win[0] : 0;
-                        const float *wp = reinterpret_cast<const float *>(win + 9);
-                        const float *wm = reinterpret_cast<const float *>(win + 9 + 64);
-#pragma unroll
-                        for (int half = 0; half < 2; half++) {
-                            uint32_t o[32];
-                            FO_TMEM_LD32(tq + TM_O + 32 * half, o);
-                            tmem_wait_ld();
-                            if (live) {
-                                float ov[32];
-                                const float4 *lv = reinterpret_cast<const float4 *>(lo + 32 * half);
-#pragma unroll
-                                for (int d = 0; d < 8; d++) {
-                                    const float4 l4 = lv[d];
-                                    ov[4 * d] = __fadd_rn(__uint_as_float(o[4 * d]), l4.x);
-                                    ov[4 * d + 1] = __fadd_rn(__uint_as_float(o[4 * d + 1]), l4.y);
-                                    ov[4 * d + 2] = __fadd_rn(__uint_as_float(o[4 * d + 2]), l4.z);
-                                    ov[4 * d + 3] = __fadd_rn(__uint_as_float(o[4 * d + 3]), l4.w);
-                                }
-                                for (int e = 0; e < nw; e++) {
-                                    const int tr = win[1 + e];
-                                    if (a.prefix_len + tr >= a.len0 + lane) continue;  // this row does not see it
-                                    const float pk =
-                                        __fmul_rn(wp[e * 8 + lane], expf(__fsub_rn(wm[e * 8 + lane], m_fin)));
-                                    const uint16_t *vr = reinterpret_cast<const uint16_t *>(pg.tail_codes) +
-                                                         ((int64_t)g * pg.tail_stride + tr) * FO_TAIL_RECORD + 64 +
-                                                         32 * half;
-#pragma unroll
-                                    for (int d = 0; d < 32; d++) ov[d] = fmaf(pk, bf16_f32(vr[d]), ov[d]);
-                                }
-#pragma unroll
-                                for (int d = 0; d < 8; d++)
-                                    dst[half * 8 + d] = make_float4(ov[4 * d], ov[4 * d + 1], ov[4 * d + 2], ov[4 * d + 3]);
-                            } else if (lane < R) {
-                                // No key of the unit is this row's: an empty partial.
-#pragma unroll
-                                for (int d = 0; d < 8; d++) dst[half * 8 + d] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            }
-                        }
-                        if (lane < R) {
-                            float l_run = 0.0f;
-                            if (live)
-                                l_run = __fadd_rn(__fadd_rn(__fadd_rn(lsum[lane], lsum[8 + lane]), lsum[16 + lane]),
-                                                  lsum[24 + lane]);
-                            *reinterpret_cast<float2 *>(pg.part_ml + idx * 2) = make_float2(m_fin, l_run);
-                        }
-                    }
-                    if (o_ok) tc_fence_before();
-                    if (hi_warp) {
-                        __syncwarp();
-                        if (lane == 0) win[0] = 0;  // this warp is the list's last reader
-                    }
+                    for (int r = 0; r < R; r++)
+                        if (lane == r) m_fin = m_ref[r];
+                    unit_partial(pg, smem, tq, h, lo_warp, lane, R, ok, m_fin, pv_done + (i & 1), (i >> 1) & 1,
+                                 abort_flag, H, g, wk.unit(a), a.prefix_len, a.len0);
                 }
 #pragma unroll
                 for (int r = 0; r < R; r++) m_ref[r] = NEG_INF;
@@ -762,20 +832,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 tc_encoder() {
 }
 
 static bool tc_map(CUtensorMap *map, const void *base, int64_t elems, int64_t rows, int64_t stride_rows,
-                   int64_t groups) {
+                   int64_t groups, uint32_t box_elems = 64) {
     auto fn = tc_encoder();
     if (!fn || rows <= 0 || rows >= (int64_t(1) << 31) || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
     cuuint64_t dims[3] = {(cuuint64_t)elems, (cuuint64_t)rows, (cuuint64_t)groups};
     cuuint64_t strides[2] = {(cuuint64_t)elems * 2, (cuuint64_t)stride_rows * elems * 2};
-    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t box[3] = {box_elems, 128, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              CU_TENSOR_MAP_INTERLEAVE_NONE, box_elems == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool fo_make_tc_maps(fo_decode_page *p, int64_t groups, int64_t tail_rows) {
     if (!tc_map(&p->tc_map, p->codes, FO_RECORD, p->prefix_len, p->prefix_stride, groups)) return false;
+    if (!tc_map(&p->s1_map, p->codes, FO_RECORD, p->prefix_len, p->prefix_stride, groups, 32)) return false;
     p->has_tail_map = 0;
     if (tail_rows > 0) {
         if (!tc_map(&p->tail_map, p->tail_codes, FO_TAIL_RECORD, tail_rows, p->tail_stride, groups)) return false;

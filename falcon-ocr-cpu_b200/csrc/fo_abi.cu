@@ -176,7 +176,7 @@ struct fo_kv_cache {
     alignas(64) CUtensorMap rec_map;                 // prefix records for the decode kernel's TMA loads
     int has_map = 0;
     // BF16 records: the tensor-core decode's maps (decode_tc.cu), built at seal.
-    alignas(64) CUtensorMap tc_map, tail_map;
+    alignas(64) CUtensorMap tc_map, tail_map, s1_map;
     int has_tc = 0, has_tail_map = 0;
 };
 
@@ -795,6 +795,7 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
         tp.tail_stride = c->tail_stride;
         if (fo_make_tc_maps(&tp, G, c->tail_capacity)) {
             c->tc_map = tp.tc_map;
+            c->s1_map = tp.s1_map;
             c->tail_map = tp.tail_map;
             c->has_tail_map = tp.has_tail_map;
             c->has_tc = 1;
@@ -992,6 +993,7 @@ int fo_kv_records(const fo_kv_cache *c, void **codes, void **scales, void **tail
 static void use_tc_layout(const fo_kv_cache *c, fo_decode_page *p) {
     if (!c->has_tc || (c->tail_len > 0 && !c->has_tail_map)) return;
     p->tc_map = c->tc_map;
+    p->s1_map = c->s1_map;
     p->tail_map = c->tail_map;
     p->has_tail_map = c->has_tail_map;
     fo_tc_layout(p, c->groups, c->tail_len);

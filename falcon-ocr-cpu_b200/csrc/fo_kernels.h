@@ -68,6 +68,7 @@ struct alignas(64) fo_decode_page {
     CUtensorMap rec_map;   // prefix records as padded slots (fo_make_record_map); valid when has_map
     CUtensorMap tc_map;    // BF16 prefix records in 64-element swizzled boxes (fo_make_tc_maps)
     CUtensorMap tail_map;  // BF16 tail records likewise; valid when has_tail_map
+    CUtensorMap s1_map;    // BF16 prefix records in 32-element boxes (64-byte swizzle): the second spatial half
     const void *codes;
     const uint16_t *scales;
     const void *tail_codes;

@@ -209,6 +209,18 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr, uint32_t lbo
     return d;
 }
 
+// The same for a K-major tile in 64-byte rows (64-byte swizzle): 8-row
+// atoms of 512 bytes.
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // version
+    d |= (uint64_t)4 << 61;  // SWIZZLE_64B
+    return d;
+}
+
 #define FO_TMEM_LD32(taddr, r)                                                                                      \
     asm volatile(                                                                                                   \
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
