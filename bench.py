@@ -664,16 +664,17 @@ def time_pages(run, args):
     """BASELINE config 5(a): 64 independent pages, each a 6,544-token
     prefix-LM prefill (C2, BF16 static shift) and then 2,048 single-row
     decode steps against its own growing BF16 split cache (KV 6,545 ->
-    8,592), pages round-robin over the ranks with no collective.  Each step
-    appends the new row to every page of the rank (fo_kv_append_batch) and
-    decodes one row per page (fo_kv_attention_decode_batch), as
-    Model::decode_batch_next does per layer (src/model/mod.rs:760-852).
-    The caches are allocated and sealed from the pages' K/V before the timed
-    region (allocation is not a per-page cost); the timed job is every
-    prefill, append and decode of the rank's pages, device time max over
-    ranks.  Synthetic pages: C2's inputs (seed 4) with each GQA pair's
-    temporal key half shared, as the split cache's records require."""
-    import ctypes
+    8,592), pages round-robin over the ranks with no collective.  A step
+    appends the new row to every page of the rank and decodes one row per
+    page, as Model::decode_batch_next does per layer
+    (src/model/mod.rs:760-852), through a batch plan (fo_kv_plan_*: the
+    descriptors stay on the device and move on by one position per step), so
+    the 2,048 steps run as 32 replays of a CUDA graph of 64 steps.  The caches
+    are allocated and sealed from the pages' K/V before the timed region
+    (allocation is not a per-page cost); the timed job is every prefill,
+    append and decode of the rank's pages, device time max over ranks.
+    Synthetic pages: C2's inputs (seed 4) with each GQA pair's temporal key
+    half shared, as the split cache's records require."""
     import generators as G
     torch, F = run.torch, run.F
     mine = list(range(run.rank, PAGES, run.world))
@@ -681,49 +682,57 @@ def time_pages(run, args):
     q, k, v, sinks, geo = G.c2_inputs(seed=4)
     k = k.copy()
     k[:, 1::2, :32] = k[:, 0::2, :32]
+    stream = torch.cuda.Stream(device=run.dev)
+    pctx = F.Context(run.local, stream=stream.cuda_stream)  # a capturable stream
     qd, kd, vd = (torch.from_numpy(x).to(run.dev) for x in (q, k, v))
     kb, vb = kd.to(torch.bfloat16), vd.to(torch.bfloat16)
     sd = torch.from_numpy(sinks).to(run.dev)
     outs = [torch.empty(SEQ * HEADS * 64, device=run.dev) for _ in range(2)]
     opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
-    warm = 4
-    caches = [F.SplitPrefix.from_compact(kd, vd, SEQ, SEQ + PAGE_STEPS + warm, fmt="bf16", ctx=run.ctx)
-              for _ in mine]
+    warm, chunk = 4, 64
+    torch.cuda.synchronize()
+    caches = [F.SplitPrefix.from_compact(kd, vd, SEQ, SEQ + PAGE_STEPS + warm, fmt="bf16", ctx=pctx) for _ in mine]
     rng = np.random.default_rng(40 + run.rank)
     row = rng.standard_normal((2, 1, KV_HEADS, 1, 64)).astype(np.float32)
     row = torch.from_numpy(np.repeat(row, 2, axis=3).reshape(2, -1)).to(run.dev)  # expanded K, V rows
     qrow = torch.from_numpy(rng.standard_normal(HEADS * 64).astype(np.float32)).to(run.dev)
     dec_out = torch.empty((n, HEADS * 64), device=run.dev)
-    L = F.lib()
-    arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
-    a_c = arr([c.handle.value for c in caches])
-    a_k, a_v = arr([row[0].data_ptr()] * n), arr([row[1].data_ptr()] * n)
-    a_q, a_s = arr([qrow.data_ptr()] * n), arr([sd.data_ptr()] * n)
-    a_o = arr([dec_out[i].data_ptr() for i in range(n)])
+    torch.cuda.synchronize()
 
     def prefill(i):
         F.attention_prefill_bf16(qd, kd, vd, geo, sd, outs[i & 1], HEADS, KV_HEADS, keys_bf16=kb, values_bf16=vb,
-                                 options=opts, ctx=run.ctx)
+                                 options=opts, ctx=pctx)
 
-    def step():
-        F.check(L.fo_kv_append_batch(a_c, n, a_k, a_v, 1))
-        F.check(L.fo_kv_attention_decode_batch(a_c, n, a_q, a_s, a_o))
+    def new_plan():
+        return F.BatchPlan(caches, [row[0]] * n, [row[1]] * n, [qrow] * n, [sd] * n, [dec_out[i] for i in range(n)])
 
-    for i in range(warm):  # untimed: warm both paths, then give the tails back
-        prefill(i)
-        step()
-    for c in caches:
-        c.truncate_tail(0)
+    with torch.cuda.stream(stream):
+        plan = new_plan()
+        for i in range(warm):  # untimed: warm both paths, then give the tails back
+            prefill(i)
+            plan.step()
+        plan.finish()
+        for c in caches:
+            c.truncate_tail(0)
+        plan = new_plan()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(chunk):
+            plan.step()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     run.barrier()
-    ev[0].record()
-    for i in range(n):
-        prefill(i)
-    ev[1].record()
-    for _ in range(PAGE_STEPS):
-        step()
-    ev[2].record()
+    with torch.cuda.stream(stream):
+        ev[0].record()
+        for i in range(n):
+            prefill(i)
+        ev[1].record()
+        for _ in range(PAGE_STEPS // chunk):
+            graph.replay()
+        ev[2].record()
+    stream.synchronize()
     run.barrier()
+    plan.finish()
     assert all(c.tail_len == PAGE_STEPS for c in caches)
     total_ms = run.max_over_ranks(ev[0].elapsed_time(ev[2]))
     prefill_ms = run.max_over_ranks(ev[0].elapsed_time(ev[1]))
@@ -741,10 +750,13 @@ def time_pages(run, args):
                                "frac": round(gbs / run.peaks["hbm_gbs"], 4),
                                "note": "record bytes of every page per step (prefix records 2,560 B per position; "
                                        "tail records counted at the same size)"},
-           "gpu_launches": n + 3 * PAGE_STEPS, "scaling": "weak per page, strong per job",
-           "note": "caches sealed before the timed region; one append, one decode and one merge launch per step"}
+           "gpu_launches": n + 4 * PAGE_STEPS, "scaling": "weak per page, strong per job",
+           "note": "caches sealed before the timed region; per step one append, one decode, one merge and one "
+                   "descriptor-advance launch, replayed from a CUDA graph of 64 steps"}
+    del graph
     for c in caches:
         c.close()
+    pctx.close()
     del outs, dec_out
     torch.cuda.empty_cache()
     return res

@@ -915,6 +915,124 @@ int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const
     return FO_OK;
 }
 
+static fo_decode_page make_page(const fo_kv_cache *c, const float *q, const float *sinks, float *out, int rows);
+
+// A batch plan: device-resident descriptors of n caches' appends and
+// single-row decodes, moved on by one position per step on the device.
+struct fo_kv_plan {
+    fo_ctx *ctx = nullptr;
+    std::vector<fo_kv_cache *> caches;
+    int32_t format = 0, fast_exp = 0;
+    int64_t heads = 0, groups = 0, max_splits = 1;
+    fo_append_page *ap = nullptr;  // [n] device
+    fo_decode_page *dp = nullptr;  // [n] device
+};
+
+static void plan_free(fo_kv_plan *p) {
+    if (p->ap) cudaFree(p->ap);
+    if (p->dp) cudaFree(p->dp);
+    delete p;
+}
+
+int fo_kv_plan_create(fo_kv_cache *const *caches, int64_t n, const float *const *k, const float *const *v,
+                      const float *const *q, const float *const *sinks, float *const *output, fo_kv_plan **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_kv_plan_create: null output pointer");
+    *out = nullptr;
+    if (!caches || !k || !v || !q || !sinks || !output || n < 1)
+        return fail(FO_ERR_INVALID, "fo_kv_plan_create: bad argument");
+    fo_ctx *ctx = caches[0] ? caches[0]->ctx : nullptr;
+    if (!ctx) return fail(FO_ERR_INVALID, "fo_kv_plan_create: null cache");
+    const fo_kv_cache *c0 = caches[0];
+    for (int64_t i = 0; i < n; i++) {
+        const fo_kv_cache *c = caches[i];
+        if (!c || !k[i] || !v[i] || !q[i] || !sinks[i] || !output[i])
+            return fail(FO_ERR_INVALID, "fo_kv_plan_create: null entry %lld", (long long)i);
+        if (c->ctx != ctx || c->format != c0->format || c->heads != c0->heads || c->fast_exp != c0->fast_exp)
+            return fail(FO_ERR_INVALID, "fo_kv_plan_create: caches must share context, format, heads and exp");
+        if (c->tail_len + 1 > c->tail_capacity)
+            return fail(FO_ERR_CAPACITY, "fo_kv_plan_create: cache %lld has no tail room", (long long)i);
+    }
+    {
+        std::vector<const fo_kv_cache *> seen(caches, caches + n);
+        std::sort(seen.begin(), seen.end());
+        if (std::adjacent_find(seen.begin(), seen.end()) != seen.end())
+            return fail(FO_ERR_INVALID, "fo_kv_plan_create: a cache appears twice");
+    }
+    DeviceGuard guard(ctx->device);
+    fo_kv_plan *p = new fo_kv_plan();
+    p->ctx = ctx;
+    p->caches.assign(caches, caches + n);
+    p->format = c0->format;
+    p->fast_exp = c0->fast_exp;
+    p->heads = c0->heads;
+    p->groups = c0->groups;
+    std::vector<fo_append_page> ha((size_t)n);
+    std::vector<fo_decode_page> hd((size_t)n);
+    for (int64_t i = 0; i < n; i++) {
+        fo_kv_cache *c = caches[i];
+        ha[i] = {k[i], v[i], c->tail_codes, c->tail_scales, c->tail_stride, c->tail_len};
+        // the decode of the step's row: it sees the position the append adds
+        hd[i] = make_page(c, q[i], sinks[i], output[i], 1);
+        hd[i].last = c->prefix_len + c->tail_len + 1;
+        hd[i].splits = (int32_t)((hd[i].last + FO_SPLIT - 1) / FO_SPLIT);
+        p->max_splits = std::max<int64_t>(p->max_splits, (c->prefix_len + c->tail_capacity + FO_SPLIT - 1) / FO_SPLIT);
+    }
+    cudaError_t e = cudaMalloc(&p->ap, sizeof(fo_append_page) * n);
+    if (e == cudaSuccess) e = cudaMalloc(&p->dp, sizeof(fo_decode_page) * n);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->ap, ha.data(), sizeof(fo_append_page) * n, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(p->dp, hd.data(), sizeof(fo_decode_page) * n, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        plan_free(p);
+        return cuda_fail(e, "fo_kv_plan_create");
+    }
+    *out = p;
+    return FO_OK;
+}
+
+int fo_kv_plan_step(fo_kv_plan *p) {
+    if (!p) return fail(FO_ERR_INVALID, "fo_kv_plan_step: null plan");
+    DeviceGuard guard(p->ctx->device);
+    const int64_t n = (int64_t)p->caches.size();
+    cudaError_t e = fo_launch_append_batch(p->ap, n, 1, p->heads, p->groups, p->format, p->ctx->stream);
+    if (e == cudaSuccess)
+        e = fo_launch_decode_batch(p->dp, n, p->format, p->groups, p->fast_exp, p->max_splits, 1, p->ctx->stream);
+    if (e == cudaSuccess) e = fo_launch_plan_advance(p->ap, p->dp, n, p->ctx->dev_err, p->ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "batch plan step launch");
+    return FO_OK;
+}
+
+int fo_kv_plan_finish(fo_kv_plan *p) {
+    if (!p) return FO_OK;
+    fo_ctx *ctx = p->ctx;
+    DeviceGuard guard(ctx->device);
+    const int64_t n = (int64_t)p->caches.size();
+    std::vector<fo_append_page> ha((size_t)n);
+    cudaError_t e = cudaMemcpyAsync(ha.data(), p->ap, sizeof(fo_append_page) * n, cudaMemcpyDeviceToHost,
+                                    p->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(p->ctx->stream);
+    unsigned bits = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&bits, p->ctx->dev_err, sizeof bits, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+        plan_free(p);
+        return cuda_fail(e, "fo_kv_plan_finish");
+    }
+    // the next append index is the number of records written (a full tail
+    // holds the capacity there)
+    for (int64_t i = 0; i < n; i++)
+        p->caches[i]->tail_len = std::min<int64_t>(ha[i].first, p->caches[i]->tail_capacity);
+    plan_free(p);
+    if (bits) {
+        cudaMemset(ctx->dev_err, 0, sizeof bits);
+        if (bits & FO_DEVERR_CAPACITY)
+            return fail(FO_ERR_CAPACITY, "a batch plan step found a cache's tail full (later steps repeated its last position)");
+        return fail(FO_ERR_CUDA, "a kernel wait exceeded its time limit and the kernel unwound (bits 0x%x)", bits);
+    }
+    return FO_OK;
+}
+
 static bool aligned8(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 
 int fo_qkv_prefix_rows(fo_ctx *ctx, const float *qkv, const float *rope, int64_t rows, int64_t n_heads,

@@ -55,6 +55,8 @@ struct fo_append_page {
     uint16_t *tail_scales;
     int64_t tail_stride, first;
 };
+// Device error bit: a batch plan step found a cache's tail full.
+#define FO_DEVERR_CAPACITY 2u
 // Append `rows` expanded rows to each of n pages in one launch.
 cudaError_t fo_launch_append_batch(const fo_append_page *pages, int64_t n, int64_t rows, int64_t heads, int64_t groups,
                                    int format, cudaStream_t stream);
@@ -122,6 +124,11 @@ cudaError_t fo_launch_decode_tc(const fo_decode_page *page, int64_t groups, int 
 // The split merge of one page (a programmatic dependent of the decode just
 // launched on `stream`).
 cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream);
+// After a batch plan step (append, decode, merge): every page moves on by one
+// position (its next append writes the following tail record, its next decode
+// sees one more position); a full tail stays and raises FO_DEVERR_CAPACITY.
+cudaError_t fo_launch_plan_advance(fo_append_page *ap, fo_decode_page *dp, int64_t n, unsigned *err,
+                                   cudaStream_t stream);
 // n_pages pages whose descriptors are a device array.
 cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format, int64_t groups,
                                    int fast_exp, int64_t max_splits, int max_rows, cudaStream_t stream);

@@ -94,6 +94,7 @@ EXPORTS = [
     "fo_kv_bytes", "fo_kv_records", "fo_kv_attention_decode", "fo_kv_attention_decode_rows",
     "fo_kv_attention_decode_batch", "fo_kv_append_batch", "fo_qkv_prefix_rows", "fo_kv_append_qkv",
     "fo_sharded_prefill_bf16", "fo_nccl_unique_id", "fo_nccl_comm_init", "fo_nccl_comm_destroy", "fo_kv_seal_layer",
+    "fo_kv_plan_create", "fo_kv_plan_step", "fo_kv_plan_finish",
     "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
@@ -144,6 +145,9 @@ def lib() -> ctypes.CDLL:
         "fo_nccl_unique_id": (I, [P]),
         "fo_nccl_comm_init": (I, [P, I32, I32, P, ctypes.POINTER(P)]),
         "fo_nccl_comm_destroy": (I, [P]),
+        "fo_kv_plan_create": (I, [PP, I64, PP, PP, PP, PP, PP, ctypes.POINTER(P)]),
+        "fo_kv_plan_step": (I, [P]),
+        "fo_kv_plan_finish": (I, [P]),
         "fo_kv_seal_layer": (I, [P, I32, ctypes.c_uint64, I32, I32, I32, P, P, I64, I64, I64, I64, I64, I32,
                                  ctypes.POINTER(P)]),
         "fo_decode_rows_static_scratch": (I, [P, P, P, P, I32, I64, I64, I64, I64, I64, I64, P, I64, P, I32, P, P]),
@@ -438,6 +442,31 @@ def append_qkv(cache: SplitPrefix, qkv, rope, rows: int, q):
     """fo_kv_append_qkv on device tensors: decode rows' queries into q, their
     keys and values appended to the cache's tail."""
     check(lib().fo_kv_append_qkv(cache.handle, qkv.data_ptr(), rope.data_ptr(), rows, q.data_ptr()))
+
+
+class BatchPlan:
+    """fo_kv_plan_*: the append of one row and the one-row decode of every
+    cache as one device-resident step (graph-capturable).  ks, vs, qs, sinks
+    and outs are device tensors the plan reads and writes at every step."""
+
+    def __init__(self, caches, ks, vs, qs, sinks, outs):
+        n = len(caches)
+        arr = lambda xs: (ctypes.c_void_p * n)(*xs)  # noqa: E731
+        h = ctypes.c_void_p()
+        check(lib().fo_kv_plan_create(arr([c.handle.value for c in caches]), n, arr([t.data_ptr() for t in ks]),
+                                      arr([t.data_ptr() for t in vs]), arr([t.data_ptr() for t in qs]),
+                                      arr([t.data_ptr() for t in sinks]), arr([t.data_ptr() for t in outs]),
+                                      ctypes.byref(h)))
+        self.handle = h
+        self._keep = (ks, vs, qs, sinks, outs)
+
+    def step(self):
+        check(lib().fo_kv_plan_step(self.handle))
+
+    def finish(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            check(lib().fo_kv_plan_finish(h))
 
 
 class NcclComm:

@@ -22,6 +22,8 @@
  *                                  calls LayerCache::attention per page (src/model/mod.rs:827-852)
  *   fo_kv_append_batch           one append per page, as Model::decode_batch_next calls
  *                                  SplitPrefix::append per page (src/model/mod.rs:760-852)
+ *   fo_kv_plan_create/step/finish  the same append + one-row decode per page as a
+ *                                  device-resident step (graph-capturable; no counterpart)
  *   fo_qkv_prefix_rows           model::fused::fused_prefix_rows (split, per-head RMS norm,
  *                                  RoPE, compact append, BF16 copies) src/model/fused.rs:17-116
  *   fo_kv_append_qkv             rope::split_norm_rope then SplitPrefix::append for decode
@@ -122,6 +124,7 @@ typedef struct {
 
 typedef struct fo_ctx fo_ctx;
 typedef struct fo_kv_cache fo_kv_cache;
+typedef struct fo_kv_plan fo_kv_plan;
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 int fo_version(void);
@@ -264,6 +267,24 @@ int fo_kv_append(fo_kv_cache *cache, const float *k, const float *v, int64_t row
  * were).  The records equal those of n separate fo_kv_append calls. */
 int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const *k, const float *const *v,
                        int64_t rows);
+/* A batch plan: the per-page append of one row and the one-row decode of
+ * Model::decode_batch_next (src/model/mod.rs:760-852) for n caches, with its
+ * launch descriptors resident on the device and moved on by one position per
+ * step on the device, so a step needs no host work and can be captured in a
+ * CUDA graph and replayed.  Cache i reads its new row from the DEVICE
+ * pointers k[i], v[i] (expanded [1][n_heads][64]) and its query from q[i],
+ * and writes its output to output[i], at every step: the caller refills
+ * those buffers between steps.  The caches share context, format, heads and
+ * exp, are distinct, and each has room for at least one more row.  While a
+ * plan is open its caches take no other calls; fo_kv_plan_finish brings
+ * their tail lengths back and frees the plan.  A step that finds a tail full
+ * writes nothing more to it and repeats its last position; finish then
+ * returns FO_ERR_CAPACITY. */
+int fo_kv_plan_create(fo_kv_cache *const *caches, int64_t n, const float *const *k, const float *const *v,
+                      const float *const *q, const float *const *sinks, float *const *output, fo_kv_plan **out);
+int fo_kv_plan_step(fo_kv_plan *plan);
+int fo_kv_plan_finish(fo_kv_plan *plan);
+
 /* The fused QKV rows of a prefill (fused_prefix_rows, src/model/fused.rs:17-116;
  * the same arithmetic as split_norm_rope, src/model/rope.rs:15-85), on DEVICE
  * pointers: qkv [rows][n_heads*64 + 2*n_kv_heads*64] projection rows, rope

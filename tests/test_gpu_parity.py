@@ -242,6 +242,116 @@ def test_append_batch_equals_per_page_appends(ctx, fmt):
         c.close()
 
 
+def plan_caches(fmt, ctx, room, prefixes=(7, 300, 1000)):
+    out = []
+    for i, p in enumerate(prefixes):
+        k, v, _ = G.kv_fixture(p, 21 + i)
+        out.append(F.SplitPrefix.from_compact(dev(k), dev(v), p, p + room, fmt=fmt, ctx=ctx))
+    return out
+
+
+def step_rows(rng, n):
+    """One decode step's expanded K, V rows and queries for n pages."""
+    kv = np.repeat(rng.standard_normal((n, 2, 8, 1, 64)).astype(np.float32), 2, axis=3).reshape(n, 2, -1)
+    q = rng.standard_normal((n, 16 * 64)).astype(np.float32)
+    return kv, q
+
+
+@pytest.mark.parametrize("fmt", [F.KV_BF16, F.KV_Q8])
+def test_batch_plan_equals_per_step_calls(ctx, fmt):
+    """fo_kv_plan_step (append + one-row decode per page from device-resident
+    descriptors) gives, step by step, the outputs of fo_kv_append_batch +
+    fo_kv_attention_decode_batch bit for bit, and leaves the same records."""
+    a, b = plan_caches(fmt, ctx, 8), plan_caches(fmt, ctx, 8)
+    n = len(a)
+    kb = [torch.empty(1024, device="cuda") for _ in range(n)]
+    vb = [torch.empty(1024, device="cuda") for _ in range(n)]
+    qb = [torch.empty(1024, device="cuda") for _ in range(n)]
+    ob = [torch.empty(1024, device="cuda") for _ in range(n)]
+    sd = [dev(np.array([h * 0.3 - 2.0 for h in range(16)], np.float32))] * n
+    plan = F.BatchPlan(b, kb, vb, qb, sd, ob)
+    rng = np.random.default_rng(8)
+    for step in range(5):
+        kv, q = step_rows(rng, n)
+        ks, vs, qs = [dev(kv[i, 0]) for i in range(n)], [dev(kv[i, 1]) for i in range(n)], [dev(q[i]) for i in range(n)]
+        oa = [torch.empty(1024, device="cuda") for _ in range(n)]
+        F.append_batch(a, ks, vs, 1)
+        F.decode_batch(a, qs, sd, oa)
+        for i in range(n):
+            kb[i].copy_(ks[i])
+            vb[i].copy_(vs[i])
+            qb[i].copy_(qs[i])
+        plan.step()
+        torch.cuda.synchronize()
+        for i in range(n):
+            assert torch.equal(oa[i].view(torch.int32), ob[i].view(torch.int32)), (step, i)
+    plan.finish()
+    for x, y in zip(a, b):
+        assert x.tail_len == y.tail_len == 5
+        rx, ry = device_records(x, fmt, 8), device_records(y, fmt, 8)
+        assert np.array_equal(rx["tail"].reshape(8, -1, 128)[:, :5], ry["tail"].reshape(8, -1, 128)[:, :5])
+    for c in a + b:
+        c.close()
+
+
+def test_batch_plan_replays_in_a_cuda_graph():
+    """A plan step captured in a CUDA graph and replayed moves the pages on
+    like eager steps (the descriptors live on the device)."""
+    stream = torch.cuda.Stream()
+    gctx = F.Context(0, stream=stream.cuda_stream)
+    a, b = plan_caches(F.KV_BF16, gctx, 12), plan_caches(F.KV_BF16, gctx, 12)
+    n = len(a)
+    rng = np.random.default_rng(9)
+    kv, q = step_rows(rng, n)
+    sd = [dev(np.linspace(-1, 1, 16).astype(np.float32))] * n
+
+    def bufs():
+        return ([dev(kv[i, 0]) for i in range(n)], [dev(kv[i, 1]) for i in range(n)], [dev(q[i]) for i in range(n)],
+                [torch.empty(1024, device="cuda") for _ in range(n)])
+    ka, va, qa, oa = bufs()
+    kb, vb, qb, ob = bufs()
+    torch.cuda.synchronize()
+    pa, pb = F.BatchPlan(a, ka, va, qa, sd, oa), F.BatchPlan(b, kb, vb, qb, sd, ob)
+    with torch.cuda.stream(stream):
+        for _ in range(7):
+            pa.step()
+        pb.step()  # one eager step before capture sets the launches up
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        pb.step()
+        pb.step()
+    for _ in range(3):
+        g.replay()
+    stream.synchronize()
+    for i in range(n):
+        assert torch.equal(oa[i].view(torch.int32), ob[i].view(torch.int32)), i
+    del g
+    pa.finish()
+    pb.finish()
+    assert [c.tail_len for c in a] == [c.tail_len for c in b] == [7] * n
+    for c in a + b:
+        c.close()
+    gctx.close()
+
+
+def test_batch_plan_stops_at_a_full_tail(ctx):
+    """A plan step past a cache's capacity writes nothing more and finish
+    reports FO_ERR_CAPACITY; the tail holds the rows it had room for."""
+    caches = plan_caches(F.KV_BF16, ctx, 2)
+    n = len(caches)
+    bufs = [[torch.zeros(1024, device="cuda") for _ in range(n)] for _ in range(4)]
+    sd = [dev(np.zeros(16, np.float32))] * n
+    plan = F.BatchPlan(caches, bufs[0], bufs[1], bufs[2], sd, bufs[3])
+    for _ in range(4):
+        plan.step()
+    with pytest.raises(F.CapacityError):
+        plan.finish()
+    assert [c.tail_len for c in caches] == [2] * n
+    for c in caches:
+        c.close()
+
+
 def test_seal_errors(ctx):
     """kv.rs:248-295 and src/quant/kv/tests.rs:355-367"""
     k = np.zeros(16 * 64, np.float32)
