@@ -307,8 +307,31 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
     float(*qw)[FO_HD] = reinterpret_cast<float(*)[FO_HD]>(dsm + L::OFF_Q) + warp * R;
     float(*pw)[CK] = reinterpret_cast<float(*)[CK]>(dsm + L::OFF_P) + warp * R;
     const int64_t H = 2 * groups;
-    const int64_t n_items = n_pages * max_splits * groups;
     const int64_t n_pairs = (int64_t)gridDim.x * NPAIR;
+    // The work items are every page's own splits x groups, page-major, split
+    // index next and group fastest (a page short of max_splits leaves no
+    // empty items behind: the pairs share only real work).  The warp reads
+    // the pages' split counts 32 at a time; `block` hands back lane's page
+    // of the block starting at b, its inclusive prefix of splits and the
+    // block's total.
+    auto page_at = [&](int64_t p) -> const fo_decode_page * { return pages ? pages + p : &page0; };
+    auto block = [&](int64_t b, int &s, int &incl) -> int64_t {
+        const int64_t p = b + lane;
+        s = p < n_pages ? page_at(p)->splits : 0;
+        incl = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += x;
+        }
+        return __shfl_sync(0xffffffffu, incl, 31);
+    };
+    int64_t n_items = 0;
+    for (int64_t b = 0; b < n_pages; b += 32) {
+        int s, incl;
+        n_items += block(b, s, incl);
+    }
+    n_items *= groups;
 
     if (t < NPAIR * S::NBUF) sm100::mbar_init(&bars[t], 32);
     if (t == 0) *abort_flag = 0;
@@ -322,16 +345,23 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
         int64_t g;
         int64_t it;
     };
-    // The next valid item at or after it (splits past a page's own count
-    // are skipped).
+    // Item it, if there is one (warp-uniform; the whole warp takes part).
     auto find = [&](Item &x, int64_t it) -> bool {
-        for (; it < n_items; it += n_pairs) {
-            x.g = it % groups;
-            const int64_t rest = it / groups;
-            x.s = (int)(rest % max_splits);
-            x.pp = pages ? pages + rest / max_splits : &page0;
-            x.it = it;
-            if (x.s < x.pp->splits) return true;
+        if (it >= n_items) return false;
+        x.g = it % groups;
+        x.it = it;
+        const int64_t k = it / groups;  // the split's index over all pages
+        int64_t base = 0;               // splits of the pages before block b
+        for (int64_t b = 0; b < n_pages; b += 32) {
+            int s, incl;
+            const int64_t total = block(b, s, incl);
+            if (k < base + total) {
+                const int l = __ffs(__ballot_sync(0xffffffffu, base + incl > k)) - 1;
+                x.pp = page_at(b + l);
+                x.s = (int)(k - base - __shfl_sync(0xffffffffu, incl - s, l));
+                return true;
+            }
+            base += total;
         }
         return false;
     };
