@@ -38,28 +38,32 @@
 
 namespace fo {
 
-enum { DF32 = 0, DQ16 = 1, DQ8 = 2, DBF16 = 3 };
+enum { DF32 = 0, DQ16 = 1, DQ8 = 2, DBF16 = 3, DQ4 = 4 };
 
 // Per-format shape of a CTA: NPAIR pairs of warps; a pair owns whole items
 // and streams their 32-key chunks through NBUF slot buffers; warp 2p + h of
 // pair p computes head h of the item's KV group.
 template <int F>
 struct Shape {
-    static constexpr int E = F == DF32 ? 4 : (F == DQ8 ? 1 : 2);  // bytes per element
-    static constexpr bool CODED = F == DQ16 || F == DQ8;
+    static constexpr int E = F == DF32 ? 4 : (F == DQ8 || F == DQ4 ? 1 : 2);  // bytes per TMA element
+    static constexpr bool CODED = F == DQ16 || F == DQ8 || F == DQ4;
+    // Bytes of n record elements (Q4: two codes per byte).
+    static constexpr int bytes(int n) { return F == DQ4 ? n / 2 : n * E; }
+    static constexpr int RB = bytes(FO_RECORD), TB = bytes(FO_TAIL_RECORD);
     static constexpr int CK = 32;                // keys per chunk (one per lane)
     static constexpr int KPL = 1;                // keys per lane
     static constexpr int NCH = FO_SPLIT / CK;    // chunks per item
     static constexpr int NPAIR = 4;
     // Slot buffers per pair: Q8 records are small enough for a third, which
     // keeps one more chunk in flight (single-row decode waits on its copies).
-    static constexpr int NBUF = F == DQ8 ? 3 : 2;
+    static constexpr int NBUF = F == DQ8 || F == DQ4 ? 3 : 2;
     static constexpr int NW = 2 * NPAIR;
     static constexpr int THREADS = 32 * NW;
     static constexpr int MIN_CTAS = F == DF32 ? 1 : 2;
     // Padded slot: 16 bytes past the record, so consecutive keys start on
-    // different banks (slot stride 4, 20 or 12 mod 32 words).
-    static constexpr int SLOT = FO_RECORD * E + 16;
+    // different banks (slot stride 4, 20 or 12 mod 32 words); a Q4 record
+    // (80 bytes, 20 mod 32 words) needs no pad.
+    static constexpr int SLOT = F == DQ4 ? RB : RB + 16;
     static_assert(NCH >= NBUF, "an item spans every buffer");
 };
 
@@ -92,6 +96,10 @@ __device__ __forceinline__ float2 slot_pair(const unsigned char *slot, int e, fl
     } else if constexpr (F == DQ16) {
         float lo, hi;
         s16x2_f32(*reinterpret_cast<const uint32_t *>(slot + 2 * e), lo, hi);
+        return make_float2(__fmul_rn(lo, scale), __fmul_rn(hi, scale));
+    } else if constexpr (F == DQ4) {
+        float lo, hi;
+        s4x2_f32(slot[e / 2], lo, hi);
         return make_float2(__fmul_rn(lo, scale), __fmul_rn(hi, scale));
     } else {
         float lo, hi;
@@ -134,6 +142,16 @@ __device__ __forceinline__ void slot_span16(const unsigned char *slot, int e, fl
                 }
             }
         }
+    } else if constexpr (F == DQ4) {
+        const uint2 x = *reinterpret_cast<const uint2 *>(slot + e / 2);
+        const uint32_t w[2] = {x.x, x.y};
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            float f[8];
+            s4x8_f32(w[c], f);
+#pragma unroll
+            for (int b = 0; b < 8; b++) out[8 * c + b] = SCALED ? __fmul_rn(f[b], scale) : f[b];
+        }
     } else {
         const uint4 x = *reinterpret_cast<const uint4 *>(slot + e);
         const uint32_t w[4] = {x.x, x.y, x.z, x.w};
@@ -167,6 +185,9 @@ __device__ __forceinline__ void slot_vpair2(const unsigned char *sa, const unsig
         if constexpr (F == DQ16) {
             s16x2_f32(*reinterpret_cast<const uint32_t *>(sa + 2 * e), a0, a1);
             s16x2_f32(*reinterpret_cast<const uint32_t *>(sb + 2 * e), b0, b1);
+        } else if constexpr (F == DQ4) {
+            s4x2_f32(sa[e / 2], a0, a1);
+            s4x2_f32(sb[e / 2], b0, b1);
         } else {
             s8x2_f32(*reinterpret_cast<const uint16_t *>(sa + e), a0, a1);
             s8x2_f32(*reinterpret_cast<const uint16_t *>(sb + e), b0, b1);
@@ -181,16 +202,16 @@ __device__ __forceinline__ void slot_vpair2(const unsigned char *sa, const unsig
 template <int F>
 __device__ __forceinline__ void stage_key(const fo_decode_page &pg, int64_t g, int64_t pos, unsigned char *slot,
                                           uint64_t *bar) {
-    constexpr int E = Shape<F>::E;
+    using S = Shape<F>;
     if (pos < pg.prefix_len) {
         const int64_t r = g * pg.prefix_stride + pos;
-        sm100::bulk_g2s(slot, reinterpret_cast<const unsigned char *>(pg.codes) + r * FO_RECORD * E, FO_RECORD * E, bar);
+        sm100::bulk_g2s(slot, reinterpret_cast<const unsigned char *>(pg.codes) + r * S::RB, S::RB, bar);
     } else {
         const int64_t r = g * pg.tail_stride + (pos - pg.prefix_len);
-        const unsigned char *rec = reinterpret_cast<const unsigned char *>(pg.tail_codes) + r * FO_TAIL_RECORD * E;
-        sm100::bulk_g2s(slot, rec, 64 * E, bar);
-        sm100::bulk_g2s(slot + 64 * E, rec + 32 * E, 32 * E, bar);
-        sm100::bulk_g2s(slot + 96 * E, rec + 64 * E, 64 * E, bar);
+        const unsigned char *rec = reinterpret_cast<const unsigned char *>(pg.tail_codes) + r * S::TB;
+        sm100::bulk_g2s(slot, rec, S::bytes(64), bar);
+        sm100::bulk_g2s(slot + S::bytes(64), rec + S::bytes(32), S::bytes(32), bar);
+        sm100::bulk_g2s(slot + S::bytes(96), rec + S::bytes(64), S::bytes(64), bar);
     }
 }
 
@@ -233,14 +254,13 @@ __device__ __forceinline__ void prefetch_item(const fo_decode_page &pg, int64_t 
     const int64_t pa = a, pb = min64(b, pg.prefix_len);
     if (pb > pa) {
         const int64_t r0 = g * pg.prefix_stride + pa;
-        prefetch_l2(reinterpret_cast<const char *>(pg.codes) + r0 * FO_RECORD * S::E, (pb - pa) * FO_RECORD * S::E);
+        prefetch_l2(reinterpret_cast<const char *>(pg.codes) + r0 * S::RB, (pb - pa) * S::RB);
         if (S::CODED) prefetch_l2(pg.scales + r0 * 5, (pb - pa) * 10);
     }
     const int64_t ta = max64(a, pg.prefix_len), tb = b;
     if (tb > ta) {
         const int64_t r0 = g * pg.tail_stride + (ta - pg.prefix_len);
-        prefetch_l2(reinterpret_cast<const char *>(pg.tail_codes) + r0 * FO_TAIL_RECORD * S::E,
-                    (tb - ta) * FO_TAIL_RECORD * S::E);
+        prefetch_l2(reinterpret_cast<const char *>(pg.tail_codes) + r0 * S::TB, (tb - ta) * S::TB);
         if (S::CODED) prefetch_l2(pg.tail_scales + r0 * 4, (tb - ta) * 8);
     }
 }
@@ -264,10 +284,29 @@ __device__ __forceinline__ void stage_chunk(const fo_decode_page &pg, int64_t g,
         if (lane == 0) sm100::tma_load_3d(crec, &pg.rec_map, bar, 0, (int)k0, (int)g);
         return;
     }
-    const uint32_t bytes = lane < nk ? FO_RECORD * S::E : 0u;
+    const uint32_t bytes = lane < nk ? (uint32_t)S::RB : 0u;
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
                  : "memory");
     if (lane < nk) stage_key<F>(pg, g, k0 + lane, crec + lane * S::SLOT, bar);
+}
+
+// rotate_query (rotation.rs:106-111: 2^-5 H D x) of a query head held as
+// dimensions (2 lane, 2 lane + 1): lanes 0-15 hold the temporal block (kind
+// 0), lanes 16-31 the spatial block (kind 1), element 2 (lane % 16) and the
+// next.  The first butterfly stage pairs a lane's own two elements, the
+// others pair lanes lane ^ 1, ^ 2, ^ 4, ^ 8 (inside the block's half-warp).
+__device__ __forceinline__ float2 rotate_query_pair(float2 v, int lane) {
+    const uint32_t signs = (lane >> 4) ? rotation_signs(1) : rotation_signs(0);
+    const int i0 = 2 * (lane & 15);
+    v.x = __uint_as_float(__float_as_uint(v.x) ^ (((signs >> i0) & 1u) << 31));
+    v.y = __uint_as_float(__float_as_uint(v.y) ^ (((signs >> (i0 + 1)) & 1u) << 31));
+    v = make_float2(__fadd_rn(v.x, v.y), __fsub_rn(v.x, v.y));
+#pragma unroll
+    for (int d = 1; d < 16; d <<= 1) {
+        const float px = __shfl_xor_sync(0xffffffffu, v.x, d), py = __shfl_xor_sync(0xffffffffu, v.y, d);
+        v = make_float2(butterfly(v.x, px, lane & d), butterfly(v.y, py, lane & d));
+    }
+    return make_float2(__fmul_rn(v.x, 0.03125f), __fmul_rn(v.y, 0.03125f));
 }
 
 // Waits on a pair's named barrier (id 1 + pair, 64 threads) and returns
@@ -370,6 +409,10 @@ __global__ void __launch_bounds__(Shape<F>::THREADS, Shape<F>::MIN_CTAS)
 #pragma unroll
         for (int r = 0; r < R; r++)
             qv[r] = __ldg(reinterpret_cast<const float2 *>(x.pp->q + (r * H + 2 * x.g + hd) * FO_HD) + lane);
+        if (x.pp->rotated) {
+#pragma unroll
+            for (int r = 0; r < R; r++) qv[r] = rotate_query_pair(qv[r], lane);
+        }
     };
 
     Item cur, nxt;
@@ -723,7 +766,19 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_const
 #pragma unroll
         for (int i = 0; i < MERGE_SLICES; i++) o = __fadd_rn(o, pf[i * FO_HD + t]);
         const float lse = m + logf(den);
-        pp->out[row_head * FO_HD + t] = (o / den) * sink_scale(pp->sinks[h], lse);
+        float y = (o / den) * sink_scale(pp->sinks[h], lse);
+        if (pp->rotated) {
+            // unrotate (rotation.rs:113-119: 2^-5 D H x) of the output block
+            // this warp holds, one element per lane: value 0..32 (kind 2) in
+            // warp 0, value 32..64 (kind 3) in warp 1.
+#pragma unroll
+            for (int half = 1; half < 32; half <<= 1)
+                y = butterfly(y, __shfl_xor_sync(0xffffffffu, y, half), lane & half);
+            y = __uint_as_float(__float_as_uint(y) ^
+                                ((((warp ? rotation_signs(3) : rotation_signs(2)) >> lane) & 1u) << 31));
+            y = __fmul_rn(y, 0.03125f);
+        }
+        pp->out[row_head * FO_HD + t] = y;
     }
 }
 
@@ -747,8 +802,8 @@ static bool record_map(CUtensorMap *map, const void *codes, int64_t prefix_len, 
     using S = fo::Shape<F>;
     auto fn = record_map_encoder();
     if (!fn || prefix_len <= 0 || prefix_len >= (int64_t(1) << 31)) return false;
-    cuuint64_t dims[3] = {FO_RECORD, (cuuint64_t)prefix_len, (cuuint64_t)groups};
-    cuuint64_t strides[2] = {(cuuint64_t)FO_RECORD * S::E, (cuuint64_t)prefix_stride * FO_RECORD * S::E};
+    cuuint64_t dims[3] = {(cuuint64_t)(S::RB / S::E), (cuuint64_t)prefix_len, (cuuint64_t)groups};
+    cuuint64_t strides[2] = {(cuuint64_t)S::RB, (cuuint64_t)prefix_stride * S::RB};
     cuuint32_t box[3] = {(cuuint32_t)(S::SLOT / S::E), (cuuint32_t)S::CK, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, type, 3, const_cast<void *>(codes), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -759,10 +814,11 @@ static bool record_map(CUtensorMap *map, const void *codes, int64_t prefix_len, 
 bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t prefix_len, int64_t prefix_stride,
                         int64_t groups) {
     if ((reinterpret_cast<uintptr_t>(codes) & 15) != 0) return false;
-    switch (format) {
+    switch (format & ~FO_KV_ROTATED_BIT) {
     case fo::DF32: return record_map<fo::DF32>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
     case fo::DQ16: return record_map<fo::DQ16>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_UINT16);
     case fo::DQ8: return record_map<fo::DQ8>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_UINT8);
+    case fo::DQ4: return record_map<fo::DQ4>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_UINT8);
     case fo::DBF16: return record_map<fo::DBF16>(map, codes, prefix_len, prefix_stride, groups, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
     }
     return false;
@@ -856,6 +912,7 @@ static cudaError_t launch_decode(const fo_decode_page &page0, const fo_decode_pa
                                  cudaStream_t stream) {
     if (n_pages <= 0 || max_splits <= 0) return cudaSuccess;
     const int ms = (int)max_splits;
+    format &= ~FO_KV_ROTATED_BIT;  // rotation travels in the pages (fo_decode_page::rotated)
 #define FO_DEC_CASE(FMT)                                                                        \
     case FMT:                                                                                   \
         return fast_exp ? launch_rows<FMT, true>(rows, page0, dev_pages, n_pages, groups, ms, stream) \
@@ -864,6 +921,7 @@ static cudaError_t launch_decode(const fo_decode_page &page0, const fo_decode_pa
         FO_DEC_CASE(fo::DF32)
         FO_DEC_CASE(fo::DQ16)
         FO_DEC_CASE(fo::DQ8)
+        FO_DEC_CASE(fo::DQ4)
         FO_DEC_CASE(fo::DBF16)
     }
 #undef FO_DEC_CASE

@@ -93,10 +93,15 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
                                              const float *sinks, int32_t fast_exp, float *output, void *stream) {
     if (!codes || !q || !sinks || !output || (tail_len > 0 && !tail_codes))
         return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: null pointer");
-    if ((format == FO_KV_Q8 || format == FO_KV_Q16) && (!scales || (tail_len > 0 && !tail_scales)))
-        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: coded records need their scales");
-    if (format < FO_KV_F32 || format > FO_KV_BF16)
+    // An element format, optionally rotated (F32, Q8 and Q4 only).
+    const int element = format & ~FO_KV_ROTATED;
+    const bool rotated = (format & FO_KV_ROTATED) != 0;
+    if ((format & ~(FO_KV_ROTATED | 7)) || element < FO_KV_F32 || element > FO_KV_Q4 ||
+        (rotated && element != FO_KV_F32 && element != FO_KV_Q8 && element != FO_KV_Q4))
         return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: unknown record format");
+    if ((element == FO_KV_Q8 || element == FO_KV_Q16 || element == FO_KV_Q4) &&
+        (!scales || (tail_len > 0 && !tail_scales)))
+        return fo_internal_fail(FO_ERR_INVALID, "static-scratch decode: coded records need their scales");
     // The records are staged with bulk copies (16-byte aligned sources); the
     // queries are read two floats at a time, the scales as 16-bit words.
     if (!aligned(codes, 16) || (tail_len > 0 && !aligned(tail_codes, 16)) || !aligned(q, 8) ||
@@ -148,6 +153,7 @@ extern "C" int fo_decode_rows_static_scratch(const void *codes, const uint16_t *
     p.last = last;
     p.rows = (int32_t)rows;
     p.splits = (int32_t)((last + FO_SPLIT - 1) / FO_SPLIT);
+    p.rotated = rotated ? 1 : 0;
     if (format == FO_KV_BF16 && fo_make_tc_maps(&p, n_kv_heads, tail_len)) {
         // The tensor-core decode's split layout (prefix and tail apart), as
         // fo_kv_attention_decode_rows uses for BF16 records; the tail map ends

@@ -191,17 +191,42 @@ struct fo_i8_cache {
 
 namespace {
 
-size_t elem_size(int format) {
-    switch (format) {
-    case FO_KV_F32: return 4;
-    case FO_KV_Q16: return 2;
-    case FO_KV_Q8: return 1;
-    case FO_KV_BF16: return 2;
+// The record formats: an element format, optionally rotated (F32, Q8 and Q4
+// only: Storage, kv.rs:128-152).
+int element_format(int format) { return format & ~FO_KV_ROTATED; }
+
+bool valid_format(int format) {
+    const int e = element_format(format);
+    if (format & ~(FO_KV_ROTATED | 7)) return false;
+    if (e < FO_KV_F32 || e > FO_KV_Q4) return false;
+    return !(format & FO_KV_ROTATED) || e == FO_KV_F32 || e == FO_KV_Q8 || e == FO_KV_Q4;
+}
+
+// Bytes of n record elements (Q4 packs two codes per byte; n even).
+size_t code_bytes(int format, size_t n) {
+    switch (element_format(format)) {
+    case FO_KV_F32: return 4 * n;
+    case FO_KV_Q16: return 2 * n;
+    case FO_KV_Q8: return n;
+    case FO_KV_BF16: return 2 * n;
+    case FO_KV_Q4: return n / 2;
     }
     return 0;
 }
 
-bool coded(int format) { return format == FO_KV_Q16 || format == FO_KV_Q8; }
+bool coded(int format) {
+    const int e = element_format(format);
+    return e == FO_KV_Q16 || e == FO_KV_Q8 || e == FO_KV_Q4;
+}
+
+const char *format_name(int format) {
+    switch (element_format(format)) {
+    case FO_KV_Q16: return "Q16";
+    case FO_KV_Q8: return "Q8";
+    case FO_KV_Q4: return "Q4";
+    }
+    return "KV";
+}
 
 // CompactKv::validate (src/kernels/attention/mod.rs:159-195).
 int validate_compact(const float *q, const fo_compact_kv *kv, int64_t query_len, const fo_geometry &g,
@@ -703,7 +728,7 @@ int fo_kv_seal_layer(fo_ctx *ctx, int32_t layer, uint64_t kv_q8_layers, int32_t 
     if (!out) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: null output pointer");
     *out = nullptr;
     if (layer < 0) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: negative layer");
-    if (mode < FO_KV_F32 || mode > FO_KV_BF16) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: unknown mode %d", mode);
+    if (!valid_format(mode)) return fail(FO_ERR_INVALID, "fo_kv_seal_layer: unknown mode %d", mode);
     // cache.rs:243-246
     if (filled != prefix_len) return fail(FO_ERR_INVALID, "seal only a complete prefix, before any text decode");
     // cache.rs:247-251: bit `layer` of the mask picks Q8 records (checked_shr: none past bit 63)
@@ -713,7 +738,9 @@ int fo_kv_seal_layer(fo_ctx *ctx, int32_t layer, uint64_t kv_q8_layers, int32_t 
     int st = fo_kv_seal(ctx, k, v, prefix_len, capacity, n_heads, n_kv_heads, 64, format, chunks, FO_MEM_DEVICE, &c);
     if (st != FO_OK) return st;
     // kv.rs:182-184: the cache's mode, not this layer's format, picks the exp
-    c->fast_exp = decode_fast_exp >= 0 ? decode_fast_exp != 0 : (fast_exps != 0 && mode == FO_KV_Q8);
+    // (the 8-bit mode and the rotated research modes)
+    const bool poly_mode = mode == FO_KV_Q8 || mode == FO_KV_Q8_ROT || mode == FO_KV_Q4_ROT;
+    c->fast_exp = decode_fast_exp >= 0 ? decode_fast_exp != 0 : (fast_exps != 0 && poly_mode);
     *out = c;
     return FO_OK;
 }
@@ -740,7 +767,7 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
     if (!(prefix_len > 0 && capacity >= prefix_len)) return fail(FO_ERR_CAPACITY, "invalid split-prefix capacity");
     // The split merge keeps two floats per split in shared memory.
     if (capacity > (int64_t)3000000) return fail(FO_ERR_CAPACITY, "split-prefix capacity above 3,000,000 positions");
-    if (format < FO_KV_F32 || format > FO_KV_BF16) return fail(FO_ERR_INVALID, "unknown split-cache format %d", format);
+    if (!valid_format(format)) return fail(FO_ERR_INVALID, "unknown split-cache format %d", format);
     if (!k || !v) return fail(FO_ERR_INVALID, "split prefix key/value pointer is null");
     if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
     if (!ctx) return fail(FO_ERR_INVALID, "null context");
@@ -757,17 +784,16 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
     c->prefix_stride = prefix_len;
     c->tail_stride = c->tail_capacity;
     c->max_splits = (capacity + FO_SPLIT - 1) / FO_SPLIT;
-    const size_t es = elem_size(format);
     const int64_t G = n_kv_heads, H = n_heads;
-    const size_t code_bytes = (size_t)G * prefix_len * FO_RECORD_ELEMS * es;
-    const size_t tail_bytes = (size_t)G * std::max<int64_t>(c->tail_capacity, 1) * FO_TAIL_ELEMS * es;
+    const size_t prefix_bytes = code_bytes(format, (size_t)G * prefix_len * FO_RECORD_ELEMS);
+    const size_t tail_bytes = code_bytes(format, (size_t)G * std::max<int64_t>(c->tail_capacity, 1) * FO_TAIL_ELEMS);
     const size_t scale_bytes = coded(format) ? (size_t)G * prefix_len * 5 * 2 : 16;
     const size_t tscale_bytes = coded(format) ? (size_t)G * std::max<int64_t>(c->tail_capacity, 1) * 4 * 2 : 16;
     cudaError_t e = cudaSuccess;
     auto alloc = [&](void **p, size_t n) {
         if (e == cudaSuccess) e = cudaMalloc(p, n);
     };
-    alloc(&c->codes, code_bytes);
+    alloc(&c->codes, prefix_bytes);
     alloc(&c->tail_codes, tail_bytes);
     alloc((void **)&c->scales, scale_bytes);
     alloc((void **)&c->tail_scales, tscale_bytes);
@@ -783,7 +809,7 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
         fo_kv_destroy(c);
         return cuda_fail(e, "fo_kv_seal: cudaMalloc");
     }
-    c->bytes = code_bytes + tail_bytes + (coded(format) ? scale_bytes + tscale_bytes : 0);
+    c->bytes = prefix_bytes + tail_bytes + (coded(format) ? scale_bytes + tscale_bytes : 0);
     // Without a tensor map the decode kernel copies record by record.
     c->has_map = fo_make_record_map(&c->rec_map, c->codes, format, prefix_len, c->prefix_stride, G) ? 1 : 0;
     if (format == FO_KV_BF16) {
@@ -833,9 +859,13 @@ int fo_kv_seal(fo_ctx *ctx, const float *k, const float *v, int64_t prefix_len, 
         fo_kv_destroy(c);
         return fail(FO_ERR_NONFINITE, "nonfinite or incomplete KV group");
     }
+    if (flags & FO_FLAG_ROTATED) {
+        fo_kv_destroy(c);
+        return fail(FO_ERR_OVERFLOW, "rotated KV group overflows");
+    }
     if (flags & FO_FLAG_OVERFLOW) {
         fo_kv_destroy(c);
-        return fail(FO_ERR_OVERFLOW, "%s KV conversion overflow", format == FO_KV_Q8 ? "Q8" : "Q16");
+        return fail(FO_ERR_OVERFLOW, "%s KV conversion overflow", format_name(format));
     }
     *out = c;
     return FO_OK;
@@ -1075,11 +1105,10 @@ int fo_kv_truncate_tail(fo_kv_cache *c, int64_t tail_len) {
         // tensor-core decode reads whole 128-position tiles of tail records,
         // and past the cache's end they must add nothing (zero keys, values).
         DeviceGuard guard(c->ctx->device);
-        const size_t es = elem_size(c->format);
-        const size_t pitch = (size_t)c->tail_stride * FO_TAIL_ELEMS * es;
-        FO_CUDA(cudaMemset2DAsync(static_cast<char *>(c->tail_codes) + (size_t)tail_len * FO_TAIL_ELEMS * es, pitch, 0,
-                                  (size_t)(c->tail_len - tail_len) * FO_TAIL_ELEMS * es, (size_t)c->groups,
-                                  c->ctx->stream),
+        const size_t pitch = code_bytes(c->format, (size_t)c->tail_stride * FO_TAIL_ELEMS);
+        FO_CUDA(cudaMemset2DAsync(static_cast<char *>(c->tail_codes) + code_bytes(c->format, (size_t)tail_len * FO_TAIL_ELEMS),
+                                  pitch, 0, code_bytes(c->format, (size_t)(c->tail_len - tail_len) * FO_TAIL_ELEMS),
+                                  (size_t)c->groups, c->ctx->stream),
                 "cudaMemset2DAsync(tail records)");
         if (coded(c->format))
             FO_CUDA(cudaMemset2DAsync(c->tail_scales + (size_t)tail_len * 4, (size_t)c->tail_stride * 4 * 2, 0,
@@ -1137,6 +1166,7 @@ static fo_decode_page make_page(const fo_kv_cache *c, const float *q, const floa
     p.last = c->prefix_len + c->tail_len;
     p.rows = rows;
     p.splits = (int32_t)((p.last + FO_SPLIT - 1) / FO_SPLIT);
+    p.rotated = (c->format & FO_KV_ROTATED) ? 1 : 0;
     return p;
 }
 

@@ -16,11 +16,50 @@
 #define FO_FLAG_PAIR 1u
 #define FO_FLAG_NONFINITE 2u
 #define FO_FLAG_OVERFLOW 4u
+#define FO_FLAG_ROTATED 8u  // a rotated block is no longer finite (kv.rs:289-293)
+
+// The record format's rotation flag (FO_KV_ROTATED of the C ABI).
+#define FO_KV_ROTATED_BIT 16
 
 namespace fo {
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// ---- rotation of 32-value blocks (src/quant/rotation.rs) ----
+// The sign pattern D of block kind k (0 temporal key half, 1 spatial key
+// half, 2 value 0..32, 3 value 32..64): the low 32 bits of SplitMix64's
+// output for the state SEED + (k + 1) * GAMMA, SEED = "KVROTATE" read
+// big-endian (rotation.rs:36-61).
+constexpr uint64_t splitmix64_out(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+constexpr uint32_t rotation_signs(int kind) {
+    return (uint32_t)splitmix64_out(0x4b56524f54415445ull + (uint64_t)(kind + 1) * 0x9e3779b97f4a7c15ull);
+}
+// The reference's own known answers (rotation.rs:163-166).
+static_assert(rotation_signs(0) == 0x04dcf6b7u && rotation_signs(1) == 0x871f5f8bu &&
+                  rotation_signs(2) == 0x489ce13cu && rotation_signs(3) == 0x4a81cbcbu,
+              "rotation sign words");
+
+// One stage of the Sylvester butterflies over elements held one per lane
+// group: element i pairs with i ^ half; the low one becomes a + b, the high
+// one a - b (a the low element, rotation.rs:71-84).  `partner` is the other
+// element, `high` whether this one is the high element.
+__device__ __forceinline__ float butterfly(float x, float partner, bool high) {
+    return high ? __fsub_rn(partner, x) : __fadd_rn(x, partner);
+}
+
+// x <- H D x for a block held one element per lane (lane = element index):
+// the stored form of a key or value block (rotation.rs:100-104).
+__device__ __forceinline__ float rotate_lane(float x, int kind, int lane) {
+    x = __uint_as_float(__float_as_uint(x) ^ (((rotation_signs(kind) >> lane) & 1u) << 31));
+#pragma unroll
+    for (int half = 1; half < 32; half <<= 1) x = butterfly(x, __shfl_xor_sync(0xffffffffu, x, half), lane & half);
+    return x;
+}
 
 __device__ __forceinline__ float bits_f32(uint32_t u) { return __uint_as_float(u); }
 __device__ __forceinline__ uint32_t f32_bits(float f) { return __float_as_uint(f); }
@@ -105,6 +144,30 @@ __device__ __forceinline__ void s8x2_f32(uint32_t w, float &lo, float &hi) {
                                 make_float2(-8388736.0f, -8388736.0f));
     lo = x.x;
     hi = x.y;
+}
+// The signed 4-bit codes of a byte (codec.rs:127-129: element 2i in the
+// low nibble), exactly: each nibble with its sign bit flipped is the code + 8,
+// placed in the mantissa of 2^23 and shifted back.
+__device__ __forceinline__ void s4x2_f32(uint32_t byte, float &lo, float &hi) {
+    const uint32_t u = byte ^ 0x88u;
+    const float2 x = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | (u & 0xFu)),
+                                            __uint_as_float(0x4B000000u | ((u >> 4) & 0xFu))),
+                                make_float2(-8388616.0f, -8388616.0f));
+    lo = x.x;
+    hi = x.y;
+}
+// The eight codes of w's four bytes in element order (byte k: 2k, 2k + 1).
+__device__ __forceinline__ void s4x8_f32(uint32_t w, float *f) {
+    const uint32_t u = w ^ 0x88888888u;
+    const uint32_t lo = u & 0x0F0F0F0Fu, hi = (u >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 x = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + k)),
+                                                __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + k))),
+                                    make_float2(-8388616.0f, -8388616.0f));
+        f[2 * k] = x.x;
+        f[2 * k + 1] = x.y;
+    }
 }
 // The two signed 16-bit halves of w.
 __device__ __forceinline__ void s16x2_f32(uint32_t w, float &lo, float &hi) {

@@ -92,6 +92,10 @@ struct alignas(64) fo_decode_page {
     // With prefix_splits set: splits per partial ("unit"), and `splits` counts
     // units per row and head (fo_tc_layout).
     int32_t chunk;
+    // Rotated records (FO_KV_ROTATED): the CUDA-core decode rotates each
+    // query head's halves as it loads them, the merge un-rotates each output
+    // head's halves before it stores them (kv.rs:83-96, 578-589).
+    int32_t rotated;
 };
 
 // The tensor-core decode's maps of BF16 records (decode_tc.cu) for page p

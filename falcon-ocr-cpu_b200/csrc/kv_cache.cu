@@ -7,15 +7,19 @@
 // `[T 32 | S(2g) 32 | S(2g+1) 32 | V 64]` lives at codes[(g * stride + t) * 160]
 // with its five BF16 block scales at scales[(g * stride + t) * 5]; tail
 // records `[K 64 | V 64]` at tail_codes[(g * tail_stride + i) * 128] with four
-// scales.  Codes are integers computed exactly as the reference does: the
-// f64 quotient value / scale rounded to nearest even and clamped, so they
-// match it bit for bit.
+// scales (element offsets: Q4 packs two codes per byte, element 2i in the
+// low nibble).  Codes are integers computed exactly as the reference does:
+// the f64 quotient value / scale rounded to nearest even and clamped, so they
+// match it bit for bit.  Rotated formats (FO_KV_ROTATED: Kv::Q8Rot, Kv::Q4Rot
+// and the rotated FP32 test storage) first rotate every 32-element block,
+// H D x (src/quant/rotation.rs:100-104), with the warp's lanes as the block's
+// elements: the sign flips, then the five butterfly stages across lanes.
 #include "fo_common.cuh"
 #include "fo_kernels.h"
 
 namespace fo {
 
-enum { KV_F32 = 0, KV_Q16 = 1, KV_Q8 = 2, KV_BF16 = 3 };
+enum { KV_F32 = 0, KV_Q16 = 1, KV_Q8 = 2, KV_BF16 = 3, KV_Q4 = 4, KV_ROTATED = 16 };
 
 // codec.rs:60-63 (clamp, then round half to even; |x| < 2^51).
 __device__ __forceinline__ double round_clamped(double x, double limit) {
@@ -44,6 +48,26 @@ __device__ __forceinline__ void encode_block(float x, int format, void *codes, u
     }
     if (format == KV_BF16) {
         reinterpret_cast<uint16_t *>(codes)[at + lane] = bf16_rne(x);
+        return;
+    }
+    if (format == KV_Q4) {
+        // codec.rs:87-122: absmax / 7, codes -7..7 packed two per byte
+        // (element 2i in the low nibble); a non-finite block gets a NaN scale.
+        const float mx = warp_max(fabsf(x));
+        const bool finite = __all_sync(0xffffffffu, isfinite(x));
+        const uint16_t stored = bf16_up(finite ? block_scale(mx, 7.0) : __uint_as_float(0x7FC00000u));
+        const float scale = bf16_f32(stored);
+        if (lane == 0) scales[at / 32] = stored;
+        int code = 0;
+        if (scale != 0.0f) {
+            const double r = round_clamped((double)x / (double)scale, 7.0);
+            code = isnan(r) ? 0 : (int)r;
+        }
+        const int high = __shfl_down_sync(0xffffffffu, code, 1);
+        if ((lane & 1) == 0)
+            reinterpret_cast<uint8_t *>(codes)[(at + lane) / 2] = (uint8_t)((code & 0xF) | ((high & 0xF) << 4));
+        // kv.rs:381-383: codes are at most 7 in magnitude
+        if (!nan_on_nonfinite && lane == 0 && !isfinite(7.0f * scale)) atomicOr(flags, FO_FLAG_OVERFLOW);
         return;
     }
     const bool q8 = format == KV_Q8;
@@ -95,9 +119,39 @@ __global__ void seal_kernel(const float *__restrict__ k, const float *__restrict
         if (lane == 0) atomicOr(flags, FO_FLAG_NONFINITE);
         return;
     }
+    if (format & KV_ROTATED) {
+        // kv.rs:289-293: every block rotated after the pair check (which saw
+        // the unrotated keys); kinds [T, S, S, V0, V1].
+        const int kinds[5] = {0, 1, 1, 2, 3};
+        ok = true;
+#pragma unroll
+        for (int b = 0; b < 5; b++) {
+            x[b] = rotate_lane(x[b], kinds[b], lane);
+            ok = ok && isfinite(x[b]);
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicOr(flags, FO_FLAG_ROTATED);
+            return;
+        }
+    }
     const int64_t base = (g * stride + t) * FO_RECORD;
 #pragma unroll
-    for (int b = 0; b < 5; b++) encode_block(x[b], format, codes, scales, base + 32 * b, false, flags);
+    for (int b = 0; b < 5; b++) encode_block(x[b], format & ~KV_ROTATED, codes, scales, base + 32 * b, false, flags);
+}
+
+// Tail record blocks [K 0..32 | K 32..64 | V 0..32 | V 32..64] (one value per
+// lane each): rotated when the format is (kv.rs:466-468, kinds T, S, V0, V1),
+// then encoded with the tail's rule for non-finite blocks.
+__device__ __forceinline__ void encode_tail_record(float k0, float k1, float v0, float v1, int format,
+                                                   void *tail_codes, uint16_t *tail_scales, int64_t base, int lane) {
+    float x[4] = {k0, k1, v0, v1};
+    if (format & KV_ROTATED) {
+#pragma unroll
+        for (int b = 0; b < 4; b++) x[b] = rotate_lane(x[b], b, lane);
+    }
+#pragma unroll
+    for (int b = 0; b < 4; b++)
+        encode_block(x[b], format & ~KV_ROTATED, tail_codes, tail_scales, base + 32 * b, true, nullptr);
 }
 
 // Tail record `first + r` of group g from expanded row r: the group's first
@@ -108,10 +162,7 @@ __device__ __forceinline__ void append_record(const float *__restrict__ k, const
     const float *kr = k + (r * heads + 2 * g) * FO_HD;
     const float *vr = v + (r * heads + 2 * g) * FO_HD;
     const int64_t base = (g * tail_stride + first + r) * FO_TAIL_RECORD;
-    encode_block(kr[lane], format, tail_codes, tail_scales, base, true, nullptr);
-    encode_block(kr[32 + lane], format, tail_codes, tail_scales, base + 32, true, nullptr);
-    encode_block(vr[lane], format, tail_codes, tail_scales, base + 64, true, nullptr);
-    encode_block(vr[32 + lane], format, tail_codes, tail_scales, base + 96, true, nullptr);
+    encode_tail_record(kr[lane], kr[32 + lane], vr[lane], vr[32 + lane], format, tail_codes, tail_scales, base, lane);
 }
 
 // One warp per (row, group) tail record.
@@ -243,10 +294,8 @@ __global__ void qkv_append_kernel(const float *__restrict__ qkv, const float *__
     const float b0 = __shfl_sync(0xffffffffu, yk.x, 16 + sl), b1 = __shfl_sync(0xffffffffu, yk.y, 16 + sl);
     const float *vr = src + qdim + kdim + g * FO_HD;
     const int64_t base = ((int64_t)g * tail_stride + first + r) * FO_TAIL_RECORD;
-    encode_block((lane & 1) ? a1 : a0, format, tail_codes, tail_scales, base, true, nullptr);
-    encode_block((lane & 1) ? b1 : b0, format, tail_codes, tail_scales, base + 32, true, nullptr);
-    encode_block(vr[lane], format, tail_codes, tail_scales, base + 64, true, nullptr);
-    encode_block(vr[32 + lane], format, tail_codes, tail_scales, base + 96, true, nullptr);
+    encode_tail_record((lane & 1) ? a1 : a0, (lane & 1) ? b1 : b0, vr[lane], vr[32 + lane], format, tail_codes,
+                       tail_scales, base, lane);
 }
 
 // FP32 -> BF16, eight values per thread (16-byte stores).

@@ -27,8 +27,11 @@ LIB_PATH = os.path.join(HERE, "lib", "libfo_cuda.so")
 
 OK, ERR_INVALID, ERR_PAIR, ERR_NONFINITE, ERR_OVERFLOW, ERR_CAPACITY, ERR_CUDA, ERR_DECLINED = range(8)
 MEM_DEVICE, MEM_HOST = 0, 1
-KV_F32, KV_Q16, KV_Q8, KV_BF16 = 0, 1, 2, 3
-KV_FORMATS = {"f32": KV_F32, "q16": KV_Q16, "q8": KV_Q8, "bf16": KV_BF16}
+KV_F32, KV_Q16, KV_Q8, KV_BF16, KV_Q4 = 0, 1, 2, 3, 4
+KV_ROTATED = 16  # flag: blocks stored rotated (src/quant/rotation.rs); with F32, Q8, Q4
+KV_Q8_ROT, KV_Q4_ROT = KV_Q8 | KV_ROTATED, KV_Q4 | KV_ROTATED  # Kv::Q8Rot, Kv::Q4Rot
+KV_FORMATS = {"f32": KV_F32, "q16": KV_Q16, "q8": KV_Q8, "bf16": KV_BF16, "q4": KV_Q4, "q8r": KV_Q8_ROT,
+              "q4r": KV_Q4_ROT, "f32r": KV_F32 | KV_ROTATED}
 EXP_EXACT, EXP_FAST = 0, 1
 SOFTMAX_ONLINE, SOFTMAX_STATIC = 0, 1
 

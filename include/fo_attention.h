@@ -81,11 +81,22 @@ typedef enum {
 #define FO_MEM_DEVICE 0
 #define FO_MEM_HOST 1
 
-/* Split-cache record formats (src/quant/kv.rs:120-127; BF16 is new). */
+/* Split-cache record formats (src/quant/kv.rs:98-152; BF16 is new). */
 #define FO_KV_F32 0
 #define FO_KV_Q16 1
 #define FO_KV_Q8 2
 #define FO_KV_BF16 3
+/* 4-bit codes -7..7, two per byte (element 2i in the low nibble), one BF16
+ * scale per 32 elements (Records::Q4, kv.rs:109-114). */
+#define FO_KV_Q4 4
+/* Flag: every 32-element block of a record is stored rotated, H D x with H
+ * the 32-point Sylvester Hadamard matrix and D a fixed sign pattern per
+ * block kind (src/quant/rotation.rs); decode rotates each query head's
+ * halves and un-rotates each output head's halves.  Valid with F32, Q8 and
+ * Q4. */
+#define FO_KV_ROTATED 16
+#define FO_KV_Q8_ROT (FO_KV_Q8 | FO_KV_ROTATED) /* Kv::Q8Rot */
+#define FO_KV_Q4_ROT (FO_KV_Q4 | FO_KV_ROTATED) /* Kv::Q4Rot */
 
 /* ExpMode / PrefillSoftmax (src/kernels/attention/mod.rs:204-221). */
 #define FO_EXP_EXACT 0

@@ -678,6 +678,107 @@ void fo_or_prefill_bf16(const float *q, const float *k, const float *v, int64_t 
 }
 
 /* ------------------------------------------------------------------ */
+/* rotation of 32-value blocks: src/quant/rotation.rs                   */
+/* ------------------------------------------------------------------ */
+/* SplitMix64's output function (rotation.rs:36-40). */
+static uint64_t splitmix64_mix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+/* rotation.rs:42-61: the low 32 bits of the SplitMix64 outputs for states
+ * SEED + (kind + 1) * GAMMA, SEED = "KVROTATE" read big-endian. */
+uint32_t fo_or_rotation_signs(int kind) {
+    const uint64_t seed = 0x4b56524f54415445ull; /* 'K' 'V' 'R' 'O' 'T' 'A' 'T' 'E' */
+    const uint64_t gamma = 0x9e3779b97f4a7c15ull;
+    return (uint32_t)splitmix64_mix(seed + (uint64_t)(kind + 1) * gamma);
+}
+
+/* rotation.rs:71-84: five stages of FP32 butterflies, half = 1, 2, .., 16;
+ * x[i] = a + b, x[i + half] = a - b. */
+void fo_or_fwht32(float *x) {
+    for (int half = 1; half < 32; half *= 2)
+        for (int start = 0; start < 32; start += 2 * half)
+            for (int i = start; i < start + half; i++) {
+                const float a = x[i], b = x[i + half];
+                x[i] = a + b;
+                x[i + half] = a - b;
+            }
+}
+
+/* rotation.rs:87-92: sign-bit flips (exact, NaN included). */
+static void flip32(float *x, uint32_t signs) {
+    for (int i = 0; i < 32; i++) {
+        uint32_t u;
+        memcpy(&u, &x[i], 4);
+        u ^= ((signs >> i) & 1u) << 31;
+        memcpy(&x[i], &u, 4);
+    }
+}
+
+static void scale32(float *x) {
+    for (int i = 0; i < 32; i++) x[i] *= 1.0f / 32.0f;
+}
+
+void fo_or_rotate(float *x, int kind) {
+    flip32(x, fo_or_rotation_signs(kind));
+    fo_or_fwht32(x);
+}
+
+void fo_or_rotate_query(float *x, int kind) {
+    fo_or_rotate(x, kind);
+    scale32(x);
+}
+
+void fo_or_unrotate(float *x, int kind) {
+    fo_or_fwht32(x);
+    flip32(x, fo_or_rotation_signs(kind));
+    scale32(x);
+}
+
+/* Block kinds of a prefix record [T | S | S | V0 | V1] and of a tail record
+ * [T | S | V0 | V1] (kv.rs:72-81). */
+static const int RECORD_KINDS[5] = {0, 1, 1, 2, 3};
+static const int TAIL_KINDS[4] = {0, 1, 2, 3};
+
+static int all_finite_block(const float *x) {
+    for (int i = 0; i < 32; i++)
+        if (!isfinite(x[i])) return 0;
+    return 1;
+}
+
+/* ---- Q4 codec (codec.rs:87-129) ---- */
+static float q4_scale(const float *values) {
+    float max = absmax(values, 32);
+    if (max == 0.0f) return 0.0f;
+    float s = (float)((double)max / 7.0);
+    float tiny = from_bits(1);
+    return s > tiny ? s : tiny;
+}
+
+/* codec.rs:98-104 */
+static int8_t q4_code(float value, float scale) {
+    if (scale == 0.0f) return 0;
+    return (int8_t)rust_as_int(fo_or_round_clamped((double)value / (double)scale, 7.0));
+}
+
+/* codec.rs:110-122 */
+uint16_t fo_or_q4_block(const float *values, uint8_t *codes) {
+    const uint16_t stored = fo_or_bf16_up(all_finite_block(values) ? q4_scale(values) : NAN);
+    const float scale = fo_or_bf16_f32(stored);
+    for (int i = 0; i < 16; i++)
+        codes[i] = (uint8_t)(((uint8_t)q4_code(values[2 * i], scale) & 0x0F) |
+                             ((uint8_t)q4_code(values[2 * i + 1], scale) << 4));
+    return stored;
+}
+
+/* codec.rs:127-129: the signed nibble (high 0: bits 0..4, 1: bits 4..8). */
+int8_t fo_or_nibble(uint8_t byte, int high) {
+    return (int8_t)((int8_t)(uint8_t)(byte << (4 - 4 * high)) >> 4);
+}
+
+/* ------------------------------------------------------------------ */
 /* split cache: src/quant/kv.rs, src/quant/kv/decode.rs                 */
 /* ------------------------------------------------------------------ */
 static inline int all_finite(const float *x, int64_t n) {
@@ -718,6 +819,16 @@ static int encode_block(const float *values, int format, void *codes, uint16_t *
         }
         return FO_OR_OK;
     }
+    case FO_OR_Q4: {
+        /* kv.rs:374-385 (prefix: codes at most 7, so 7 * scale bounds them)
+         * and kv.rs:503-508 (tail: a non-finite block gets a NaN scale) */
+        float block[32];
+        memcpy(block, values, sizeof block);
+        if (!nonfinite_to_nan && !all_finite_block(block)) return FO_OR_ERR_NONFINITE;
+        scales[at / 32] = fo_or_q4_block(block, (uint8_t *)codes + at / 2);
+        if (!nonfinite_to_nan && !isfinite(7.0f * fo_or_bf16_f32(scales[at / 32]))) return FO_OR_ERR_OVERFLOW;
+        return FO_OR_OK;
+    }
     }
     return FO_OR_ERR_SHAPE;
 }
@@ -749,8 +860,17 @@ int fo_or_kv_seal(const float *k, const float *v, int64_t prefix_len, int64_t ca
             status = status > FO_OR_ERR_NONFINITE ? status : FO_OR_ERR_NONFINITE;
             continue;
         }
+        /* kv.rs:289-293: rotated storage rotates every block after the pair
+         * check (which saw the unrotated keys) and refuses an overflow */
+        if (format & FO_OR_ROTATED) {
+            for (int blk = 0; blk < RECORD / 32; blk++) fo_or_rotate(dst + 32 * blk, RECORD_KINDS[blk]);
+            if (!all_finite(dst, RECORD)) {
+                status = status > FO_OR_ERR_ROTATED ? status : FO_OR_ERR_ROTATED;
+                continue;
+            }
+        }
         for (int blk = 0; blk < RECORD / 32; blk++) {
-            int e = encode_block(dst + 32 * blk, format, codes, scales, record * RECORD + 32 * blk, 0);
+            int e = encode_block(dst + 32 * blk, format & ~FO_OR_ROTATED, codes, scales, record * RECORD + 32 * blk, 0);
             if (e > status) status = e;
         }
     }
@@ -765,8 +885,11 @@ void fo_or_kv_push(const float *k_unique, const float *v_unique, int64_t groups,
         memcpy(values, k_unique + g * 64, 64 * sizeof(float));
         memcpy(values + 64, v_unique + g * 64, 64 * sizeof(float));
         int64_t record = g * tail_capacity + index;
+        if (format & FO_OR_ROTATED) /* kv.rs:466-468 */
+            for (int blk = 0; blk < TAIL_RECORD / 32; blk++) fo_or_rotate(values + 32 * blk, TAIL_KINDS[blk]);
         for (int blk = 0; blk < TAIL_RECORD / 32; blk++)
-            encode_block(values + 32 * blk, format, tail_codes, tail_scales, record * TAIL_RECORD + 32 * blk, 1);
+            encode_block(values + 32 * blk, format & ~FO_OR_ROTATED, tail_codes, tail_scales,
+                         record * TAIL_RECORD + 32 * blk, 1);
     }
 }
 
@@ -774,7 +897,8 @@ void fo_or_kv_push(const float *k_unique, const float *v_unique, int64_t groups,
 float fo_or_kv_value(const void *codes, const uint16_t *scales, int format, int64_t width, int64_t record,
                      int64_t offset) {
     int64_t at = record * width + offset;
-    switch (format) {
+    switch (format & ~FO_OR_ROTATED) {
+    case FO_OR_Q4: return (float)fo_or_nibble(((const uint8_t *)codes)[at / 2], (int)(at % 2)) * fo_or_bf16_f32(scales[at / 32]);
     case FO_OR_F32: return ((const float *)codes)[at];
     case FO_OR_BF16: return fo_or_bf16_f32(((const uint16_t *)codes)[at]);
     case FO_OR_Q8: return (float)((const int8_t *)codes)[at] * fo_or_bf16_f32(scales[at / 32]);
@@ -928,8 +1052,28 @@ void fo_or_kv_decode_rows(const void *codes, const uint16_t *scales, const void 
     store_t st = {codes, tail_codes, scales, tail_scales, format, prefix_len, tail_capacity};
     int64_t last = prefix_len + tail_len;
     int64_t width = heads * 64;
-    for (int64_t r = 0; r < rows; r++)
-        decode_one(&st, last + 1 + r - rows, heads, groups, q + r * width, sinks, chunks, fast_exp, out + r * width);
+    const int rotated = (format & FO_OR_ROTATED) != 0;
+    float *qr = rotated ? (float *)malloc((size_t)width * sizeof(float)) : NULL;
+    for (int64_t r = 0; r < rows; r++) {
+        const float *qq = q + r * width;
+        if (rotated) {
+            /* kv.rs:83-96, 578-589: every head's query halves rotated
+             * (rotate_query), the output's value halves un-rotated */
+            memcpy(qr, qq, (size_t)width * sizeof(float));
+            for (int64_t h = 0; h < heads; h++) {
+                fo_or_rotate_query(qr + h * 64, 0);
+                fo_or_rotate_query(qr + h * 64 + 32, 1);
+            }
+            qq = qr;
+        }
+        decode_one(&st, last + 1 + r - rows, heads, groups, qq, sinks, chunks, fast_exp, out + r * width);
+        if (rotated)
+            for (int64_t h = 0; h < heads; h++) {
+                fo_or_unrotate(out + r * width + h * 64, 2);
+                fo_or_unrotate(out + r * width + h * 64 + 32, 3);
+            }
+    }
+    free(qr);
 }
 
 /* ------------------------------------------------------- fused QKV rows */

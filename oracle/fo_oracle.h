@@ -26,6 +26,12 @@ extern "C" {
 #define FO_OR_Q16 1
 #define FO_OR_Q8 2
 #define FO_OR_BF16 3 /* new in this build: BF16 records, no scales */
+#define FO_OR_Q4 4   /* 4-bit codes -7..7, two per byte (element 2i low), BF16 scale per 32 (kv.rs:109-114) */
+/* Flag: every 32-element block stored rotated, H D x (src/quant/rotation.rs,
+ * kv.rs:128-152); with F32, Q8 or Q4.  Q8|ROTATED is Kv::Q8Rot and
+ * Q4|ROTATED Kv::Q4Rot; rotated F32 and unrotated Q4 are the reference's
+ * test storages. */
+#define FO_OR_ROTATED 16
 
 /* ---- seal / append status codes (src/quant/kv.rs:248-295) ---- */
 #define FO_OR_OK 0
@@ -34,6 +40,19 @@ extern "C" {
 #define FO_OR_ERR_OVERFLOW 3  /* code * scale overflowed */
 #define FO_OR_ERR_SHAPE 4     /* head_dim/heads/groups not Falcon's paired GQA */
 #define FO_OR_ERR_CAPACITY 5  /* prefix_len == 0 or capacity < prefix_len */
+#define FO_OR_ERR_ROTATED 6   /* a rotated block is no longer finite (kv.rs:290-293) */
+
+/* Randomized Hadamard rotation of 32-value blocks (src/quant/rotation.rs).
+ * kind: 0 temporal key half, 1 spatial key half, 2 value 0..32, 3 value
+ * 32..64.  signs(kind) is D's bit pattern (bit i set: element i negated). */
+uint32_t fo_or_rotation_signs(int kind);
+void fo_or_fwht32(float *x);                    /* x <- H x, Sylvester order */
+void fo_or_rotate(float *x, int kind);          /* x <- H D x (stored form) */
+void fo_or_rotate_query(float *x, int kind);    /* x <- 2^-5 H D x */
+void fo_or_unrotate(float *x, int kind);        /* x <- 2^-5 D H x */
+/* Q4 codec (codec.rs:87-129): the block's BF16 scale bits; codes packed. */
+uint16_t fo_or_q4_block(const float *values, uint8_t *codes);
+int8_t fo_or_nibble(uint8_t byte, int high);
 
 /* codec (src/quant/kv/codec.rs) */
 uint16_t fo_or_bf16_up(float scale);

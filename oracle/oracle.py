@@ -21,12 +21,17 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 
-F32, Q16, Q8, BF16 = 0, 1, 2, 3
-FORMATS = {"f32": F32, "q16": Q16, "q8": Q8, "bf16": BF16}
-# Record codes dtype per format (src/quant/kv.rs:98-118; BF16 is new here).
-CODE_DTYPES = {F32: np.float32, Q16: np.int16, Q8: np.int8, BF16: np.uint16}
+F32, Q16, Q8, BF16, Q4 = 0, 1, 2, 3, 4
+# Flag: every 32-element block stored rotated (src/quant/rotation.rs); with
+# F32, Q8 or Q4.  Q8 | ROTATED is Kv::Q8Rot, Q4 | ROTATED Kv::Q4Rot.
+ROTATED = 16
+FORMATS = {"f32": F32, "q16": Q16, "q8": Q8, "bf16": BF16, "q4": Q4, "q8r": Q8 | ROTATED, "q4r": Q4 | ROTATED,
+           "f32r": F32 | ROTATED}
+# Record codes dtype per element format (src/quant/kv.rs:98-118; BF16 is
+# new here); Q4 packs two codes per byte.
+CODE_DTYPES = {F32: np.float32, Q16: np.int16, Q8: np.int8, BF16: np.uint16, Q4: np.uint8}
 
-OK, ERR_PAIR, ERR_NONFINITE, ERR_OVERFLOW, ERR_SHAPE, ERR_CAPACITY = range(6)
+OK, ERR_PAIR, ERR_NONFINITE, ERR_OVERFLOW, ERR_SHAPE, ERR_CAPACITY, ERR_ROTATED = range(7)
 
 RECORD, TAIL_RECORD = 160, 128
 
@@ -77,6 +82,13 @@ def lib() -> ctypes.CDLL:
         "fo_or_kv_value": (F, [P, P, I, I64, I64, I64]),
         "fo_or_kv_decode_rows": (None, [P, P, P, P, I] + [I64] * 5 + [P, I64, P, I64, I, P]),
         "fo_or_qkv_rows": (None, [P, P, I64, I64, I64, P, P, P]),
+        "fo_or_rotation_signs": (ctypes.c_uint32, [I]),
+        "fo_or_fwht32": (None, [P]),
+        "fo_or_rotate": (None, [P, I]),
+        "fo_or_rotate_query": (None, [P, I]),
+        "fo_or_unrotate": (None, [P, I]),
+        "fo_or_q4_block": (ctypes.c_uint16, [P, P]),
+        "fo_or_nibble": (ctypes.c_int8, [ctypes.c_uint8, I]),
         "fo_or_set_threads": (None, [I]),
         "fo_or_max_threads": (I, []),
     }
@@ -196,6 +208,44 @@ def prefill_bf16(q, k, v, n_heads, n_kv_heads, image, sinks, softmax_static=True
 
 
 # ---------------------------------------------------------- split cache
+def rotation_signs(kind: int) -> int:
+    """D's bit pattern of block kind 0..3 (rotation.rs:42-61)."""
+    return int(lib().fo_or_rotation_signs(int(kind)))
+
+
+def _block_op(name, x, kind):
+    x = _f32(x).copy()
+    assert x.size == 32
+    getattr(lib(), name)(_p(x), int(kind))
+    return x
+
+
+def fwht32(x):
+    x = _f32(x).copy()
+    lib().fo_or_fwht32(_p(x))
+    return x
+
+
+def rotate(x, kind):
+    return _block_op("fo_or_rotate", x, kind)
+
+
+def rotate_query(x, kind):
+    return _block_op("fo_or_rotate_query", x, kind)
+
+
+def unrotate(x, kind):
+    return _block_op("fo_or_unrotate", x, kind)
+
+
+def q4_block(values):
+    """(BF16 scale bits, 16 packed code bytes) of one 32-value block."""
+    values = _f32(values)
+    codes = np.zeros(16, np.uint8)
+    bits = lib().fo_or_q4_block(_p(values), _p(codes))
+    return int(bits), codes
+
+
 def qkv_rows(qkv, rope, rows, heads=16, groups=8):
     """fo_or_qkv_rows: the fused split + per-head RMS norm + RoPE of the
     projection rows (src/model/fused.rs:96-116).  Returns q, k [rows][heads][64]
@@ -214,16 +264,18 @@ class SplitCache:
 
     def __init__(self, k, v, prefix_len, capacity, heads=16, groups=8, fmt=F32, chunks=None, fast_exp=False):
         self.fmt = fmt if isinstance(fmt, int) else FORMATS[fmt]
+        self.element, self.rotated = self.fmt & ~ROTATED, bool(self.fmt & ROTATED)
         self.prefix_len, self.capacity, self.heads, self.groups = prefix_len, capacity, heads, groups
         self.tail_capacity = capacity - prefix_len
         self.tail_len = 0
         # default_chunks (kv.rs:188-197): F32 one scan, coded caches four.
-        self.chunks = chunks if chunks else (1 if self.fmt in (F32,) else 4)
+        self.chunks = chunks if chunks else (1 if self.element in (F32,) else 4)
         self.fast_exp = bool(fast_exp)
-        dt = CODE_DTYPES[self.fmt]
-        self.codes = np.zeros(max(groups * prefix_len * RECORD, 1), dt)
+        dt = CODE_DTYPES[self.element]
+        per = 2 if self.element == Q4 else 1  # codes per stored element
+        self.codes = np.zeros(max(groups * prefix_len * RECORD // per, 1), dt)
         self.scales = np.zeros(max(groups * prefix_len * 5, 1), np.uint16)
-        self.tail_codes = np.zeros(max(groups * self.tail_capacity * TAIL_RECORD, 1), dt)
+        self.tail_codes = np.zeros(max(groups * self.tail_capacity * TAIL_RECORD // per, 1), dt)
         self.tail_scales = np.zeros(max(groups * self.tail_capacity * 4, 1), np.uint16)
         k, v = _f32(k), _f32(v)
         self.status = lib().fo_or_kv_seal(_p(k), _p(v), prefix_len, capacity, heads, groups, 64, self.fmt,
@@ -284,7 +336,14 @@ class SplitCache:
 
 
 def decode_records(codes, scales, fmt):
-    """Vectorised kv.rs:209-219: fl(code * bf16 scale)."""
+    """Vectorised kv.rs:209-219: fl(code * bf16 scale) (rotated records stay
+    in the rotated basis)."""
+    fmt &= ~ROTATED
+    if fmt == Q4:
+        lo = ((codes.astype(np.uint8) << 4).view(np.int8) >> 4).astype(np.int8)
+        hi = (codes.view(np.int8) >> 4).astype(np.int8)
+        codes = np.stack([lo, hi], axis=-1).reshape(-1)
+        fmt = Q8
     if fmt == F32:
         return codes.astype(np.float32)
     if fmt == BF16:

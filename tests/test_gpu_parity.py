@@ -140,7 +140,10 @@ def test_baseline_c1_causal_fp32(ctx):
 
 
 # -------------------------------------------------------------- split cache
-FORMATS = [F.KV_F32, F.KV_Q16, F.KV_Q8, F.KV_BF16]
+# The element formats, the rotated research formats (Q8Rot, Q4Rot) and the
+# reference's test storages (unrotated Q4, rotated FP32).
+FORMATS = [F.KV_F32, F.KV_Q16, F.KV_Q8, F.KV_BF16, F.KV_Q4, F.KV_Q8_ROT, F.KV_Q4_ROT, F.KV_F32 | F.KV_ROTATED]
+CODED = (F.KV_Q16, F.KV_Q8, F.KV_Q4)
 
 
 def sealed_pair(fmt, p, generated, seed, capacity=None, key_scale=None):
@@ -169,9 +172,11 @@ def d2h(ptr, n, dtype):
 
 def device_records(gpu, fmt, groups):
     (codes, scales, tcodes, tscales), ps, ts = gpu.records()
-    dt = {F.KV_F32: np.float32, F.KV_Q16: np.int16, F.KV_Q8: np.int8, F.KV_BF16: np.uint16}[fmt]
-    out = {"codes": d2h(codes, groups * ps * 160, dt), "tail": d2h(tcodes, groups * max(ts, 1) * 128, dt)}
-    if fmt in (F.KV_Q16, F.KV_Q8):
+    element = fmt & ~F.KV_ROTATED
+    dt = {F.KV_F32: np.float32, F.KV_Q16: np.int16, F.KV_Q8: np.int8, F.KV_BF16: np.uint16, F.KV_Q4: np.uint8}[element]
+    per = 2 if element == F.KV_Q4 else 1  # Q4: two codes per byte
+    out = {"codes": d2h(codes, groups * ps * 160 // per, dt), "tail": d2h(tcodes, groups * max(ts, 1) * 128 // per, dt)}
+    if element in CODED:
         out["scales"] = d2h(scales, groups * ps * 5, np.uint16)
         out["tail_scales"] = d2h(tscales, groups * max(ts, 1) * 4, np.uint16)
     return out
@@ -186,10 +191,11 @@ def test_seal_and_append_are_bit_exact(ctx, fmt, p, generated):
     recs = device_records(gpu, fmt, 8)
     bits = lambda x: x.view(np.uint32) if x.dtype == np.float32 else x  # noqa: E731
     assert np.array_equal(bits(recs["codes"]), bits(ref.codes))
-    ta = recs["tail"].reshape(8, -1, 128)[:, :generated]
-    tb = ref.tail_codes.reshape(8, -1, 128)[:, :generated]
+    width = 64 if fmt & ~F.KV_ROTATED == F.KV_Q4 else 128  # stored elements per tail record
+    ta = recs["tail"].reshape(8, -1, width)[:, :generated]
+    tb = ref.tail_codes.reshape(8, -1, width)[:, :generated]
     assert np.array_equal(bits(np.ascontiguousarray(ta)), bits(np.ascontiguousarray(tb)))
-    if fmt in (F.KV_Q16, F.KV_Q8):
+    if fmt & ~F.KV_ROTATED in CODED:
         assert np.array_equal(recs["scales"], ref.scales)
         assert np.array_equal(recs["tail_scales"].reshape(8, -1, 4)[:, :generated],
                               ref.tail_scales.reshape(8, -1, 4)[:, :generated])
@@ -222,13 +228,14 @@ def test_append_batch_equals_per_page_appends(ctx, fmt):
         F.append_batch(batched, ks, vs, rows)
     torch.cuda.synchronize()
     bits = lambda x: x.view(np.uint32) if x.dtype == np.float32 else x  # noqa: E731
+    width = 64 if fmt & ~F.KV_ROTATED == F.KV_Q4 else 128
     for a, b in zip(singles, batched):
         assert a.tail_len == b.tail_len == 5
         ra, rb = device_records(a, fmt, 8), device_records(b, fmt, 8)
-        ta = np.ascontiguousarray(ra["tail"].reshape(8, -1, 128)[:, :5])
-        tb = np.ascontiguousarray(rb["tail"].reshape(8, -1, 128)[:, :5])
+        ta = np.ascontiguousarray(ra["tail"].reshape(8, -1, width)[:, :5])
+        tb = np.ascontiguousarray(rb["tail"].reshape(8, -1, width)[:, :5])
         assert np.array_equal(bits(ta), bits(tb))
-        if fmt in (F.KV_Q16, F.KV_Q8):
+        if fmt & ~F.KV_ROTATED in CODED:
             assert np.array_equal(ra["tail_scales"].reshape(8, -1, 4)[:, :5], rb["tail_scales"].reshape(8, -1, 4)[:, :5])
     # one cache without room: nothing is written anywhere
     x = dev(np.zeros(8 * 16 * 64, np.float32))
@@ -257,7 +264,7 @@ def step_rows(rng, n):
     return kv, q
 
 
-@pytest.mark.parametrize("fmt", [F.KV_BF16, F.KV_Q8])
+@pytest.mark.parametrize("fmt", [F.KV_BF16, F.KV_Q8, F.KV_Q4_ROT])
 def test_batch_plan_equals_per_step_calls(ctx, fmt):
     """fo_kv_plan_step (append + one-row decode per page from device-resident
     descriptors) gives, step by step, the outputs of fo_kv_append_batch +
@@ -289,7 +296,8 @@ def test_batch_plan_equals_per_step_calls(ctx, fmt):
     for x, y in zip(a, b):
         assert x.tail_len == y.tail_len == 5
         rx, ry = device_records(x, fmt, 8), device_records(y, fmt, 8)
-        assert np.array_equal(rx["tail"].reshape(8, -1, 128)[:, :5], ry["tail"].reshape(8, -1, 128)[:, :5])
+        width = 64 if fmt & ~F.KV_ROTATED == F.KV_Q4 else 128
+        assert np.array_equal(rx["tail"].reshape(8, -1, width)[:, :5], ry["tail"].reshape(8, -1, width)[:, :5])
     for c in a + b:
         c.close()
 
@@ -499,6 +507,38 @@ def test_truncated_tails_take_new_positions_like_fresh_ones(ctx, fmt):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+def test_research_formats_stay_close_to_fp32(ctx):
+    """src/quant/kv/tests.rs:282-304 on the GPU: Q8Rot within 0.02 and Q4Rot
+    within 0.05 of the compact FP32 attention (the golden output)."""
+    p = 257
+    k, v, q = G.kv_fixture(p, 9)
+    tail = np.full(16 * 64, 0.02, np.float32)
+    for fmt, bound in (("q8r", 0.02), ("q4r", 0.05)):
+        gpu = F.SplitPrefix.from_compact(k, v, p, p + 1, fmt=fmt)
+        gpu.append(tail, tail)
+        out = np.zeros(1024, np.float32)
+        gpu.attention_decode(q, p + 1, np.full(16, 0.5, np.float32), out)
+        assert np.isfinite(out).all()
+        assert np.all(np.abs(out - GOLD["kv_lowprec_expected"]) < bound), fmt
+
+
+def test_rotated_seal_refuses_pairs_and_overflow(ctx):
+    """kv/tests.rs:355-369 and kv.rs:289-293: the pair check sees the
+    unrotated keys; a block whose rotation overflows is refused."""
+    k = np.zeros(16 * 64, np.float32)
+    v = np.zeros(8 * 64, np.float32)
+    k[64] = 1.0
+    with pytest.raises(F.PairError):
+        F.SplitPrefix.from_compact(k, v, 1, 2, fmt="q8r")
+    k[64] = 0.0
+    k[:32] = k[64:96] = np.arange(32, dtype=np.float32)
+    F.SplitPrefix.from_compact(k, v, 1, 2, fmt="q8r").close()
+    with pytest.raises(F.FoError, match="rotated KV group overflows"):
+        F.SplitPrefix.from_compact(np.full(16 * 64, 3e37, np.float32), v, 1, 2, fmt="q4r")
+    with pytest.raises(F.FoError):
+        F.SplitPrefix.from_compact(k, v, 1, 2, fmt=F.KV_BF16 | F.KV_ROTATED)
+
+
 def test_decode_errors(ctx):
     k, v, q = G.kv_fixture(10, 1)
     gpu = F.SplitPrefix.from_compact(k, v, 10, 12, fmt="q8")
@@ -541,12 +581,13 @@ def test_baseline_c3_verify_rows(ctx, fmt, length):
     close(out, ref.decode_rows(q, 5, sinks), 1e-5, 1e-5)
 
 
-def test_batch_decode_equals_single_pages(ctx):
+@pytest.mark.parametrize("fmt", ["q8", "q8r", "q4r"])
+def test_batch_decode_equals_single_pages(ctx, fmt):
     """Page-parallel decode (call stack D): each page equals its own decode."""
     caches, qs, ss, outs, singles = [], [], [], [], []
     for i, p in enumerate([300, 1000, 17, 2049]):
         k, v, q = G.kv_fixture(p, 3 + i)
-        c = F.SplitPrefix.from_compact(dev(k), dev(v), p, p + 1, fmt="q8")
+        c = F.SplitPrefix.from_compact(dev(k), dev(v), p, p + 1, fmt=fmt)
         caches.append(c)
         qs.append(dev(q))
         ss.append(dev(np.full(16, 0.3 * i, np.float32)))

@@ -53,7 +53,7 @@ def both(cache, fmt, rows, stream=None):
     return got, expected
 
 
-@pytest.mark.parametrize("fmt", ["q8", "q16", "f32", "bf16"])
+@pytest.mark.parametrize("fmt", ["q8", "q16", "f32", "bf16", "q4", "q8r", "q4r"])
 def test_static_scratch_decode_equals_decode_rows_twice(fmt):
     """Two calls in a row (a long cache with 5 rows, then a short one with 2
     rows, which runs over the array the first call left behind), each equal
