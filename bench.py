@@ -49,7 +49,11 @@ FLOP_PER_CALL = 4 * 64 * VISIBLE_PAIRS * HEADS  # QK and PV multiply-adds, 2 FLO
 DECODE_L, DECODE_ROWS = 16384, 5
 SHARDED_T = 16384  # C5b page
 C4_L, C4_PAGES = 16384, 8
-RECORD_BYTES = {"bf16": 8 * 160 * 2, "f32": 8 * 160 * 4}  # per position, all groups (tail records are smaller)
+# Prefix record bytes per position, all groups, codes and BF16 scales (tail
+# records are smaller: TAIL_BYTES per group).
+RECORD_BYTES = {"bf16": 8 * 160 * 2, "f32": 8 * 160 * 4, "q8": 8 * (160 + 10), "q8r": 8 * (160 + 10),
+                "q4r": 8 * (80 + 10)}
+TAIL_BYTES = {"bf16": 256, "f32": 512, "q8": 136, "q8r": 136, "q4r": 72}
 
 
 def load_peaks():
@@ -579,7 +583,9 @@ def time_sharded(run, args):
 
 def time_decode(run, args, lengths=(DECODE_L,)):
     """5-row verify decode over BF16 and FP32 records at each cache length,
-    rotating distinct caches (together more than 4x L2).  The K calls are
+    and over the 8-bit, rotated 8-bit and rotated 4-bit records (Kv::Q8,
+    Kv::Q8Rot, Kv::Q4Rot) at DECODE_L, rotating distinct caches (together
+    more than 4x L2).  The K calls are
     captured once in a CUDA graph on the caches' own stream and replayed, so
     the device time is not bounded by the Python launch path (a serving loop
     replays a graph the same way).  Returns {length: {format: line}}."""
@@ -590,7 +596,10 @@ def time_decode(run, args, lengths=(DECODE_L,)):
     dctx = F.Context(run.local, stream=stream.cuda_stream)
     l2 = getattr(torch.cuda.get_device_properties(run.dev), "L2_cache_size", 126 << 20) or (126 << 20)
     res = {}
-    for length, fmt in [(n, f) for n in lengths for f in ("bf16", "f32")]:
+    plan = [(n, f) for n in lengths for f in ("bf16", "f32")]
+    if DECODE_L in lengths:
+        plan += [(DECODE_L, f) for f in ("q8", "q8r", "q4r")]
+    for length, fmt in plan:
         out = res.setdefault(length, {})
         p = length - DECODE_ROWS
         n_caches = max(2, -(-4 * l2 // (p * RECORD_BYTES[fmt])))
@@ -634,7 +643,7 @@ def time_decode(run, args, lengths=(DECODE_L,)):
             end.record()
         run.barrier()
         us = run.max_over_ranks(start.elapsed_time(end)) * 1e3 / steps
-        bytes_step = p * RECORD_BYTES[fmt] + DECODE_ROWS * KV_HEADS * 128 * (2 if fmt == "bf16" else 4)
+        bytes_step = p * RECORD_BYTES[fmt] + DECODE_ROWS * KV_HEADS * TAIL_BYTES[fmt]
         gbs = bytes_step / (us * 1e-6) / 1e9
         out[fmt] = {"us_per_step": round(us, 2), "rows": DECODE_ROWS, "kv_len": length,
                     "bytes_per_step": int(bytes_step),
@@ -643,7 +652,7 @@ def time_decode(run, args, lengths=(DECODE_L,)):
                                  "traffic": run.traffic.get(f"decode_{fmt}") if length == DECODE_L else None},
                     "caches_rotated": n_caches,
                     # the decode kernel (tensor-core for BF16 records, CUDA-core
-                    # for F32) and its split-merge kernel
+                    # for the others) and its split-merge kernel
                     "gpu_launches_per_step": 2, "timing": "CUDA graph of the steps"}
         del graph
         for c in caches:

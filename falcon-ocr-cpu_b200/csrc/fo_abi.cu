@@ -129,6 +129,7 @@ struct DeviceGuard {
 };
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool aligned4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
 
 }  // namespace
 
@@ -178,6 +179,18 @@ struct fo_kv_cache {
     // BF16 records: the tensor-core decode's maps (decode_tc.cu), built at seal.
     alignas(64) CUtensorMap tc_map, tail_map, s1_map;
     int has_tc = 0, has_tail_map = 0;
+};
+
+// The draft head's int8 key/value cache (DraftState's Kv::Q8,
+// src/draft_head.rs:177-220): codes [8][capacity][64], one scale per row.
+struct fo_draft_kv {
+    fo_ctx *ctx = nullptr;
+    int64_t capacity = 0, len = 0;
+    int8_t *key_codes = nullptr, *value_codes = nullptr;
+    float *key_scales = nullptr, *value_scales = nullptr;
+    float *scores = nullptr;  // [8][2][capacity + FO_DRAFT_MAX_CHAIN] attention scratch
+    float *stage = nullptr;   // host-mode staging: q, out [16][64], chain keys and values
+    size_t bytes = 0;
 };
 
 struct fo_i8_cache {
@@ -1378,6 +1391,139 @@ int fo_i8_decode_batch(fo_i8_cache *const *caches, int64_t n, const float *const
         cudaError_t e = fo_launch_decode_i8((const fo_i8_page *)ctx->i8_pages.ptr, m, heads, max_splits, fast_exp,
                                             ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "i8 decode launch");
+    }
+    return FO_OK;
+}
+
+// ------------------------------------------------------------ draft head KV
+int fo_draft_kv_destroy(fo_draft_kv *kv) {
+    if (!kv) return FO_OK;
+    DeviceGuard guard(kv->ctx->device);
+    cudaStreamSynchronize(kv->ctx->stream);
+    void *ptrs[] = {kv->key_codes, kv->value_codes, kv->key_scales, kv->value_scales, kv->scores, kv->stage};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    delete kv;
+    return FO_OK;
+}
+
+// Host staging: q and out (16 x 64 each), chain keys and values (up to
+// FO_DRAFT_MAX_CHAIN rows of 512 each); pushes from the host go through the
+// chain part FO_DRAFT_MAX_CHAIN rows at a time.
+static constexpr size_t DRAFT_STAGE_FLOATS = 2 * 1024 + 2 * (size_t)FO_DRAFT_MAX_CHAIN * FO_DRAFT_KV_WIDTH;
+
+int fo_draft_kv_create(fo_ctx *ctx, int64_t capacity, fo_draft_kv **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_draft_kv_create: null output pointer");
+    *out = nullptr;
+    if (!ctx) return fail(FO_ERR_INVALID, "null context");
+    if (capacity < 1 || capacity > (int64_t)1 << 24)
+        return fail(FO_ERR_CAPACITY, "draft KV capacity must be 1..16,777,216 positions");
+    DeviceGuard guard(ctx->device);
+    fo_draft_kv *kv = new fo_draft_kv();
+    kv->ctx = ctx;
+    kv->capacity = capacity;
+    const size_t rows = (size_t)8 * capacity;
+    cudaError_t e = cudaSuccess;
+    auto alloc = [&](void **p, size_t bytes) {
+        if (e == cudaSuccess) e = cudaMalloc(p, bytes);
+    };
+    alloc((void **)&kv->key_codes, rows * 64);
+    alloc((void **)&kv->value_codes, rows * 64);
+    alloc((void **)&kv->key_scales, rows * 4);
+    alloc((void **)&kv->value_scales, rows * 4);
+    alloc((void **)&kv->scores, (size_t)8 * 2 * (capacity + FO_DRAFT_MAX_CHAIN) * 4);
+    alloc((void **)&kv->stage, DRAFT_STAGE_FLOATS * 4);
+    if (e != cudaSuccess) {
+        fo_draft_kv_destroy(kv);
+        return cuda_fail(e, "fo_draft_kv_create: cudaMalloc");
+    }
+    kv->bytes = 2 * rows * 64 + 2 * rows * 4;
+    *out = kv;
+    return FO_OK;
+}
+
+int64_t fo_draft_kv_len(const fo_draft_kv *kv) { return kv ? kv->len : -1; }
+int64_t fo_draft_kv_bytes(const fo_draft_kv *kv) { return kv ? (int64_t)kv->bytes : -1; }
+
+int fo_draft_kv_records(const fo_draft_kv *kv, const int8_t **key_codes, const float **key_scales,
+                        const int8_t **value_codes, const float **value_scales) {
+    if (!kv) return fail(FO_ERR_INVALID, "null draft KV");
+    if (key_codes) *key_codes = kv->key_codes;
+    if (key_scales) *key_scales = kv->key_scales;
+    if (value_codes) *value_codes = kv->value_codes;
+    if (value_scales) *value_scales = kv->value_scales;
+    return FO_OK;
+}
+
+int fo_draft_kv_push(fo_draft_kv *kv, const float *keys, const float *values, int64_t rows, int mem) {
+    if (!kv || rows < 0 || (rows > 0 && (!keys || !values))) return fail(FO_ERR_INVALID, "fo_draft_kv_push: bad argument");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    if (kv->len + rows > kv->capacity) return fail(FO_ERR_CAPACITY, "draft KV capacity");
+    if (mem == FO_MEM_DEVICE && !(aligned8(keys) && aligned8(values)))
+        return fail(FO_ERR_INVALID, "fo_draft_kv_push: keys and values must be 8-byte aligned");
+    DeviceGuard guard(kv->ctx->device);
+    cudaStream_t st = kv->ctx->stream;
+    for (int64_t done = 0; done < rows;) {
+        const int64_t n = mem == FO_MEM_HOST ? std::min<int64_t>(FO_DRAFT_MAX_CHAIN, rows - done) : rows - done;
+        const float *dk = keys + done * FO_DRAFT_KV_WIDTH, *dv = values + done * FO_DRAFT_KV_WIDTH;
+        if (mem == FO_MEM_HOST) {
+            float *sk = kv->stage + 2048, *sv = sk + (size_t)FO_DRAFT_MAX_CHAIN * FO_DRAFT_KV_WIDTH;
+            const size_t bytes = (size_t)n * FO_DRAFT_KV_WIDTH * 4;
+            FO_CUDA(cudaMemcpyAsync(sk, dk, bytes, cudaMemcpyHostToDevice, st), "H2D(draft keys)");
+            FO_CUDA(cudaMemcpyAsync(sv, dv, bytes, cudaMemcpyHostToDevice, st), "H2D(draft values)");
+            dk = sk;
+            dv = sv;
+        }
+        cudaError_t e = fo_launch_draft_push(dk, dv, n, kv->capacity, kv->len, kv->key_codes, kv->key_scales,
+                                             kv->value_codes, kv->value_scales, st);
+        if (e != cudaSuccess) return cuda_fail(e, "draft push launch");
+        if (mem == FO_MEM_HOST) FO_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+        kv->len += n;
+        done += n;
+    }
+    return FO_OK;
+}
+
+int fo_draft_attend(fo_draft_kv *kv, const float *q, int64_t bases, int64_t window, const float *chain_keys,
+                    const float *chain_values, int64_t chain, float *output, int mem) {
+    if (!kv || !q || !output) return fail(FO_ERR_INVALID, "fo_draft_attend: null argument");
+    if (mem != FO_MEM_HOST && mem != FO_MEM_DEVICE) return fail(FO_ERR_INVALID, "bad mem mode");
+    if (bases < 0 || bases > kv->len) return fail(FO_ERR_INVALID, "fo_draft_attend: bases beyond the pushed rows");
+    if (window < 0) return fail(FO_ERR_INVALID, "fo_draft_attend: negative window");
+    if (chain < 0 || chain > FO_DRAFT_MAX_CHAIN)
+        return fail(FO_ERR_INVALID, "fo_draft_attend: chain rows must be 0..%d", FO_DRAFT_MAX_CHAIN);
+    if (chain > 0 && (!chain_keys || !chain_values)) return fail(FO_ERR_INVALID, "fo_draft_attend: null chain rows");
+    // draft_head.rs:549-553: only the newest `window` verified rows (0: all)
+    const int64_t start = window == 0 ? 0 : std::max<int64_t>(0, bases - window);
+    const int64_t n = bases - start;
+    if (n + chain == 0) return fail(FO_ERR_INVALID, "fo_draft_attend: nothing to attend to");
+    if (mem == FO_MEM_DEVICE &&
+        !(aligned16(q) && aligned4(output) && (chain == 0 || (aligned16(chain_keys) && aligned8(chain_values)))))
+        return fail(FO_ERR_INVALID, "fo_draft_attend: q and chain keys must be 16-byte aligned, chain values 8");
+    DeviceGuard guard(kv->ctx->device);
+    cudaStream_t st = kv->ctx->stream;
+    const float *dq = q, *dk = chain_keys, *dv = chain_values;
+    float *dout = output;
+    if (mem == FO_MEM_HOST) {
+        float *sq = kv->stage, *so = kv->stage + 1024, *sk = kv->stage + 2048;
+        float *sv = sk + (size_t)FO_DRAFT_MAX_CHAIN * FO_DRAFT_KV_WIDTH;
+        FO_CUDA(cudaMemcpyAsync(sq, q, 1024 * 4, cudaMemcpyHostToDevice, st), "H2D(draft q)");
+        if (chain > 0) {
+            const size_t bytes = (size_t)chain * FO_DRAFT_KV_WIDTH * 4;
+            FO_CUDA(cudaMemcpyAsync(sk, chain_keys, bytes, cudaMemcpyHostToDevice, st), "H2D(chain keys)");
+            FO_CUDA(cudaMemcpyAsync(sv, chain_values, bytes, cudaMemcpyHostToDevice, st), "H2D(chain values)");
+        }
+        dq = sq;
+        dk = sk;
+        dv = sv;
+        dout = so;
+    }
+    cudaError_t e = fo_launch_draft_attend(kv->key_codes, kv->key_scales, kv->value_codes, kv->value_scales,
+                                           kv->capacity, dq, start, n, dk, dv, chain, kv->scores, dout, st);
+    if (e != cudaSuccess) return cuda_fail(e, "draft attention launch");
+    if (mem == FO_MEM_HOST) {
+        FO_CUDA(cudaMemcpyAsync(output, dout, 1024 * 4, cudaMemcpyDeviceToHost, st), "D2H(draft out)");
+        FO_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     }
     return FO_OK;
 }

@@ -158,6 +158,18 @@ cudaError_t fo_launch_quantize_i8(const float *x, int64_t len, int64_t heads, in
 cudaError_t fo_launch_decode_i8(const fo_i8_page *dev_pages, int64_t n_pages, int64_t heads, int32_t max_splits,
                                 int fast_exp, cudaStream_t stream);
 
+// The draft head's int8 KV (draft.cu; src/draft_head.rs:177-220, 548-759):
+// codes [8][capacity][64] and one FP32 scale per row, for keys and values.
+#define FO_DRAFT_KV_WIDTH 512  // KV_HEADS * HEAD_DIM (draft_head.rs:41)
+#define FO_DRAFT_MAX_CHAIN 64  // FP32 chain rows one attention takes
+cudaError_t fo_launch_draft_push(const float *keys, const float *values, int64_t rows, int64_t capacity, int64_t len,
+                                 int8_t *key_codes, float *key_scales, int8_t *value_codes, float *value_scales,
+                                 cudaStream_t stream);
+cudaError_t fo_launch_draft_attend(const int8_t *key_codes, const float *key_scales, const int8_t *value_codes,
+                                   const float *value_scales, int64_t capacity, const float *q, int64_t start,
+                                   int64_t n, const float *chain_keys, const float *chain_values, int64_t chain,
+                                   float *scores, float *out, cudaStream_t stream);
+
 // The bounded-wait self-test kernel (selftest.cu).
 cudaError_t fo_launch_bounded_wait(unsigned *err, unsigned long long limit_ns, cudaStream_t stream);
 

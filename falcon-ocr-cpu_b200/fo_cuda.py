@@ -101,7 +101,8 @@ EXPORTS = [
     "fo_decode_rows_static_scratch", "fo_decode_static_scratch_status",
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
-    "fo_i8_decode_batch",
+    "fo_i8_decode_batch", "fo_draft_kv_create", "fo_draft_kv_destroy", "fo_draft_kv_push", "fo_draft_kv_len",
+    "fo_draft_kv_bytes", "fo_draft_kv_records", "fo_draft_attend",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -164,6 +165,13 @@ def lib() -> ctypes.CDLL:
         "fo_i8_bytes": (I64, [P]),
         "fo_i8_records": (I, [P, PP, PP, PP, PP]),
         "fo_i8_decode_batch": (I, [PP, I64, PP, PP, PP, I32]),
+        "fo_draft_kv_create": (I, [P, I64, ctypes.POINTER(P)]),
+        "fo_draft_kv_destroy": (I, [P]),
+        "fo_draft_kv_push": (I, [P, P, P, I64, I]),
+        "fo_draft_kv_len": (I64, [P]),
+        "fo_draft_kv_bytes": (I64, [P]),
+        "fo_draft_kv_records": (I, [P, PP, PP, PP, PP]),
+        "fo_draft_attend": (I, [P, P, I64, I64, P, P, I64, P, I]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -510,6 +518,58 @@ def sharded_prefill_bf16(comm: NcclComm, q, keys_bf16, values_bf16, geometry, si
                                         Geometry(*geometry), sinks.data_ptr(), options, n_bands, kv_splits,
                                         gathered.data_ptr()))
     return gathered
+
+
+class DraftKv:
+    """The draft head's int8 key/value cache on the device (fo_draft_kv_*:
+    DraftState's Kv::Q8 and attend, src/draft_head.rs:177-220, 548-759)."""
+
+    def __init__(self, capacity, ctx=None):
+        ctx = ctx or default_context()
+        h = ctypes.c_void_p()
+        check(lib().fo_draft_kv_create(ctx.handle, capacity, ctypes.byref(h)))
+        self.handle, self.capacity, self.ctx = h, capacity, ctx
+
+    @property
+    def len(self) -> int:
+        return lib().fo_draft_kv_len(self.handle)
+
+    def push(self, keys, values):
+        """Rows [rows][512] of keys and values (numpy: host; CUDA tensors: device)."""
+        keys, values = _f32(keys), _f32(values)
+        (pk, pv), mem = _ptr_mem([keys, values])
+        n = keys.numel() if _is_torch(keys) else keys.size
+        check(lib().fo_draft_kv_push(self.handle, pk, pv, n // 512, mem))
+
+    def attend(self, q, bases, output, window=0, chain_keys=None, chain_values=None):
+        """Attention of q [16][64] over the verified rows (the newest `window`
+        of the first `bases`; 0: all) and the chain rows [chain][512]."""
+        chain = 0
+        if chain_keys is not None:
+            chain = (chain_keys.numel() if _is_torch(chain_keys) else np.asarray(chain_keys).size) // 512
+        q = _f32(q)
+        ck = _f32(chain_keys) if chain else None
+        cv = _f32(chain_values) if chain else None
+        (pq, pk, pv, po), mem = _ptr_mem([q, ck, cv, output])
+        check(lib().fo_draft_attend(self.handle, pq, bases, window, pk, pv, chain, po, mem))
+        return output
+
+    def records(self):
+        """Device pointers (key_codes, key_scales, value_codes, value_scales)."""
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        check(lib().fo_draft_kv_records(self.handle, *[ctypes.byref(p) for p in ptrs]))
+        return tuple(p.value for p in ptrs)
+
+    def close(self):
+        if self.handle:
+            lib().fo_draft_kv_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Int8Cache:

@@ -28,6 +28,9 @@
  *                                  RoPE, compact append, BF16 copies) src/model/fused.rs:17-116
  *   fo_kv_append_qkv             rope::split_norm_rope then SplitPrefix::append for decode
  *                                  rows, src/model/rope.rs:15-85, src/quant/kv.rs:430-449
+ *   fo_draft_kv_create/destroy   DraftState::new with DraftKv::Q8   src/draft_head.rs:222-240
+ *   fo_draft_kv_push             Kv::push / quantize_row             src/draft_head.rs:194-220
+ *   fo_draft_attend              attend + group_q8                  src/draft_head.rs:548-759
  *
  * Entry points with no single reference counterpart (each says why below):
  *   fo_attention_prefill_bf16_rows[_split]  query-row bands of the BF16 prefill
@@ -387,6 +390,33 @@ int fo_i8_records(const fo_i8_cache *cache, const int8_t **k_codes, const float 
  * attends over all len positions of its page. */
 int fo_i8_decode_batch(fo_i8_cache *const *caches, int64_t n, const float *const *q, const float *const *sinks,
                        float *const *output, int32_t fast_exp);
+
+/* The draft head's int8 key/value cache (DraftState's Kv::Q8,
+ * src/draft_head.rs:177-220): each verified position's key and value,
+ * [512] FP32 = 8 groups x 64, stored as int8 codes group-major
+ * [8][capacity][64] with one FP32 scale per 64-value row, code =
+ * round(v * 127 / max |row|) (half away from zero, clamped to +-127, NaN 0),
+ * scale = max / 127. */
+typedef struct fo_draft_kv fo_draft_kv;
+int fo_draft_kv_create(fo_ctx *ctx, int64_t capacity, fo_draft_kv **out);
+int fo_draft_kv_destroy(fo_draft_kv *kv);
+/* Append `rows` positions: keys and values [rows][512] (host or device per
+ * `mem`; device pointers 8-byte aligned). */
+int fo_draft_kv_push(fo_draft_kv *kv, const float *keys, const float *values, int64_t rows, int mem);
+int64_t fo_draft_kv_len(const fo_draft_kv *kv);
+int64_t fo_draft_kv_bytes(const fo_draft_kv *kv);
+/* Device pointers to the codes and scales (for tests and tools). */
+int fo_draft_kv_records(const fo_draft_kv *kv, const int8_t **key_codes, const float **key_scales,
+                        const int8_t **value_codes, const float **value_scales);
+/* attend (src/draft_head.rs:548-627) with group_q8 (:706-759): the query
+ * q [16][64] of heads 2g, 2g+1 over KV group g's verified rows
+ * [max(0, bases - window), bases) (window 0: all of them) and then `chain`
+ * FP32 rows chain_keys / chain_values [chain][512] (0..64 rows); scores
+ * q.k / 8 (a row's dot times its key scale), softmax with the reference's
+ * exp_poly, output = sum p * v (value scale folded into p) times 1 / sum,
+ * [16][64].  bases <= fo_draft_kv_len; at least one row attended. */
+int fo_draft_attend(fo_draft_kv *kv, const float *q, int64_t bases, int64_t window, const float *chain_keys,
+                    const float *chain_values, int64_t chain, float *output, int mem);
 
 #ifdef __cplusplus
 }

@@ -1115,3 +1115,108 @@ void fo_or_qkv_rows(const float *qkv, const float *rope, int64_t rows, int64_t h
         memcpy(v + r * kdim, src + qdim + kdim, (size_t)kdim * sizeof(float));
     }
 }
+
+/* ------------------------------------------------------------------ */
+/* draft-head KV: src/draft_head.rs (DraftState's Kv::Q8 and attend)    */
+/* ------------------------------------------------------------------ */
+#define DRAFT_KV_WIDTH 512 /* draft_head.rs:41: KV_HEADS * HEAD_DIM */
+
+/* draft_head.rs:213-220: int8 codes with one absmax scale per 64 values,
+ * (v * (127 / max)).round() clamped to +-127 (NaN codes 0). */
+float fo_or_draft_quantize_row(const float *x, int8_t *codes) {
+    float max = absmax(x, 64);
+    const float inverse = max > 0.0f ? 127.0f / max : 0.0f;
+    for (int i = 0; i < 64; i++) {
+        float r = roundf(x[i] * inverse); /* Rust f32::round: half away from zero */
+        r = r < -127.0f ? -127.0f : (r > 127.0f ? 127.0f : r);
+        codes[i] = (int8_t)rust_as_int((double)r);
+    }
+    return max / 127.0f;
+}
+
+/* draft_head.rs:194-210 (Kv::Q8 push): rows [rows][512] keys and values into
+ * group-major codes [8][capacity][64] and scales [8][capacity], at `len`. */
+void fo_or_draft_push(const float *keys, const float *values, int64_t rows, int64_t capacity, int64_t len,
+                      int8_t *key_codes, float *key_scales, int8_t *value_codes, float *value_scales) {
+    for (int64_t r = 0; r < rows; r++)
+        for (int g = 0; g < 8; g++) {
+            const int64_t row = g * capacity + len + r;
+            key_scales[row] = fo_or_draft_quantize_row(keys + r * DRAFT_KV_WIDTH + g * 64, key_codes + row * 64);
+            value_scales[row] =
+                fo_or_draft_quantize_row(values + r * DRAFT_KV_WIDTH + g * 64, value_codes + row * 64);
+        }
+}
+
+/* attend (draft_head.rs:548-627) with group_q8 (:706-759) for the int8
+ * rows: per KV group, both heads' scores over verified rows
+ * [max(0, bases - window), bases) (window 0: all of them), each a dot times
+ * key_scale / 8, then the FP32 chain rows' dots / 8; max, exp (exp_poly,
+ * the vector kernels' exp), sum; out = (sum_t p_t * value_scale_t * v_t +
+ * sum_r p_r * chain_v_r) * (1 / sum). */
+void fo_or_draft_attend(const int8_t *key_codes, const float *key_scales, const int8_t *value_codes,
+                        const float *value_scales, int64_t capacity, const float *q, int64_t bases, int64_t window,
+                        const float *chain_keys, const float *chain_values, int64_t chain, float *out) {
+    const int64_t start = window == 0 ? 0 : (bases > window ? bases - window : 0);
+    const int64_t n = bases - start, total = n + chain;
+    float *s = (float *)malloc((size_t)(2 * total + 1) * sizeof(float));
+    for (int g = 0; g < 8; g++) {
+        const float *q0 = q + 2 * g * 64, *q1 = q0 + 64;
+        float *s0 = s, *s1 = s + total;
+        for (int64_t t = 0; t < n; t++) {
+            const int64_t row = g * capacity + start + t;
+            float d0 = 0.0f, d1 = 0.0f;
+            for (int d = 0; d < 64; d++) {
+                d0 = fmaf(q0[d], (float)key_codes[row * 64 + d], d0);
+                d1 = fmaf(q1[d], (float)key_codes[row * 64 + d], d1);
+            }
+            const float f = key_scales[row] * 0.125f;
+            s0[t] = d0 * f;
+            s1[t] = d1 * f;
+        }
+        for (int64_t r = 0; r < chain; r++) {
+            const float *k = chain_keys + r * DRAFT_KV_WIDTH + g * 64;
+            float d0 = 0.0f, d1 = 0.0f;
+            for (int d = 0; d < 64; d++) {
+                d0 = fmaf(q0[d], k[d], d0);
+                d1 = fmaf(q1[d], k[d], d1);
+            }
+            s0[n + r] = d0 * 0.125f;
+            s1[n + r] = d1 * 0.125f;
+        }
+        float m0 = NEG_INF, m1 = NEG_INF;
+        for (int64_t t = 0; t < total; t++) {
+            m0 = fmaxf(m0, s0[t]);
+            m1 = fmaxf(m1, s1[t]);
+        }
+        float sum0 = 0.0f, sum1 = 0.0f;
+        for (int64_t t = 0; t < total; t++) {
+            s0[t] = fo_or_exp_poly(s0[t] - m0);
+            s1[t] = fo_or_exp_poly(s1[t] - m1);
+            sum0 += s0[t];
+            sum1 += s1[t];
+        }
+        float o0[64] = {0}, o1[64] = {0};
+        for (int64_t t = 0; t < n; t++) {
+            const int64_t row = g * capacity + start + t;
+            const float f = value_scales[row], p0 = s0[t] * f, p1 = s1[t] * f;
+            for (int d = 0; d < 64; d++) {
+                const float v = (float)value_codes[row * 64 + d];
+                o0[d] = fmaf(p0, v, o0[d]);
+                o1[d] = fmaf(p1, v, o1[d]);
+            }
+        }
+        for (int64_t r = 0; r < chain; r++) {
+            const float *v = chain_values + r * DRAFT_KV_WIDTH + g * 64;
+            for (int d = 0; d < 64; d++) {
+                o0[d] = fmaf(s0[n + r], v[d], o0[d]);
+                o1[d] = fmaf(s1[n + r], v[d], o1[d]);
+            }
+        }
+        const float i0 = 1.0f / sum0, i1 = 1.0f / sum1;
+        for (int d = 0; d < 64; d++) {
+            out[2 * g * 64 + d] = o0[d] * i0;
+            out[(2 * g + 1) * 64 + d] = o1[d] * i1;
+        }
+    }
+    free(s);
+}

@@ -125,6 +125,17 @@ void fo_or_kv_decode_rows(const void *codes, const uint16_t *scales, const void 
 void fo_or_qkv_rows(const float *qkv, const float *rope, int64_t rows, int64_t heads, int64_t groups, float *q,
                     float *k, float *v);
 
+/* Draft-head KV (src/draft_head.rs:177-220, 548-759): int8 rows with one
+ * FP32 absmax scale per 64 values, group-major [8][capacity][64]; attention
+ * of q [16][64] over the verified rows [max(0, bases - window), bases)
+ * (window 0: all) and `chain` FP32 rows [chain][512]; out [16][64]. */
+float fo_or_draft_quantize_row(const float *x, int8_t *codes);
+void fo_or_draft_push(const float *keys, const float *values, int64_t rows, int64_t capacity, int64_t len,
+                      int8_t *key_codes, float *key_scales, int8_t *value_codes, float *value_scales);
+void fo_or_draft_attend(const int8_t *key_codes, const float *key_scales, const int8_t *value_codes,
+                        const float *value_scales, int64_t capacity, const float *q, int64_t bases, int64_t window,
+                        const float *chain_keys, const float *chain_values, int64_t chain, float *out);
+
 /* OpenMP threads used by the parallel oracle loops (0 = library default). */
 void fo_or_set_threads(int threads);
 int fo_or_max_threads(void);

@@ -89,6 +89,9 @@ def lib() -> ctypes.CDLL:
         "fo_or_unrotate": (None, [P, I]),
         "fo_or_q4_block": (ctypes.c_uint16, [P, P]),
         "fo_or_nibble": (ctypes.c_int8, [ctypes.c_uint8, I]),
+        "fo_or_draft_quantize_row": (F, [P, P]),
+        "fo_or_draft_push": (None, [P, P, I64, I64, I64, P, P, P, P]),
+        "fo_or_draft_attend": (None, [P, P, P, P, I64, P, I64, I64, P, P, I64, P]),
         "fo_or_set_threads": (None, [I]),
         "fo_or_max_threads": (I, []),
     }
@@ -351,3 +354,35 @@ def decode_records(codes, scales, fmt):
     sc = (scales.astype(np.uint32) << 16).view(np.float32)
     per = np.repeat(sc, 32)[: codes.size]
     return (codes.astype(np.float32) * per).astype(np.float32)
+
+
+class DraftKv:
+    """The draft head's int8 key/value cache (src/draft_head.rs:177-220):
+    codes [8][capacity][64] with one FP32 scale per 64-value row."""
+
+    def __init__(self, capacity):
+        self.capacity, self.len = capacity, 0
+        self.key_codes = np.zeros(8 * capacity * 64, np.int8)
+        self.value_codes = np.zeros(8 * capacity * 64, np.int8)
+        self.key_scales = np.zeros(8 * capacity, np.float32)
+        self.value_scales = np.zeros(8 * capacity, np.float32)
+
+    def push(self, keys, values):
+        """Rows [rows][512] of keys and values (Kv::push, draft_head.rs:194-210)."""
+        keys, values = _f32(keys), _f32(values)
+        rows = keys.size // 512
+        assert self.len + rows <= self.capacity
+        lib().fo_or_draft_push(_p(keys), _p(values), rows, self.capacity, self.len, _p(self.key_codes),
+                               _p(self.key_scales), _p(self.value_codes), _p(self.value_scales))
+        self.len += rows
+
+    def attend(self, q, bases, window=0, chain_keys=None, chain_values=None):
+        """attend + group_q8 (draft_head.rs:548-759): out [16][64]."""
+        q = _f32(q)
+        chain = 0 if chain_keys is None else _f32(chain_keys).size // 512
+        ck = _f32(chain_keys) if chain else np.zeros(1, np.float32)
+        cv = _f32(chain_values) if chain else np.zeros(1, np.float32)
+        out = np.zeros(16 * 64, np.float32)
+        lib().fo_or_draft_attend(_p(self.key_codes), _p(self.key_scales), _p(self.value_codes), _p(self.value_scales),
+                                 self.capacity, _p(q), bases, window, _p(ck), _p(cv), chain, _p(out))
+        return out

@@ -127,6 +127,10 @@ def test_null_handles_are_rejected():
     assert L.fo_i8_seal(None, None, None, 1, 16, F.MEM_HOST, ctypes.byref(ctypes.c_void_p())) == F.ERR_INVALID
     assert L.fo_i8_decode_batch(None, 1, None, None, None, 0) == F.ERR_INVALID
     assert L.fo_i8_bytes(None) == -1 and L.fo_i8_destroy(None) == F.OK
+    assert L.fo_draft_kv_create(None, 8, ctypes.byref(ctypes.c_void_p())) == F.ERR_INVALID
+    assert L.fo_draft_kv_push(None, None, None, 1, F.MEM_HOST) == F.ERR_INVALID
+    assert L.fo_draft_attend(None, None, 1, 0, None, None, 0, None, F.MEM_HOST) == F.ERR_INVALID
+    assert L.fo_draft_kv_len(None) == -1 and L.fo_draft_kv_destroy(None) == F.OK
     h = ctypes.c_void_p()
     assert L.fo_ctx_create(-1, None, ctypes.byref(h)) != F.OK
 
@@ -147,6 +151,10 @@ def test_batched_and_fused_entries_reject_bad_arguments():
     seal = L.fo_kv_seal_layer
     assert seal(None, 0, 0, F.KV_BF16, 0, -1, None, None, 8, 8, 9, 16, 8, 0, None) == F.ERR_INVALID
     assert seal(None, 0, 0, 7, 0, -1, None, None, 8, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
+    # rotation only with F32, Q8 or Q4 records (Storage, kv.rs:128-152)
+    for mode in (F.KV_BF16 | F.KV_ROTATED, F.KV_Q16 | F.KV_ROTATED, 32):
+        assert seal(None, 0, 0, mode, 0, -1, None, None, 8, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
+        assert "unknown mode" in last_error()
     assert seal(None, 0, 0, F.KV_BF16, 0, -1, None, None, 7, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
     assert "complete prefix" in last_error()
     assert seal(None, -1, 0, F.KV_BF16, 0, -1, None, None, 8, 8, 9, 16, 8, 0, ctypes.byref(out)) == F.ERR_INVALID
