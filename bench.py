@@ -669,6 +669,82 @@ PAGES = 64  # BASELINE config 5(a): independent pages, sharded by page
 PAGE_STEPS = 2048  # single-row decode steps per page after its prefill
 
 
+DRAFT_ROWS, DRAFT_CHAIN = 1500, 4  # verified positions (draft_head.rs's profile size), chain rows
+
+
+def time_draft(run, args):
+    """The draft head's int8 KV attention (draft_head.rs:548-759)
+    over 1,500 verified positions and 4 FP32 chain rows, full and with the
+    reference profile's windows of 1,024 and 256 positions: CUDA-event time
+    of a graph of calls on the cache's stream, and the oracle restatement of
+    the same call on one host core beside it."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    torch, F = run.torch, run.F
+    rng = np.random.default_rng(6 + run.rank)
+    keys = rng.standard_normal(DRAFT_ROWS * 512).astype(np.float32)
+    values = rng.standard_normal(DRAFT_ROWS * 512).astype(np.float32)
+    q = rng.standard_normal(1024).astype(np.float32)
+    ck = rng.standard_normal(DRAFT_CHAIN * 512).astype(np.float32)
+    cv = rng.standard_normal(DRAFT_CHAIN * 512).astype(np.float32)
+    stream = torch.cuda.Stream(device=run.dev)
+    dctx = F.Context(run.local, stream=stream.cuda_stream)
+    kv = F.DraftKv(DRAFT_ROWS, ctx=dctx)
+    kd, vd = torch.from_numpy(keys).to(run.dev), torch.from_numpy(values).to(run.dev)
+    qd, ckd, cvd = (torch.from_numpy(x).to(run.dev) for x in (q, ck, cv))
+    od = torch.empty(1024, device=run.dev)
+    torch.cuda.synchronize()
+    kv.push(kd, vd)
+    ref = None
+    if run.rank == 0:
+        ref = O.DraftKv(DRAFT_ROWS)
+        ref.push(keys, values)
+    res = {"workload": f"draft-head int8 KV attention, {DRAFT_ROWS} verified positions + {DRAFT_CHAIN} chain rows, "
+                       "16 heads x 64, 8 KV groups"}
+    for window in (0, 1024, 256):
+        n = DRAFT_ROWS if window == 0 else min(window, DRAFT_ROWS)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                kv.attend(qd, DRAFT_ROWS, od, window, ckd, cvd)
+        stream.synchronize()
+        steps = 200
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(steps):
+                kv.attend(qd, DRAFT_ROWS, od, window, ckd, cvd)
+        graph.replay()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record()
+            graph.replay()
+            end.record()
+        stream.synchronize()
+        us = start.elapsed_time(end) * 1e3 / steps
+        # codes and scales of n rows for keys and values, plus the chain rows
+        nbytes = 8 * n * 2 * (64 + 4) + 2 * DRAFT_CHAIN * 512 * 4
+        gbs = nbytes / (us * 1e-6) / 1e9
+        line = {"us_per_call": round(us, 2), "positions": n, "bytes_per_call": nbytes,
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": round(gbs / run.peaks["hbm_gbs"], 4),
+                             "note": "8 CTAs (one per KV group) on a cache this small: launch- and latency-bound"},
+                "gpu_launches_per_call": 1}
+        if ref is not None:
+            O.set_threads(1)
+            t0, k = time.perf_counter(), 0
+            while k < 20 or time.perf_counter() - t0 < 0.5:
+                ref.attend(q, DRAFT_ROWS, window, ck, cv)
+                k += 1
+            line["cpu_baseline"] = {"value": round((time.perf_counter() - t0) / k * 1e6, 1), "unit": "us/call",
+                                    "cores": 1, "kind": "port",
+                                    "sample": f"{k} calls of the same attention (oracle restatement)"}
+            O.set_threads(0)
+        res[f"window_{window}" if window else "full"] = line
+        del graph
+    kv.close()
+    dctx.close()
+    return res
+
+
 def time_pages(run, args):
     """BASELINE config 5(a): 64 independent pages, each a 6,544-token
     prefix-LM prefill (C2, BF16 static shift) and then 2,048 single-row
@@ -857,6 +933,8 @@ def run_ours(args, world, rank, local):
         extra["sharded_prefill"] = time_sharded(run, args)
     if args.mode in ("full", "pages"):
         extra["pages"] = time_pages(run, args)
+    if args.mode in ("full", "draft"):
+        extra["draft"] = time_draft(run, args)
     if args.mode == "full":
         extra["prefill_rows"] = time_prefill_rows(run, args, inputs)
     cpu_decode_us = None
@@ -888,7 +966,7 @@ def main():
                     help="key ranges per query pair in the sharded prefill (0: chosen from the CTA count)")
     ap.add_argument("--bands", type=int, default=1,
                     help="query-row bands of the sharded prefill (C5b); one band measured fastest at 2 ranks")
-    ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded", "pages"], default="full",
+    ap.add_argument("--mode", choices=["full", "prefill", "decode", "c4", "sharded", "pages", "draft"], default="full",
                     help="full: the contract line; prefill/decode: only that part (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup()

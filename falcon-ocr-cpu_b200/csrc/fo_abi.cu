@@ -188,7 +188,8 @@ struct fo_draft_kv {
     int64_t capacity = 0, len = 0;
     int8_t *key_codes = nullptr, *value_codes = nullptr;
     float *key_scales = nullptr, *value_scales = nullptr;
-    float *scores = nullptr;  // [8][2][capacity + FO_DRAFT_MAX_CHAIN] attention scratch
+    float *part = nullptr;        // [8][FO_DRAFT_MAX_SPLITS][2][66] attention partials
+    unsigned *counters = nullptr;  // [8] CTAs done per group (zero between calls)
     float *stage = nullptr;   // host-mode staging: q, out [16][64], chain keys and values
     size_t bytes = 0;
 };
@@ -1400,7 +1401,8 @@ int fo_draft_kv_destroy(fo_draft_kv *kv) {
     if (!kv) return FO_OK;
     DeviceGuard guard(kv->ctx->device);
     cudaStreamSynchronize(kv->ctx->stream);
-    void *ptrs[] = {kv->key_codes, kv->value_codes, kv->key_scales, kv->value_scales, kv->scores, kv->stage};
+    void *ptrs[] = {kv->key_codes, kv->value_codes, kv->key_scales, kv->value_scales, kv->part, kv->counters,
+                    kv->stage};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete kv;
@@ -1431,8 +1433,11 @@ int fo_draft_kv_create(fo_ctx *ctx, int64_t capacity, fo_draft_kv **out) {
     alloc((void **)&kv->value_codes, rows * 64);
     alloc((void **)&kv->key_scales, rows * 4);
     alloc((void **)&kv->value_scales, rows * 4);
-    alloc((void **)&kv->scores, (size_t)8 * 2 * (capacity + FO_DRAFT_MAX_CHAIN) * 4);
+    alloc((void **)&kv->part, (size_t)8 * FO_DRAFT_MAX_SPLITS * 2 * (64 + 2) * 4);
+    alloc((void **)&kv->counters, 8 * sizeof(unsigned));
     alloc((void **)&kv->stage, DRAFT_STAGE_FLOATS * 4);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->counters, 0, 8 * sizeof(unsigned), ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) {
         fo_draft_kv_destroy(kv);
         return cuda_fail(e, "fo_draft_kv_create: cudaMalloc");
@@ -1519,7 +1524,8 @@ int fo_draft_attend(fo_draft_kv *kv, const float *q, int64_t bases, int64_t wind
         dout = so;
     }
     cudaError_t e = fo_launch_draft_attend(kv->key_codes, kv->key_scales, kv->value_codes, kv->value_scales,
-                                           kv->capacity, dq, start, n, dk, dv, chain, kv->scores, dout, st);
+                                           kv->capacity, dq, start, n, dk, dv, chain, kv->part, kv->counters, dout,
+                                           st);
     if (e != cudaSuccess) return cuda_fail(e, "draft attention launch");
     if (mem == FO_MEM_HOST) {
         FO_CUDA(cudaMemcpyAsync(output, dout, 1024 * 4, cudaMemcpyDeviceToHost, st), "D2H(draft out)");

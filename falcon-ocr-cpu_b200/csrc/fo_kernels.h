@@ -165,10 +165,12 @@ cudaError_t fo_launch_decode_i8(const fo_i8_page *dev_pages, int64_t n_pages, in
 cudaError_t fo_launch_draft_push(const float *keys, const float *values, int64_t rows, int64_t capacity, int64_t len,
                                  int8_t *key_codes, float *key_scales, int8_t *value_codes, float *value_scales,
                                  cudaStream_t stream);
+#define FO_DRAFT_MAX_SPLITS 64  // CTAs per KV group of one attention
+// part: [8][FO_DRAFT_MAX_SPLITS][2][64 + 2] partials; counters: [8], zeroed.
 cudaError_t fo_launch_draft_attend(const int8_t *key_codes, const float *key_scales, const int8_t *value_codes,
                                    const float *value_scales, int64_t capacity, const float *q, int64_t start,
                                    int64_t n, const float *chain_keys, const float *chain_values, int64_t chain,
-                                   float *scores, float *out, cudaStream_t stream);
+                                   float *part, unsigned *counters, float *out, cudaStream_t stream);
 
 // The bounded-wait self-test kernel (selftest.cu).
 cudaError_t fo_launch_bounded_wait(unsigned *err, unsigned long long limit_ns, cudaStream_t stream);
