@@ -726,7 +726,8 @@ def time_draft(run, args):
         line = {"us_per_call": round(us, 2), "positions": n, "bytes_per_call": nbytes,
                 "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": run.peaks["hbm_gbs"], "unit": "GB/s",
                              "frac": round(gbs / run.peaks["hbm_gbs"], 4),
-                             "note": "8 CTAs (one per KV group) on a cache this small: launch- and latency-bound"},
+                             "note": "a cache this small is launch- and latency-bound: CTAs split the positions "
+                                     "of each KV group, then the last one merges"},
                 "gpu_launches_per_call": 1}
         if ref is not None:
             O.set_threads(1)
