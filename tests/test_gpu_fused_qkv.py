@@ -65,7 +65,7 @@ def test_prefix_rows_are_the_oracle_bit_for_bit(ctx, rows):
     assert np.array_equal(vb.view(torch.int16).cpu().numpy().view(np.uint16), bf16_rne(v_ref))
 
 
-FORMATS = [F.KV_F32, F.KV_Q16, F.KV_Q8, F.KV_BF16]
+FORMATS = [F.KV_F32, F.KV_Q16, F.KV_Q8, F.KV_BF16, F.KV_Q4, F.KV_Q8_ROT, F.KV_Q4_ROT]
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
@@ -93,12 +93,14 @@ def test_decode_rows_append_what_the_oracle_pushes(ctx, fmt):
     for t in range(gen):
         ref.push(np.ascontiguousarray(kr[t]).reshape(-1), np.ascontiguousarray(vr[t]).reshape(-1))
     (codes, scales, tcodes, tscales), ps, ts = gpu.records()
-    dt = {F.KV_F32: np.float32, F.KV_Q16: np.int16, F.KV_Q8: np.int8, F.KV_BF16: np.uint16}[fmt]
-    tail = F.device_to_host(tcodes, GROUPS * ts * 128, dt).reshape(GROUPS, ts, 128)[:, :gen]
-    want = ref.tail_codes.reshape(GROUPS, -1, 128)[:, :gen]
+    element = fmt & ~F.KV_ROTATED
+    dt = {F.KV_F32: np.float32, F.KV_Q16: np.int16, F.KV_Q8: np.int8, F.KV_BF16: np.uint16, F.KV_Q4: np.uint8}[element]
+    width = 64 if element == F.KV_Q4 else 128  # stored elements per tail record
+    tail = F.device_to_host(tcodes, GROUPS * ts * width, dt).reshape(GROUPS, ts, width)[:, :gen]
+    want = ref.tail_codes.reshape(GROUPS, -1, width)[:, :gen]
     b = (lambda x: x.view(np.uint32)) if dt == np.float32 else (lambda x: x)
     assert np.array_equal(b(np.ascontiguousarray(tail)), b(np.ascontiguousarray(want)))
-    if fmt in (F.KV_Q16, F.KV_Q8):
+    if element in (F.KV_Q16, F.KV_Q8, F.KV_Q4):
         got = F.device_to_host(tscales, GROUPS * ts * 4, np.uint16).reshape(GROUPS, ts, 4)[:, :gen]
         assert np.array_equal(got, ref.tail_scales.reshape(GROUPS, -1, 4)[:, :gen])
     with pytest.raises(F.CapacityError):
@@ -133,7 +135,7 @@ def test_fused_prefill_operands_give_the_same_attention(ctx):
     assert torch.equal(out_a.view(torch.int32), out_b.view(torch.int32))
 
 
-@pytest.mark.parametrize("mode,fast", [("bf16", False), ("q8", True)])
+@pytest.mark.parametrize("mode,fast", [("bf16", False), ("q8", True), ("q4r", True)])
 def test_layer_flow_stays_on_the_device(ctx, mode, fast):
     """Three layers of one page with no host round trip (seal_layer,
     src/model/cache.rs:218-276): fused QKV rows -> prefill attention ->
@@ -172,7 +174,7 @@ def test_layer_flow_stays_on_the_device(ctx, mode, fast):
         assert (np.abs(got - want) <= 1e-5 * (1 + np.abs(want))).all()
         fmt = "q8" if (mask >> layer) & 1 else mode
         ref = O.SplitCache(k_ref, v_ref, T, T + gen, fmt=fmt)
-        ref.fast_exp = fast and mode == "q8"
+        ref.fast_exp = fast and mode in ("q8", "q8r", "q4r")  # default_fast_exp (kv.rs:182-184)
         qd_ref, kd_ref, vd_ref = O.qkv_rows(dec, rd, gen)
         kr = kd_ref.reshape(gen, HEADS, 64)[:, 0::2]
         for t in range(gen):
