@@ -836,9 +836,10 @@ def time_pages(run, args):
                                "frac": round(gbs / run.peaks["hbm_gbs"], 4),
                                "note": "record bytes of every page per step (prefix records 2,560 B per position; "
                                        "tail records counted at the same size)"},
-           "gpu_launches": n + 4 * PAGE_STEPS, "scaling": "weak per page, strong per job",
-           "note": "caches sealed before the timed region; per step one append, one decode, one merge and one "
-                   "descriptor-advance launch, replayed from a CUDA graph of 64 steps"}
+           "gpu_launches": n + 3 * PAGE_STEPS, "scaling": "weak per page, strong per job",
+           "note": "caches sealed before the timed region; per step one append (which also sets every page's "
+                   "decode length), one decode and one merge launch (which moves every page's append index on), "
+                   "replayed from a CUDA graph of 64 steps"}
     del graph
     for c in caches:
         c.close()

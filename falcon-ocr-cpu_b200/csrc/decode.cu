@@ -671,9 +671,16 @@ constexpr int MERGE_SLICES = 16;
 constexpr int MERGE_THREADS = (FO_HD / 4) * MERGE_SLICES;
 
 __global__ void __launch_bounds__(MERGE_THREADS) merge_kernel(const __grid_constant__ fo_decode_page page0,
-                                                              const fo_decode_page *pages, int64_t H) {
+                                                              const fo_decode_page *pages, int64_t H,
+                                                              fo_append_page *advance) {
     extern __shared__ __align__(16) float msm[];
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (advance && blockIdx.x == 0 && threadIdx.x == 0) {
+        // A batch plan's step: this page's append and decode are complete, so
+        // its next append index moves on (a full tail keeps its capacity).
+        fo_append_page &a = advance[blockIdx.y];
+        if (a.first < a.tail_stride) a.first += 1;
+    }
     const fo_decode_page *pp = pages ? pages + blockIdx.y : &page0;
     const int64_t row_head = blockIdx.x;
     const int64_t r = row_head / H, h = row_head % H;
@@ -829,7 +836,8 @@ bool fo_make_record_map(CUtensorMap *map, const void *codes, int format, int64_t
 // the slice sums) stays below 200 KB up to 25,000 splits (3.2M positions).
 constexpr int MERGE_DSMEM_MAX = 200 * 1024;
 static cudaError_t launch_merge(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
-                                int64_t groups, int max_splits, int rows, cudaStream_t stream) {
+                                int64_t groups, int max_splits, int rows, cudaStream_t stream,
+                                fo_append_page *advance = nullptr) {
     // The attribute belongs to each device's context: set once per device.
     static std::atomic<unsigned long long> configured{0};
     int dev = 0;
@@ -855,7 +863,7 @@ static cudaError_t launch_merge(const fo_decode_page &page0, const fo_decode_pag
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, fo::merge_kernel, page0, dev_pages, H);
+    return cudaLaunchKernelEx(&cfg, fo::merge_kernel, page0, dev_pages, H, advance);
 }
 
 // Launches one instantiation as persistent CTAs (as many as fit on the
@@ -863,7 +871,7 @@ static cudaError_t launch_merge(const fo_decode_page &page0, const fo_decode_pag
 // limit once.
 template <int F, bool FAST, int R>
 static cudaError_t launch_one(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
-                              int64_t groups, int max_splits, cudaStream_t stream) {
+                              int64_t groups, int max_splits, cudaStream_t stream, fo_append_page *advance) {
     constexpr int smem = fo::Smem<F, R>::BYTES;
     constexpr int threads = fo::Shape<F>::THREADS;
     // CTAs of this instantiation each device holds at once (the attribute and
@@ -888,35 +896,35 @@ static cudaError_t launch_one(const fo_decode_page &page0, const fo_decode_page 
     fo::decode_kernel<F, FAST, R><<<grid, threads, smem, stream>>>(page0, dev_pages, n_pages, groups, max_splits);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return launch_merge(page0, dev_pages, n_pages, groups, max_splits, R, stream);
+    return launch_merge(page0, dev_pages, n_pages, groups, max_splits, R, stream, advance);
 }
 
 template <int F, bool FAST>
 static cudaError_t launch_rows(int rows, const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
-                               int64_t groups, int max_splits, cudaStream_t stream) {
+                               int64_t groups, int max_splits, cudaStream_t stream, fo_append_page *advance) {
     switch (rows) {
-    case 1: return launch_one<F, FAST, 1>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 2: return launch_one<F, FAST, 2>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 3: return launch_one<F, FAST, 3>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 4: return launch_one<F, FAST, 4>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 5: return launch_one<F, FAST, 5>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 6: return launch_one<F, FAST, 6>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 7: return launch_one<F, FAST, 7>(page0, dev_pages, n_pages, groups, max_splits, stream);
-    case 8: return launch_one<F, FAST, 8>(page0, dev_pages, n_pages, groups, max_splits, stream);
+    case 1: return launch_one<F, FAST, 1>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 2: return launch_one<F, FAST, 2>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 3: return launch_one<F, FAST, 3>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 4: return launch_one<F, FAST, 4>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 5: return launch_one<F, FAST, 5>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 6: return launch_one<F, FAST, 6>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 7: return launch_one<F, FAST, 7>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
+    case 8: return launch_one<F, FAST, 8>(page0, dev_pages, n_pages, groups, max_splits, stream, advance);
     }
     return cudaErrorInvalidValue;
 }
 
 static cudaError_t launch_decode(const fo_decode_page &page0, const fo_decode_page *dev_pages, int64_t n_pages,
                                  int format, int64_t groups, int fast_exp, int64_t max_splits, int rows,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, fo_append_page *advance = nullptr) {
     if (n_pages <= 0 || max_splits <= 0) return cudaSuccess;
     const int ms = (int)max_splits;
     format &= ~FO_KV_ROTATED_BIT;  // rotation travels in the pages (fo_decode_page::rotated)
 #define FO_DEC_CASE(FMT)                                                                        \
     case FMT:                                                                                   \
-        return fast_exp ? launch_rows<FMT, true>(rows, page0, dev_pages, n_pages, groups, ms, stream) \
-                        : launch_rows<FMT, false>(rows, page0, dev_pages, n_pages, groups, ms, stream);
+        return fast_exp ? launch_rows<FMT, true>(rows, page0, dev_pages, n_pages, groups, ms, stream, advance) \
+                        : launch_rows<FMT, false>(rows, page0, dev_pages, n_pages, groups, ms, stream, advance);
     switch (format) {
         FO_DEC_CASE(fo::DF32)
         FO_DEC_CASE(fo::DQ16)
@@ -936,9 +944,9 @@ extern "C" cudaError_t fo_launch_decode_one(const fo_decode_page *page, int form
 
 extern "C" cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format,
                                               int64_t groups, int fast_exp, int64_t max_splits, int max_rows,
-                                              cudaStream_t stream) {
+                                              fo_append_page *advance, cudaStream_t stream) {
     fo_decode_page none{};
-    return launch_decode(none, dev_pages, n_pages, format, groups, fast_exp, max_splits, max_rows, stream);
+    return launch_decode(none, dev_pages, n_pages, format, groups, fast_exp, max_splits, max_rows, stream, advance);
 }
 
 extern "C" cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream) {

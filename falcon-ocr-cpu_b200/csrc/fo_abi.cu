@@ -952,7 +952,7 @@ int fo_kv_append_batch(fo_kv_cache *const *caches, int64_t n, const float *const
                 "H2D(append pages)");
         FO_CUDA(ctx->host_append_pages.uploaded(slot, ctx->stream), "cudaEventRecord");
         cudaError_t e = fo_launch_append_batch((const fo_append_page *)ctx->append_pages.ptr, m, rows, c0->heads,
-                                               c0->groups, c0->format, ctx->stream);
+                                               c0->groups, c0->format, nullptr, nullptr, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "append batch launch");
         for (int64_t i = 0; i < m; i++) caches[base + i]->tail_len += rows;
     }
@@ -1040,10 +1040,13 @@ int fo_kv_plan_step(fo_kv_plan *p) {
     if (!p) return fail(FO_ERR_INVALID, "fo_kv_plan_step: null plan");
     DeviceGuard guard(p->ctx->device);
     const int64_t n = (int64_t)p->caches.size();
-    cudaError_t e = fo_launch_append_batch(p->ap, n, 1, p->heads, p->groups, p->format, p->ctx->stream);
+    // The append also sets each page's decode length; the merge moves each
+    // page's append index on for the next step.
+    cudaError_t e = fo_launch_append_batch(p->ap, n, 1, p->heads, p->groups, p->format, p->dp, p->ctx->dev_err,
+                                           p->ctx->stream);
     if (e == cudaSuccess)
-        e = fo_launch_decode_batch(p->dp, n, p->format, p->groups, p->fast_exp, p->max_splits, 1, p->ctx->stream);
-    if (e == cudaSuccess) e = fo_launch_plan_advance(p->ap, p->dp, n, p->ctx->dev_err, p->ctx->stream);
+        e = fo_launch_decode_batch(p->dp, n, p->format, p->groups, p->fast_exp, p->max_splits, 1, p->ap,
+                                   p->ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "batch plan step launch");
     return FO_OK;
 }
@@ -1272,7 +1275,7 @@ int fo_kv_attention_decode_batch(fo_kv_cache *const *caches, int64_t n, const fl
                 "H2D(pages)");
         FO_CUDA(ctx->host_pages.uploaded(slot, ctx->stream), "cudaEventRecord");
         cudaError_t e = fo_launch_decode_batch((const fo_decode_page *)ctx->pages.ptr, m, c0->format, c0->groups,
-                                               c0->fast_exp, max_splits, 1, ctx->stream);
+                                               c0->fast_exp, max_splits, 1, nullptr, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "decode batch launch");
     }
     return FO_OK;

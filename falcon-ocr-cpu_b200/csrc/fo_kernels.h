@@ -48,6 +48,7 @@ int fo_nccl_comm_destroy_impl(void *comm, char *msg, size_t n);
 int fo_nccl_gather_bf16(void *comm, uint16_t *block, size_t count, int rank, cudaStream_t stream, char *msg,
                         size_t n);
 
+struct fo_decode_page;
 // One cache's share of a batched append: its expanded rows and tail.
 struct fo_append_page {
     const float *k, *v;  // [rows][H][64]
@@ -58,8 +59,11 @@ struct fo_append_page {
 // Device error bit: a batch plan step found a cache's tail full.
 #define FO_DEVERR_CAPACITY 2u
 // Append `rows` expanded rows to each of n pages in one launch.
+// plan_pages (a batch plan's decode descriptors, or null): the append's first
+// lane per page also sets that page's decode length (prefix + first + rows),
+// or raises FO_DEVERR_CAPACITY in *err when the tail has no room.
 cudaError_t fo_launch_append_batch(const fo_append_page *pages, int64_t n, int64_t rows, int64_t heads, int64_t groups,
-                                   int format, cudaStream_t stream);
+                                   int format, fo_decode_page *plan_pages, unsigned *err, cudaStream_t stream);
 // Append rows of expanded K, V [rows][H][64] as tail records at index first..
 cudaError_t fo_launch_append(const float *k, const float *v, int64_t rows, int64_t heads, int64_t groups, int format,
                              void *tail_codes, uint16_t *tail_scales, int64_t tail_stride, int64_t first,
@@ -128,14 +132,13 @@ cudaError_t fo_launch_decode_tc(const fo_decode_page *page, int64_t groups, int 
 // The split merge of one page (a programmatic dependent of the decode just
 // launched on `stream`).
 cudaError_t fo_launch_decode_merge(const fo_decode_page *page, int64_t groups, cudaStream_t stream);
-// After a batch plan step (append, decode, merge): every page moves on by one
-// position (its next append writes the following tail record, its next decode
-// sees one more position); a full tail stays and raises FO_DEVERR_CAPACITY.
-cudaError_t fo_launch_plan_advance(fo_append_page *ap, fo_decode_page *dp, int64_t n, unsigned *err,
-                                   cudaStream_t stream);
-// n_pages pages whose descriptors are a device array.
+// n_pages pages whose descriptors are a device array.  advance (a batch
+// plan's append descriptors, or null): the merge moves each page's next
+// append index on by one once its append and decode are complete (a full tail
+// keeps its capacity).
 cudaError_t fo_launch_decode_batch(const fo_decode_page *dev_pages, int64_t n_pages, int format, int64_t groups,
-                                   int fast_exp, int64_t max_splits, int max_rows, cudaStream_t stream);
+                                   int fast_exp, int64_t max_splits, int max_rows, fo_append_page *advance,
+                                   cudaStream_t stream);
 
 // One page of BASELINE's INT8 KV format (decode_i8.cu): codes
 // [heads][len][64], FP32 scales [heads][ceil(len / 64)], for keys and values.

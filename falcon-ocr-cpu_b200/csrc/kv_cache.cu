@@ -177,33 +177,26 @@ __global__ void append_kernel(const float *__restrict__ k, const float *__restri
 
 // The same over many caches at once: one warp per (page, row, group).
 __global__ void append_batch_kernel(const fo_append_page *__restrict__ pages, int64_t n, int64_t rows,
-                                    int64_t heads, int64_t groups, int format) {
+                                    int64_t heads, int64_t groups, int format, fo_decode_page *dp, unsigned *err) {
     const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t per_page = rows * groups;
     if (w >= n * per_page) return;
     const int64_t i = w / per_page, rg = w - i * per_page;
     const fo_append_page &pg = pages[i];
+    if (dp && rg == 0 && (threadIdx.x & 31) == 0) {
+        // A batch plan's step (one lane per page): the page's decode covers
+        // the rows appended now; a tail without room for them writes nothing,
+        // keeps its decode length and raises the capacity bit.
+        if (pg.first + rows > pg.tail_stride) {
+            if (err) atomicOr(err, FO_DEVERR_CAPACITY);
+        } else {
+            dp[i].last = dp[i].prefix_len + pg.first + rows;
+            dp[i].splits = (int32_t)((dp[i].last + FO_SPLIT - 1) / FO_SPLIT);
+        }
+    }
     if (pg.first + rg / groups >= pg.tail_stride) return;  // a full batch-plan tail
     append_record(pg.k, pg.v, rg / groups, rg % groups, heads, format, pg.tail_codes, pg.tail_scales,
                   pg.tail_stride, pg.first, threadIdx.x & 31);
-}
-
-// One thread per page of a batch plan: the page's next append index and its
-// decode length move on by one, unless the next index would leave the tail
-// (then the index becomes the capacity, so later appends write nothing, the
-// decode length stays, and the error bit is raised).
-__global__ void plan_advance_kernel(fo_append_page *ap, fo_decode_page *dp, int64_t n, unsigned *err) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    if (ap[i].first + 1 >= ap[i].tail_stride) {
-        // the tail is full: no further append writes, the decode stays
-        ap[i].first = ap[i].tail_stride;
-        if (err) atomicOr(err, FO_DEVERR_CAPACITY);
-        return;
-    }
-    ap[i].first += 1;
-    dp[i].last += 1;
-    dp[i].splits = (int32_t)((dp[i].last + FO_SPLIT - 1) / FO_SPLIT);
 }
 
 // ------------------------------------------------------- fused QKV rows
@@ -342,19 +335,14 @@ extern "C" cudaError_t fo_launch_append(const float *k, const float *v, int64_t 
 }
 
 extern "C" cudaError_t fo_launch_append_batch(const fo_append_page *pages, int64_t n, int64_t rows, int64_t heads,
-                                              int64_t groups, int format, cudaStream_t stream) {
+                                              int64_t groups, int format, fo_decode_page *plan_pages, unsigned *err,
+                                              cudaStream_t stream) {
     const int64_t warps = n * rows * groups;
     if (warps == 0) return cudaSuccess;
     const int threads = 256;
     const int64_t blocks = (warps * 32 + threads - 1) / threads;
-    fo::append_batch_kernel<<<(unsigned)blocks, threads, 0, stream>>>(pages, n, rows, heads, groups, format);
-    return cudaGetLastError();
-}
-
-extern "C" cudaError_t fo_launch_plan_advance(fo_append_page *ap, fo_decode_page *dp, int64_t n, unsigned *err,
-                                              cudaStream_t stream) {
-    if (n == 0) return cudaSuccess;
-    fo::plan_advance_kernel<<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(ap, dp, n, err);
+    fo::append_batch_kernel<<<(unsigned)blocks, threads, 0, stream>>>(pages, n, rows, heads, groups, format,
+                                                                      plan_pages, err);
     return cudaGetLastError();
 }
 

@@ -360,6 +360,37 @@ def test_batch_plan_stops_at_a_full_tail(ctx):
         c.close()
 
 
+def test_batch_plan_that_fills_its_tails_exactly_finishes_cleanly(ctx):
+    """As many steps as the caches have room for: every row is written,
+    finish reports no error, and the last step's output equals a decode of
+    the full caches."""
+    room = 3
+    caches = plan_caches(F.KV_Q8, ctx, room)
+    n = len(caches)
+    rng = np.random.default_rng(12)
+    kb = [torch.empty(1024, device="cuda") for _ in range(n)]
+    vb = [torch.empty(1024, device="cuda") for _ in range(n)]
+    qb = [torch.empty(1024, device="cuda") for _ in range(n)]
+    ob = [torch.empty(1024, device="cuda") for _ in range(n)]
+    sd = [dev(np.linspace(-1, 1, 16).astype(np.float32))] * n
+    plan = F.BatchPlan(caches, kb, vb, qb, sd, ob)
+    for _ in range(room):
+        kv, q = step_rows(rng, n)
+        for i in range(n):
+            kb[i].copy_(dev(kv[i, 0]))
+            vb[i].copy_(dev(kv[i, 1]))
+            qb[i].copy_(dev(q[i]))
+        plan.step()
+    plan.finish()
+    assert [c.tail_len for c in caches] == [room] * n
+    for i, c in enumerate(caches):
+        single = torch.empty(1024, device="cuda")
+        c.attention_decode(qb[i], c.prefix_len + room, sd[i], single)
+        torch.cuda.synchronize()
+        assert torch.equal(single.view(torch.int32), ob[i].view(torch.int32)), i
+        c.close()
+
+
 def test_seal_errors(ctx):
     """kv.rs:248-295 and src/quant/kv/tests.rs:355-367"""
     k = np.zeros(16 * 64, np.float32)
