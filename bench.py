@@ -511,11 +511,13 @@ def time_c4(run, args):
 
 def time_sharded(run, args):
     """C5b: one 16,384-token causal prefill (BF16 static shift, seed 4)
-    sharded by KV group over the ranks through the C ABI
-    (fo_sharded_prefill_bf16 on an NCCL communicator of the ranks): each band
-    of rows is stored as BF16 straight into this rank's slot of the gathered
-    page and all-gathered in place while the next band computes.  Every rank
-    builds the same page and keeps its own heads."""
+    sharded by KV group over the ranks through the C ABI.  With more than one
+    rank the headline path is fo_sharded_prefill_bf16_peers: the kernels store
+    every finished BF16 row into all ranks' registered blocks over NVLink
+    (plain peer stores, overlapped with the computation), between two one-word
+    NCCL barriers.  The NCCL all-gather path (fo_sharded_prefill_bf16: each
+    band stored into this rank's slot, then all-gathered in place) is timed
+    beside it.  Every rank builds the same page and keeps its own heads."""
     import generators as G
     import sharded as S
     torch, F = run.torch, run.F
@@ -539,19 +541,33 @@ def time_sharded(run, args):
     comm = F.NcclComm(run.world, run.rank, uid[0], ctx=run.ctx)
     gathered = torch.empty(run.world * T * h * 64, dtype=torch.bfloat16, device=run.dev)
     n_bands = args.bands
+    steps = max(3, min(args.steps, 20))
 
-    def step(_):
+    def nccl_step(_):
         F.sharded_prefill_bf16(comm, q_r, kb_r, vb_r, geo, s_r, gathered, h, g1 - g0, n_bands=n_bands,
                                kv_splits=args.kv_splits, ctx=run.ctx)
 
     for i in range(max(args.warmup, 3)):
-        step(i)
-    steps = max(3, min(args.steps, 20))
-    ms, _ = run.timed(step, steps)
-    ms /= steps
+        nccl_step(i)
+    ms_nccl, _ = run.timed(nccl_step, steps)
+    ms_nccl /= steps
+    ms, path, block, layout = ms_nccl, "nccl all-gather", None, S.bands(T, n_bands)
+    if run.world > 1:
+        block = F.PeerBlock(comm, gathered, ctx=run.ctx)
+
+        def peer_step(_):
+            F.sharded_prefill_bf16_peers(block, q_r, kb_r, vb_r, geo, s_r, h, g1 - g0, kv_splits=args.kv_splits,
+                                         ctx=run.ctx)
+
+        for i in range(max(args.warmup, 3)):
+            peer_step(i)
+        ms_peer, _ = run.timed(peer_step, steps)
+        ms_peer /= steps
+        ms, path, layout = ms_peer, "kernel peer stores (NVLink)", [(0, T)]
     flop = S.flops(T, HEADS, geo)
-    # Parity of the gathered page with the whole page on one GPU (bitwise
-    # when both use one key range: every head's arithmetic is the same).
+    # Parity of the gathered page (the headline path's) with the whole page
+    # on one GPU (bitwise when both use one key range: every head's
+    # arithmetic is the same).
     check = None
     if run.rank == 0:
         kb, vb = kd.to(torch.bfloat16), vd.to(torch.bfloat16)
@@ -559,23 +575,27 @@ def time_sharded(run, args):
         F.attention_prefill_bf16(qd, kd, vd, geo, sd, whole, HEADS, KV_HEADS, keys_bf16=kb, values_bf16=vb,
                                  ctx=run.ctx)
         parts, off = [], 0
-        for b, e in S.bands(T, n_bands):
+        for b, e in layout:
             n = run.world * (e - b) * h * 64
             parts.append(gathered[off:off + n].view(run.world, e - b, h, 64))
             off += n
         got = S.token_major(parts).float()
         check = float((got - whole.view(T, HEADS, 64).to(torch.bfloat16).float()).abs().max().item())
     run.barrier()
+    if block is not None:
+        block.close()
     comm.close()
     gathered_bytes = T * HEADS * 64 * 2
     achieved = flop / (ms / 1e3) / 1e12
-    out = {"workload": "C5b: 16,384-token causal prefill, heads sharded by KV group, BF16 output all-gathered "
-                       "(fo_sharded_prefill_bf16, NCCL)",
-           "tokens": T, "ranks": run.world, "bands": len(S.bands(T, n_bands)),
+    out = {"workload": "C5b: 16,384-token causal prefill, heads sharded by KV group, BF16 output gathered on every "
+                       "rank",
+           "tokens": T, "ranks": run.world, "gather": path, "bands": len(layout),
            "kv_splits": args.kv_splits or "auto", "ms_per_step": round(ms, 4),
            "tok_per_s": round(T / (ms / 1e3), 1), "gflop": round(flop / 1e9, 1), "tflops": round(achieved, 1),
            "frac_of_world_peak": round(achieved / (run.world * run.peaks["bf16_tflops"]), 4),
            "gather_bytes": gathered_bytes, "max_abs_diff_vs_one_gpu": check}
+    if run.world > 1:
+        out["nccl_gather_ms_per_step"] = round(ms_nccl, 4)
     del qd, kd, vd, gathered
     torch.cuda.empty_cache()
     return out

@@ -2,6 +2,7 @@
 // sealed caches, shape validation with the reference's rules, host/device
 // staging and kernel dispatch.  Host code only; kernels live in the other
 // .cu files of this directory.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -25,7 +26,7 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
                                               int64_t image_end,
                                               int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
                                               unsigned *err, int n_split, float *part_o, float *part_ml,
-                                              cudaStream_t stream);
+                                              const fo_peer_out *peers, cudaStream_t stream);
 
 #define FO_WAIT_LIMIT_MAX_NS 10000000000ull
 #define FO_BATCH_PAGES 1024  // pages per batched launch
@@ -179,6 +180,19 @@ struct fo_kv_cache {
     // BF16 records: the tensor-core decode's maps (decode_tc.cu), built at seal.
     alignas(64) CUtensorMap tc_map, tail_map, s1_map;
     int has_tc = 0, has_tail_map = 0;
+};
+
+// Every rank's gathered block of a head-sharded prefill, mapped into this
+// process (CUDA IPC over NVLink): the destinations of the peer-store gather.
+struct fo_peer_block {
+    fo_ctx *ctx = nullptr;
+    void *comm = nullptr;
+    int32_t rank = 0, world = 0;
+    uint16_t *local = nullptr;
+    int64_t bytes = 0;
+    uint16_t *block[FO_MAX_PEERS] = {};  // every rank's block (this rank's is `local`)
+    void *opened[FO_MAX_PEERS] = {};     // IPC mappings to close
+    int32_t *word = nullptr;             // the barriers' device word
 };
 
 // The draft head's int8 key/value cache (DraftState's Kv::Q8,
@@ -402,7 +416,7 @@ int prefill_bf16_host_pipelined(fo_ctx *ctx, const float *q, const fo_compact_kv
         if (e != cudaSuccess) return cuda_fail(e, "convert kernel launch");
         e = fo_launch_prefill_bf16(dq, kb, vb, ds, dout, 0, T, H, G, geometry.image_start, geometry.image_end, r0, r1,
                                    options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err, 1,
-                                   nullptr, nullptr, ctx->stream);
+                                   nullptr, nullptr, nullptr, ctx->stream);
         if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
         FO_CUDA(cudaEventRecord(done, ctx->stream), "cudaEventRecord");
     }
@@ -601,7 +615,7 @@ int fo_attention_prefill_bf16(fo_ctx *ctx, const float *q, const fo_compact_kv *
         return fail(FO_ERR_INVALID, "BF16 prefill buffers must be 16-byte aligned");
     e = fo_launch_prefill_bf16(s.q, kb, vb, s.sinks, s.out, 0, T, H, G, geometry.image_start, geometry.image_end, 0, T,
                                options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST, ctx->dev_err, 1,
-                               nullptr, nullptr, ctx->stream);
+                               nullptr, nullptr, nullptr, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
     if ((st = timed_end(ctx, options.profile)) != FO_OK) return st;
     return finish_host(ctx, output, s.out, query_len * H * 64, mem);
@@ -647,7 +661,7 @@ int fo_attention_prefill_bf16_rows_split(fo_ctx *ctx, const float *q, const uint
                                            n_kv_heads,
                                            geometry.image_start, geometry.image_end, query_begin, query_end,
                                            options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST,
-                                           ctx->dev_err, kv_splits, po, pml, ctx->stream);
+                                           ctx->dev_err, kv_splits, po, pml, nullptr, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
     return FO_OK;
 }
@@ -733,6 +747,152 @@ int fo_sharded_prefill_bf16(fo_ctx *ctx, void *comm, int32_t rank, int32_t world
     cudaEvent_t all = ctx->comm_ev[band.size() + 1];
     FO_CUDA(cudaEventRecord(all, ctx->comm), "cudaEventRecord");
     FO_CUDA(cudaStreamWaitEvent(ctx->stream, all, 0), "cudaStreamWaitEvent");
+    return FO_OK;
+}
+
+int fo_peer_block_destroy(fo_peer_block *pb) {
+    if (!pb) return FO_OK;
+    DeviceGuard guard(pb->ctx->device);
+    cudaStreamSynchronize(pb->ctx->stream);
+    for (int p = 0; p < FO_MAX_PEERS; p++)
+        if (pb->opened[p]) cudaIpcCloseMemHandle(pb->opened[p]);
+    if (pb->word) cudaFree(pb->word);
+    delete pb;
+    return FO_OK;
+}
+
+int fo_peer_block_register(fo_ctx *ctx, void *comm, int32_t rank, int32_t world, uint16_t *gathered, int64_t bytes,
+                           fo_peer_block **out) {
+    if (!out) return fail(FO_ERR_INVALID, "fo_peer_block_register: null output pointer");
+    *out = nullptr;
+    if (!ctx || !comm || !gathered) return fail(FO_ERR_INVALID, "fo_peer_block_register: null argument");
+    if (world < 1 || world > FO_MAX_PEERS || rank < 0 || rank >= world)
+        return fail(FO_ERR_INVALID, "fo_peer_block_register: rank %d of %d (at most %d ranks)", rank, world,
+                    FO_MAX_PEERS);
+    if (bytes <= 0 || !aligned16(gathered)) return fail(FO_ERR_INVALID, "fo_peer_block_register: bad buffer");
+    DeviceGuard guard(ctx->device);
+    // The allocation holding `gathered` (an IPC handle names a whole allocation).
+    typedef CUresult (*AddressRange)(CUdeviceptr *, size_t *, CUdeviceptr);
+    static AddressRange range = nullptr;
+    if (!range) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return fail(FO_ERR_CUDA, "fo_peer_block_register: cuMemGetAddressRange is unavailable");
+        range = reinterpret_cast<AddressRange>(fn);
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, (CUdeviceptr)gathered) != CUDA_SUCCESS ||
+        (uintptr_t)gathered + (size_t)bytes > (uintptr_t)base + size)
+        return fail(FO_ERR_INVALID, "fo_peer_block_register: the buffer is not one device allocation");
+    struct Entry {
+        cudaIpcMemHandle_t handle;
+        int64_t offset, bytes;
+    } mine{};
+    cudaError_t e = cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void *>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "fo_peer_block_register: cudaIpcGetMemHandle (an IPC-capable allocation is needed)");
+    mine.offset = (int64_t)((uintptr_t)gathered - (uintptr_t)base);
+    mine.bytes = bytes;
+    // Every rank's entry, exchanged over the communicator.
+    std::vector<Entry> all((size_t)world);
+    void *d = nullptr;
+    FO_CUDA(cudaMalloc(&d, sizeof(Entry) * (world + 1)), "cudaMalloc(handles)");
+    char msg[256];
+    e = cudaMemcpyAsync(d, &mine, sizeof mine, cudaMemcpyHostToDevice, ctx->stream);
+    int st = 0;
+    if (e == cudaSuccess)
+        st = fo_nccl_allgather_bytes(comm, d, static_cast<char *>(d) + sizeof(Entry), sizeof(Entry), ctx->stream, msg,
+                                     sizeof msg);
+    if (e == cudaSuccess && !st)
+        e = cudaMemcpyAsync(all.data(), static_cast<char *>(d) + sizeof(Entry), sizeof(Entry) * world,
+                            cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess && !st) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    if (st) return fail(FO_ERR_CUDA, "%s", msg);
+    if (e != cudaSuccess) return cuda_fail(e, "fo_peer_block_register: handle exchange");
+    fo_peer_block *pb = new fo_peer_block();
+    pb->ctx = ctx;
+    pb->comm = comm;
+    pb->rank = rank;
+    pb->world = world;
+    pb->local = gathered;
+    pb->bytes = bytes;
+    for (int p = 0; p < world; p++) {
+        if (p == rank) {
+            pb->block[p] = gathered;
+            continue;
+        }
+        if (all[p].bytes != bytes) {
+            fo_peer_block_destroy(pb);
+            return fail(FO_ERR_INVALID, "fo_peer_block_register: rank %d registered %lld bytes, this rank %lld", p,
+                        (long long)all[p].bytes, (long long)bytes);
+        }
+        void *ptr = nullptr;
+        e = cudaIpcOpenMemHandle(&ptr, all[p].handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            fo_peer_block_destroy(pb);
+            return cuda_fail(e, "fo_peer_block_register: cudaIpcOpenMemHandle");
+        }
+        pb->opened[p] = ptr;
+        pb->block[p] = reinterpret_cast<uint16_t *>(static_cast<char *>(ptr) + all[p].offset);
+    }
+    e = cudaMalloc(reinterpret_cast<void **>(&pb->word), sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemset(pb->word, 0, sizeof(int32_t));
+    if (e != cudaSuccess) {
+        fo_peer_block_destroy(pb);
+        return cuda_fail(e, "fo_peer_block_register: cudaMalloc");
+    }
+    *out = pb;
+    return FO_OK;
+}
+
+int fo_sharded_prefill_bf16_peers(fo_ctx *ctx, fo_peer_block *pb, const float *q, const uint16_t *keys_bf16,
+                                  const uint16_t *values_bf16, int64_t total_len, int64_t n_heads, int64_t n_kv_heads,
+                                  fo_geometry geometry, const float *sinks, fo_prefill_options options,
+                                  int32_t kv_splits) {
+    if (!ctx || !pb) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16_peers: null argument");
+    if (pb->ctx->device != ctx->device) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16_peers: another device");
+    if (kv_splits < 0 || kv_splits > 64) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16_peers: bad kv_splits");
+    if (total_len < 4 || n_heads < 1) return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16_peers: bad shape");
+    const int64_t row_elems = n_heads * 64;
+    if ((int64_t)pb->world * total_len * row_elems * 2 > pb->bytes)
+        return fail(FO_ERR_INVALID, "fo_sharded_prefill_bf16_peers: the registered block holds fewer than %d x %lld rows",
+                    pb->world, (long long)total_len);
+    DeviceGuard guard(ctx->device);
+    const int64_t pairs = (total_len + 255) / 256;
+    if (kv_splits == 0) {
+        // Enough key ranges that the launch has a CTA per SM (at most 8).
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+        kv_splits = 1;
+        while (kv_splits < 8 && pairs * n_heads * kv_splits < sms) kv_splits *= 2;
+    }
+    char msg[256];
+    // 1. Every rank is done with its blocks' previous contents (all work
+    //    queued before this call on each rank's stream has completed).
+    if (fo_nccl_barrier(pb->comm, pb->word, ctx->stream, msg, sizeof msg)) return fail(FO_ERR_CUDA, "%s", msg);
+    // 2. This rank's rows, stored into its own block and, over NVLink, into
+    //    every peer's at the same place [rank][rows][heads][64].
+    const int64_t at = (int64_t)pb->rank * total_len * row_elems;
+    fo_peer_out peers{};
+    for (int p = 0; p < pb->world; p++)
+        if (p != pb->rank) peers.dst[peers.n++] = pb->block[p] + at;
+    float *po = nullptr, *pml = nullptr;
+    if (kv_splits > 1) {
+        FO_CUDA(ctx->split_o.ensure((size_t)kv_splits * pairs * 256 * n_heads * 64 * 4), "cudaMalloc(split partials)");
+        FO_CUDA(ctx->split_ml.ensure((size_t)kv_splits * pairs * 256 * n_heads * 2 * 4), "cudaMalloc(split partials)");
+        po = (float *)ctx->split_o.ptr;
+        pml = (float *)ctx->split_ml.ptr;
+    }
+    cudaError_t e = fo_launch_prefill_bf16(q, keys_bf16, values_bf16, sinks, pb->local + at, 1, total_len, n_heads,
+                                           n_kv_heads, geometry.image_start, geometry.image_end, 0, total_len,
+                                           options.softmax == FO_SOFTMAX_STATIC, options.exp == FO_EXP_FAST,
+                                           ctx->dev_err, kv_splits, po, pml, &peers, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(e, "BF16 prefill kernel launch");
+    // 3. Every rank's stores have landed: the whole page is in every block.
+    if (fo_nccl_barrier(pb->comm, pb->word, ctx->stream, msg, sizeof msg)) return fail(FO_ERR_CUDA, "%s", msg);
     return FO_OK;
 }
 

@@ -47,8 +47,22 @@ int fo_nccl_comm_init_impl(int world, int rank, const uint8_t *id, void **comm, 
 int fo_nccl_comm_destroy_impl(void *comm, char *msg, size_t n);
 int fo_nccl_gather_bf16(void *comm, uint16_t *block, size_t count, int rank, cudaStream_t stream, char *msg,
                         size_t n);
+int fo_nccl_allgather_bytes(void *comm, const void *send, void *recv, size_t bytes, cudaStream_t stream, char *msg,
+                            size_t n);
+int fo_nccl_barrier(void *comm, int32_t *word, cudaStream_t stream, char *msg, size_t n);
 
 struct fo_decode_page;
+
+// Other ranks' destinations of a head-sharded prefill's BF16 rows: the same
+// offset in each peer's gathered block, mapped into this process over NVLink
+// (CUDA IPC).  The prefill kernels store every finished row there as well as
+// locally (plain peer stores), so the gather overlaps the computation.
+#define FO_MAX_PEERS 8
+struct fo_peer_out {
+    void *dst[FO_MAX_PEERS];
+    int32_t n;
+};
+
 // One cache's share of a batched append: its expanded rows and tail.
 struct fo_append_page {
     const float *k, *v;  // [rows][H][64]

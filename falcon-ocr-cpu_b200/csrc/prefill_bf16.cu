@@ -65,6 +65,7 @@ struct Bf16Args {
     // 256 x its pairs).
     int n_split;
     float *part_o, *part_ml;
+    fo_peer_out peers;  // other ranks' BF16 destinations (n = 0: none)
 };
 
 // Bounded wait that ignores the abort flag (for copies/MMAs that complete on
@@ -331,21 +332,59 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
             } else if (row < T) {
                 const float lse = STATIC ? logf(l) : m2 * 0.69314718055994530942f + logf(l);
                 const float ss = sink_scale(a.sinks[head], lse);
-                const int64_t at = (row * H + head) * FO_HD;
+                if (a.out_bf16) {
+                    // BF16 row to this tile's Q buffer (free once the tile's MMAs
+                    // are done): 128-byte rows, 16-byte chunks XOR-swizzled by row.
+                    uint8_t *stage = smem + OFF_Q + t * BT_TILE + r * 128;
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    float4 v;
-                    v.x = (__uint_as_float(o[4 * i]) / l) * ss;
-                    v.y = (__uint_as_float(o[4 * i + 1]) / l) * ss;
-                    v.z = (__uint_as_float(o[4 * i + 2]) / l) * ss;
-                    v.w = (__uint_as_float(o[4 * i + 3]) / l) * ss;
-                    if (a.out_bf16)
-                        reinterpret_cast<uint2 *>(static_cast<uint16_t *>(a.out) + at)[i] =
-                            make_uint2((uint32_t)bf16_rne(v.x) | ((uint32_t)bf16_rne(v.y) << 16),
-                                       (uint32_t)bf16_rne(v.z) | ((uint32_t)bf16_rne(v.w) << 16));
-                    else
+                    for (int c = 0; c < 8; c++) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            const float x0 = (__uint_as_float(o[8 * c + 2 * k]) / l) * ss;
+                            const float x1 = (__uint_as_float(o[8 * c + 2 * k + 1]) / l) * ss;
+                            w[k] = (uint32_t)bf16_rne(x0) | ((uint32_t)bf16_rne(x1) << 16);
+                        }
+                        *reinterpret_cast<uint4 *>(stage + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+                    const int64_t at = (row * H + head) * FO_HD;
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        float4 v;
+                        v.x = (__uint_as_float(o[4 * i]) / l) * ss;
+                        v.y = (__uint_as_float(o[4 * i + 1]) / l) * ss;
+                        v.z = (__uint_as_float(o[4 * i + 2]) / l) * ss;
+                        v.w = (__uint_as_float(o[4 * i + 3]) / l) * ss;
                         reinterpret_cast<float4 *>(static_cast<float *>(a.out) + at)[i] = v;
+                    }
                 }
+            }
+        }
+        if constexpr (!SPLIT) {
+            if (a.out_bf16) {
+                // The tile's four warps store whole 128-byte rows of one head,
+                // coalesced, into this rank's block and every peer's (the
+                // head-sharded prefill's gather as NVLink stores).  The barrier
+                // is reached once by all four warps; rows of a warp whose waits
+                // gave up are not stored.
+                __shared__ int ok_w[2][4];
+                if (lane == 0) ok_w[t][wq] = ok;
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");
+                const uint8_t *stage = smem + OFF_Q + t * BT_TILE;
+#pragma unroll 2
+                for (int it = 0; it < 8; it++) {
+                    const int rr = wq * 32 + it * 4 + (lane >> 3), c = lane & 7;
+                    const int64_t grow = q0 + 128 * t + rr;
+                    if (grow < T && ok_w[t][rr >> 5]) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+                        const int64_t at = (grow * H + head) * FO_HD + 8 * c;
+                        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.out) + at) = v;
+                        for (int p = 0; p < a.peers.n; p++)
+                            *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.peers.dst[p]) + at) = v;
+                    }
+                }
+                if (a.peers.n) __threadfence_system();
             }
         }
     } else if (warp == 8) {
@@ -498,7 +537,8 @@ template <bool STATIC>
 __global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *part_o, const float *part_ml,
                                                                   const float *sinks, void *out, int out_bf16,
                                                                   int64_t span, int64_t base, int64_t H, int64_t row0,
-                                                                  int64_t rows, int n_split) {
+                                                                  int64_t rows, int n_split,
+                                                                  const __grid_constant__ fo_peer_out peers) {
     const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (w >= rows * H) return;
     const int lane = threadIdx.x & 31;
@@ -526,11 +566,14 @@ __global__ void __launch_bounds__(256) prefill_split_merge_kernel(const float *p
     const float ss = sink_scale(sinks[head], lse);
     const float y0 = (o0 / l) * ss, y1 = (o1 / l) * ss;
     const int64_t at = (row * H + head) * FO_HD + 2 * lane;
-    if (out_bf16)
-        *reinterpret_cast<uint32_t *>(static_cast<uint16_t *>(out) + at) =
-            (uint32_t)bf16_rne(y0) | ((uint32_t)bf16_rne(y1) << 16);
-    else
+    if (out_bf16) {
+        const uint32_t w = (uint32_t)bf16_rne(y0) | ((uint32_t)bf16_rne(y1) << 16);
+        *reinterpret_cast<uint32_t *>(static_cast<uint16_t *>(out) + at) = w;
+        for (int p = 0; p < peers.n; p++) *reinterpret_cast<uint32_t *>(static_cast<uint16_t *>(peers.dst[p]) + at) = w;
+        if (peers.n) __threadfence_system();
+    } else {
         *reinterpret_cast<float2 *>(static_cast<float *>(out) + at) = make_float2(y0, y1);
+    }
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -566,8 +609,11 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
                                               int64_t n_kv_heads, int64_t image_start, int64_t image_end,
                                               int64_t query_begin, int64_t query_end, int softmax_static, int exp_fast,
                                               unsigned *err, int n_split, float *part_o, float *part_ml,
-                                              cudaStream_t stream) {
+                                              const fo_peer_out *peers, cudaStream_t stream) {
     (void)exp_fast;  // the tensor-core softmax always takes the hardware exp2
+    fo_peer_out none{};
+    const fo_peer_out po = peers ? *peers : none;
+    if (po.n < 0 || po.n > FO_MAX_PEERS || (po.n > 0 && !out_bf16)) return cudaErrorInvalidValue;
     if (total == 0 || query_end <= query_begin) return cudaSuccess;
     if (n_split < 1 || (n_split > 1 && (!part_o || !part_ml))) return cudaErrorInvalidValue;
     CUtensorMap mk, mv;
@@ -575,7 +621,7 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
         return cudaErrorInvalidValue;
     const int64_t pb = query_begin / 256, pe = (query_end + 255) / 256;
     fo::Bf16Args args{q, sinks, out, out_bf16 != 0, err, total, n_heads, n_kv_heads, image_start, image_end, pb, pe,
-                      n_split, part_o, part_ml};
+                      n_split, part_o, part_ml, po};
     if ((pe - pb) * n_split > 65535) return cudaErrorInvalidValue;  // grid y limit
     dim3 grid((unsigned)n_heads, (unsigned)((pe - pb) * n_split));
     auto launch = [&](auto kernel) -> cudaError_t {
@@ -596,10 +642,10 @@ extern "C" cudaError_t fo_launch_prefill_bf16(const float *q, const uint16_t *ke
     if (softmax_static)
         fo::prefill_split_merge_kernel<true><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, out_bf16,
                                                                          (pe - pb) * 256, pb * 256, n_heads,
-                                                                         query_begin, rows, n_split);
+                                                                         query_begin, rows, n_split, po);
     else
         fo::prefill_split_merge_kernel<false><<<blocks, 256, 0, stream>>>(part_o, part_ml, sinks, out, out_bf16,
                                                                           (pe - pb) * 256, pb * 256, n_heads,
-                                                                          query_begin, rows, n_split);
+                                                                          query_begin, rows, n_split, po);
     return cudaGetLastError();
 }

@@ -35,6 +35,8 @@ struct NcclApi {
     ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
     const char *(*error_string)(ncclResult_t) = nullptr;
     bool ok = false;
 };
@@ -59,8 +61,10 @@ static const NcclApi *nccl_api(char *msg, size_t n) {
     a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-    if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_gather || !a.error_string) {
+    if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_gather || !a.all_reduce ||
+        !a.error_string) {
         snprintf(msg, n, "libnccl.so.2 lacks an entry point the sharded prefill needs");
         return nullptr;
     }
@@ -123,6 +127,34 @@ int fo_nccl_gather_bf16(void *comm, uint16_t *block, size_t count, int rank, cud
                                          static_cast<ncclComm_t>(comm), stream);
     if (r != ncclSuccess) {
         snprintf(msg, n, "ncclAllGather: %s", a->error_string(r));
+        return -1;
+    }
+    return 0;
+}
+
+// Every rank's `bytes` bytes at send gathered into recv [world][bytes] (the
+// peer-block registration's handle exchange).
+int fo_nccl_allgather_bytes(void *comm, const void *send, void *recv, size_t bytes, cudaStream_t stream, char *msg,
+                            size_t n) {
+    const NcclApi *a = nccl_api(msg, n);
+    if (!a) return -1;
+    const ncclResult_t r = a->all_gather(send, recv, bytes, ncclUint8, static_cast<ncclComm_t>(comm), stream);
+    if (r != ncclSuccess) {
+        snprintf(msg, n, "ncclAllGather: %s", a->error_string(r));
+        return -1;
+    }
+    return 0;
+}
+
+// A barrier of the communicator's ranks on `stream`: an all-reduce of one
+// word.  Once it completes on a rank, every rank's work queued before it on
+// its own stream has completed (the peer-store gather's end).
+int fo_nccl_barrier(void *comm, int32_t *word, cudaStream_t stream, char *msg, size_t n) {
+    const NcclApi *a = nccl_api(msg, n);
+    if (!a) return -1;
+    const ncclResult_t r = a->all_reduce(word, word, 1, ncclInt32, ncclSum, static_cast<ncclComm_t>(comm), stream);
+    if (r != ncclSuccess) {
+        snprintf(msg, n, "ncclAllReduce: %s", a->error_string(r));
         return -1;
     }
     return 0;

@@ -102,7 +102,8 @@ EXPORTS = [
     "fo_selftest_bounded_wait",
     "fo_attention_prefill_bf16_rows", "fo_attention_prefill_bf16_rows_split", "fo_i8_seal", "fo_i8_destroy", "fo_i8_bytes", "fo_i8_records",
     "fo_i8_decode_batch", "fo_draft_kv_create", "fo_draft_kv_destroy", "fo_draft_kv_push", "fo_draft_kv_len",
-    "fo_draft_kv_bytes", "fo_draft_kv_records", "fo_draft_attend",
+    "fo_draft_kv_bytes", "fo_draft_kv_records", "fo_draft_attend", "fo_peer_block_register",
+    "fo_peer_block_destroy", "fo_sharded_prefill_bf16_peers",
 ]
 
 _lib: Optional[ctypes.CDLL] = None
@@ -172,6 +173,9 @@ def lib() -> ctypes.CDLL:
         "fo_draft_kv_bytes": (I64, [P]),
         "fo_draft_kv_records": (I, [P, PP, PP, PP, PP]),
         "fo_draft_attend": (I, [P, P, I64, I64, P, P, I64, P, I]),
+        "fo_peer_block_register": (I, [P, P, I32, I32, P, I64, ctypes.POINTER(P)]),
+        "fo_peer_block_destroy": (I, [P]),
+        "fo_sharded_prefill_bf16_peers": (I, [P, P, P, P, P, I64, I64, I64, Geometry, P, PrefillOptions, I32]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -570,6 +574,38 @@ class DraftKv:
             self.close()
         except Exception:
             pass
+
+
+class PeerBlock:
+    """fo_peer_block_register: every rank's gathered buffer mapped into this
+    process (collective over the communicator's ranks)."""
+
+    def __init__(self, comm: "NcclComm", gathered, ctx=None):
+        ctx = ctx or default_context()
+        h = ctypes.c_void_p()
+        nbytes = gathered.numel() * gathered.element_size()
+        check(lib().fo_peer_block_register(ctx.handle, comm.handle, comm.rank, comm.world, gathered.data_ptr(), nbytes,
+                                           ctypes.byref(h)))
+        self.handle, self.gathered = h, gathered
+
+    def close(self):
+        if self.handle:
+            lib().fo_peer_block_destroy(self.handle)
+            self.handle = None
+
+
+def sharded_prefill_bf16_peers(block: PeerBlock, q, keys_bf16, values_bf16, geometry, sinks, n_heads, n_kv_heads,
+                               kv_splits=0, options=None, ctx=None):
+    """fo_sharded_prefill_bf16_peers: this rank's heads, every finished row
+    stored by the kernels into all ranks' registered blocks."""
+    ctx = ctx or default_context()
+    total = q.numel() // (n_heads * 64)
+    if options is None:
+        options = PrefillOptions(EXP_FAST, 0, SOFTMAX_STATIC, SOFTMAX_ONLINE)
+    check(lib().fo_sharded_prefill_bf16_peers(ctx.handle, block.handle, q.data_ptr(), keys_bf16.data_ptr(),
+                                              values_bf16.data_ptr(), total, n_heads, n_kv_heads, Geometry(*geometry),
+                                              sinks.data_ptr(), options, kv_splits))
+    return block.gathered
 
 
 class Int8Cache:

@@ -39,6 +39,8 @@
  *                                  an NCCL communicator, output all-gathered (BASELINE
  *                                  config 5b; the reference prefills on one host)
  *   fo_nccl_unique_id, fo_nccl_comm_init, fo_nccl_comm_destroy  its communicator
+ *   fo_peer_block_register/destroy, fo_sharded_prefill_bf16_peers  the same prefill
+ *                                  with the gather as NVLink peer stores from the kernels
  *   fo_convert_bf16                the Bf16Kv::Convert rounding on its own
  *   fo_decode_rows_static_scratch  verify decode with no device allocation,
  *   fo_decode_static_scratch_status  and its device error report
@@ -240,6 +242,28 @@ int fo_sharded_prefill_bf16(fo_ctx *ctx, void *comm, int32_t rank, int32_t world
 int fo_nccl_unique_id(uint8_t *id);
 int fo_nccl_comm_init(fo_ctx *ctx, int32_t world, int32_t rank, const uint8_t *id, void **comm);
 int fo_nccl_comm_destroy(void *comm);
+
+/* The head-sharded prefill with the gather done by the kernels themselves:
+ * fo_peer_block_register (collective: every rank of `comm` calls it with its
+ * own device buffer of `bytes` bytes, an allocation that CUDA IPC can share,
+ * on one node, at most 8 ranks) maps every rank's buffer into this process
+ * over NVLink.  fo_sharded_prefill_bf16_peers then computes this rank's heads
+ * (one launch over all rows) and its kernels store every finished BF16 row
+ * into all ranks' buffers at [rank][total_len][n_heads][64] (plain peer
+ * stores, overlapped with the computation; no multicast, no peer loads).  The
+ * call starts with a barrier of the ranks (every rank's earlier work, such as
+ * reads of the previous page, has completed before anyone overwrites its
+ * buffer) and ends with one (every rank's stores have landed); both are
+ * one-word NCCL all-reduces on the context's stream.  Results are bit for bit
+ * those of fo_sharded_prefill_bf16 with one band and the same kv_splits. */
+typedef struct fo_peer_block fo_peer_block;
+int fo_peer_block_register(fo_ctx *ctx, void *comm, int32_t rank, int32_t world, uint16_t *gathered, int64_t bytes,
+                           fo_peer_block **out);
+int fo_peer_block_destroy(fo_peer_block *block);
+int fo_sharded_prefill_bf16_peers(fo_ctx *ctx, fo_peer_block *block, const float *q, const uint16_t *keys_bf16,
+                                  const uint16_t *values_bf16, int64_t total_len, int64_t n_heads, int64_t n_kv_heads,
+                                  fo_geometry geometry, const float *sinks, fo_prefill_options options,
+                                  int32_t kv_splits);
 
 /* FP32 -> BF16 (round to nearest even) of n device values, the conversion
  * fo_attention_prefill_bf16 applies to Bf16Kv::Convert inputs. */

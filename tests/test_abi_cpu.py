@@ -131,6 +131,11 @@ def test_null_handles_are_rejected():
     assert L.fo_draft_kv_push(None, None, None, 1, F.MEM_HOST) == F.ERR_INVALID
     assert L.fo_draft_attend(None, None, 1, 0, None, None, 0, None, F.MEM_HOST) == F.ERR_INVALID
     assert L.fo_draft_kv_len(None) == -1 and L.fo_draft_kv_destroy(None) == F.OK
+    assert L.fo_peer_block_register(None, None, 0, 2, None, 16, ctypes.byref(ctypes.c_void_p())) == F.ERR_INVALID
+    assert L.fo_peer_block_destroy(None) == F.OK
+    opts = F.PrefillOptions(F.EXP_FAST, 0, F.SOFTMAX_STATIC, F.SOFTMAX_ONLINE)
+    assert L.fo_sharded_prefill_bf16_peers(None, None, None, None, None, 4096, 2, 1, F.Geometry(0, 0, 0), None, opts,
+                                           0) == F.ERR_INVALID
     h = ctypes.c_void_p()
     assert L.fo_ctx_create(-1, None, ctypes.byref(h)) != F.OK
 
