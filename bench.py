@@ -552,8 +552,22 @@ def time_sharded(run, args):
     ms_nccl, _ = run.timed(nccl_step, steps)
     ms_nccl /= steps
     ms, path, block, layout = ms_nccl, "nccl all-gather", None, S.bands(T, n_bands)
+    peer_error = None
     if run.world > 1:
-        block = F.PeerBlock(comm, gathered, ctx=run.ctx)
+        # Registration exchanges handles collectively, then maps the peers'
+        # buffers locally; every rank must succeed before any uses the path
+        # (its barriers are collectives), else all keep the NCCL gather.
+        try:
+            block = F.PeerBlock(comm, gathered, ctx=run.ctx)
+        except F.FoError as e:
+            peer_error = str(e)
+        if run.max_over_ranks(0.0 if block is not None else 1.0) > 0.0:
+            if block is not None:
+                block.close()
+                block = None
+            peer_error = peer_error or "another rank could not map the peers' buffers"
+
+    if block is not None:
 
         def peer_step(_):
             F.sharded_prefill_bf16_peers(block, q_r, kb_r, vb_r, geo, s_r, h, g1 - g0, kv_splits=args.kv_splits,
@@ -596,6 +610,8 @@ def time_sharded(run, args):
            "gather_bytes": gathered_bytes, "max_abs_diff_vs_one_gpu": check}
     if run.world > 1:
         out["nccl_gather_ms_per_step"] = round(ms_nccl, 4)
+    if peer_error:
+        out["peer_gather_unavailable"] = peer_error
     del qd, kd, vd, gathered
     torch.cuda.empty_cache()
     return out
